@@ -1,0 +1,541 @@
+"""Benchmark of the B200 matmul engine (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit_block|square|skinny]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --impl reference ...   # the reference's CPU path (NumPy oracle port)
+
+Default workload (``dit_block``, benchmark config 4): the four linears of a
+DiT block (QKV 1920->5760, out 1920->1920 + bias + residual, FFN-up
+1920->7680 + bias + GELU-tanh, FFN-down 7680->1920 + bias + residual) on
+2 x 17776 = 35552 tokens, bf16 with fp32 accumulation, tokens (M) sharded
+over N GPUs with weights replicated and the block output all-gathered over
+NCCL (strong scaling: the total work is fixed).  A step is one block
+forward over the whole token batch.  ``value`` = algorithmic TFLOP/s of the
+whole job (3.1455 TFLOP per step / max-over-ranks step time).
+
+Timing: W warm-up steps, then exactly K steps, each bracketed by CUDA events
+on the launching stream; a 512 MiB buffer (> the 126 MB L2) is written
+between steps outside the events, so every step starts with a cold L2.
+Barrier + device synchronize on both sides of the timed loop; the per-rank
+sum of step times is reduced with MAX over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+if "OPENBLAS_NUM_THREADS" not in os.environ:
+    os.environ["OPENBLAS_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
+
+import numpy as np  # noqa: E402
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, TOKENS, BATCH = 1920, 17776, 2
+M_TOTAL = TOKENS * BATCH
+L2_FLUSH_BYTES = 512 << 20
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ───────────────────────────── distributed plumbing ─────────────────────────────
+
+class Dist:
+    """Rank bookkeeping; torch.distributed (gloo) only bootstraps NCCL and
+    reduces host-side timings."""
+
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", str(self.rank)))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as td
+            td.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+            self.td = td
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.td.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if not self.pg:
+            return b
+        obj = [b]
+        self.td.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.td.destroy_process_group()
+
+
+# ───────────────────────────── clocks ─────────────────────────────
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                if int(parts[0]) not in self.gpus:
+                    continue
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ───────────────────────────── CPU legs ─────────────────────────────
+
+def _dit_weights_np(seed=1):
+    rng = np.random.default_rng(seed)
+    C = HIDDEN
+
+    def w(n, k):
+        return rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+
+    return {"qkv_w": w(3 * C, C), "out_w": w(C, C), "out_b": np.zeros(C, np.float32),
+            "up_w": w(4 * C, C), "up_b": np.zeros(4 * C, np.float32),
+            "down_w": w(C, 4 * C), "down_b": np.zeros(C, np.float32)}
+
+
+def cpu_reference_sample(workload: str, budget_s: float = 10.0, rows: int = 1024):
+    """Time the reference's CPU arithmetic (NumPy oracle port) on a bounded
+    sample of the workload; returns (TFLOP/s, description)."""
+    from oracle import oracle as O
+    cores = len(os.sched_getaffinity(0))
+    if workload == "dit_block":
+        w = {k: O.round_bf16(v) for k, v in _dit_weights_np().items()}
+        x = O.round_bf16(np.random.default_rng(2).standard_normal((rows, HIDDEN), dtype=np.float32))
+        flops = 2.0 * rows * HIDDEN * 23040
+        fn = lambda: O.dit_block_linears(x, w, dtype="f32")  # noqa: E731
+        what = f"{rows} of {M_TOTAL} token rows of one DiT block (4 linears), fp32 NumPy on bf16-rounded operands"
+    elif workload == "square":
+        n = 2048
+        a, b = O.square_inputs(n, "bf16", seed=0)
+        flops = 2.0 * n ** 3
+        fn = lambda: O.matmul_nt(a, b)  # noqa: E731
+        what = f"{n}^3 NT GEMM, fp32 NumPy on bf16-rounded operands"
+    else:
+        x, W, b = O.skinny_inputs(8, 11008)
+        flops = 2.0 * 8 * 4096 * 11008
+        fn = lambda: O.linear_act(x, W, b, O.ACT_GELU_TANH)  # noqa: E731
+        what = "skinny M=8 K=4096 N=11008 linear + GELU, fp32 NumPy"
+    fn()
+    best, t_end, n = float("inf"), time.perf_counter() + budget_s, 0
+    while time.perf_counter() < t_end or n < 2:
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+        n += 1
+    return flops / best / 1e12, f"{what}; best of {n} runs; {cores} threads", cores
+
+
+def run_reference_arm(args, dist):
+    if dist.rank != 0:
+        return
+    from oracle import oracle as O  # noqa: F401  (the CPU port is the reference arm here)
+    cores = len(os.sched_getaffinity(0))
+    rows = 512
+    for _ in range(args.warmup):
+        cpu_reference_sample(args.workload, budget_s=0.0, rows=rows)
+    times = []
+    if args.workload == "dit_block":
+        from oracle import oracle as O2
+        w = {k: O2.round_bf16(v) for k, v in _dit_weights_np().items()}
+        x = O2.round_bf16(np.random.default_rng(2).standard_normal((rows, HIDDEN), dtype=np.float32))
+        flops = 2.0 * rows * HIDDEN * 23040
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            O2.dit_block_linears(x, w, dtype="f32")
+            times.append(time.perf_counter() - t0)
+        sample = f"{rows} of {M_TOTAL} token rows of one DiT block per step (4 linears), fp32 NumPy"
+    else:
+        v, sample, _ = cpu_reference_sample(args.workload, budget_s=1.0)
+        flops, times = v * 1e12, [1.0] * args.steps
+    t = sum(times) / len(times)
+    value = flops / t / 1e12
+    line = {"impl": "reference", "metric": _metric(args.workload), "value": value,
+            "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t * 1e3, "higher_is_better": True, "dtype": "f32",
+            "data": "synthetic", "config": _config(args, 1),
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _metric(workload):
+    return {"dit_block": "GEMM TFLOP/s (DiT-block linears, bf16, M-sharded)",
+            "square": "GEMM TFLOP/s (square NT GEMM, bf16)",
+            "skinny": "GEMM TFLOP/s (skinny-M linear, bf16)"}[workload]
+
+
+def _config(args, world):
+    if args.workload == "dit_block":
+        return {"workload": "dit_block_linears (config 4)", "tokens": M_TOTAL, "hidden": HIDDEN,
+                "global_batch": BATCH, "seq_len": TOKENS, "parallelism": f"m-shard{world}",
+                "l2": "flushed between steps (512 MiB write)"}
+    if args.workload == "square":
+        return {"workload": f"square NT GEMM {args.size}^3 (config 2)",
+                "parallelism": f"replicas{world}", "l2": "flushed between steps (512 MiB write)"}
+    return {"workload": f"skinny linear M={args.size} K=4096 N=11008 (config 3)",
+            "parallelism": f"replicas{world}", "l2": "flushed between steps (512 MiB write)"}
+
+
+# ───────────────────────────── GPU arm ─────────────────────────────
+
+class EventTimer:
+    """CUDA-event timing of named launches on one stream."""
+
+    def __init__(self, lib, stream):
+        self.lib, self.stream = lib, stream
+        self.pending = []
+        self.cur = {}
+
+    def _ev(self):
+        import ctypes as C
+        p = C.c_void_p()
+        self.lib.sf_event_create(1, C.byref(p))
+        return p.value
+
+    def start(self, name):
+        import ctypes as C
+        e = self._ev()
+        self.lib.sf_event_record(C.c_void_p(e), C.c_void_p(self.stream))
+        self.cur[name] = e
+
+    def stop(self, name):
+        import ctypes as C
+        e = self._ev()
+        self.lib.sf_event_record(C.c_void_p(e), C.c_void_p(self.stream))
+        self.pending.append((name, self.cur.pop(name), e))
+
+    def collect(self):
+        import ctypes as C
+        out = {}
+        for name, a, b in self.pending:
+            ms = C.c_float()
+            self.lib.sf_event_elapsed_ms(C.c_void_p(a), C.c_void_p(b), C.byref(ms))
+            out.setdefault(name, []).append(ms.value)
+            self.lib.sf_event_destroy(C.c_void_p(a))
+            self.lib.sf_event_destroy(C.c_void_p(b))
+        self.pending = []
+        return out
+
+
+def run_gpu_arm(args, dist):
+    import ctypes as C
+
+    from scaffolding_b200 import _cuda_ops as ops
+    from scaffolding_b200 import dit
+    from scaffolding_b200 import engine as E
+    from scaffolding_b200._lib import lib
+
+    dev = dist.local_rank
+    E.set_device(dev)
+    sp = C.c_void_p()
+    E.check(lib.sf_stream_create(dev, 1, C.byref(sp)), "sf_stream_create")
+    stream = sp.value
+    E.set_stream(dev, stream)
+    bf = E.bfloat16
+    world, rank = dist.world, dist.rank
+
+    comm = None
+    if world > 1:
+        uid = (C.c_uint8 * 128)()
+        if rank == 0:
+            E.check(lib.sf_comm_unique_id(uid), "sf_comm_unique_id")
+        raw = dist.bcast_bytes(bytes(uid) if rank == 0 else None)
+        uid = (C.c_uint8 * 128).from_buffer_copy(raw)
+        cp = C.c_void_p()
+        E.check(lib.sf_comm_init(C.byref(cp), world, rank, uid), "sf_comm_init")
+        comm = cp.value
+
+    flush = E.DeviceBuffer.alloc(L2_FLUSH_BYTES, dev)
+
+    def l2_flush():
+        E.check(lib.sf_memset(C.c_void_p(flush.ptr), 1, L2_FLUSH_BYTES, C.c_void_p(stream)),
+                "sf_memset")
+
+    # ── workload
+    if args.workload == "dit_block":
+        assert M_TOTAL % world == 0
+        m = M_TOTAL // world
+        w = {k: v for k, v in _dit_weights_np().items()}
+        block = dit.DitLinears(w, m, dev)
+        rng = np.random.default_rng(100 + rank)
+        x_host = rng.standard_normal((m, HIDDEN), dtype=np.float32).astype(bf)
+        x = ops.gputensor_from_numpy(x_host, dev)
+        y_full = ops._alloc((M_TOTAL, HIDDEN), bf, dev) if world > 1 else None
+        flops_rank = dit.block_flops(m)
+        flops_job = dit.block_flops(M_TOTAL)
+        out_bytes = m * HIDDEN * 2
+
+        def step(timer=None, x_ptr=None):
+            block.run(x.ptr if x_ptr is None else x_ptr, stream=stream, timer=timer)
+            if comm is not None:
+                E.check(lib.sf_comm_allgather(C.c_void_p(comm), C.c_void_p(block.y.ptr),
+                                              C.c_void_p(y_full.ptr), out_bytes,
+                                              C.c_void_p(stream)), "sf_comm_allgather")
+        launches_per_step = 4
+        h2d_bytes = m * HIDDEN * 2
+        d2h_bytes = out_bytes
+        in_ptr_host = None
+    elif args.workload == "square":
+        n = args.size
+        rng = np.random.default_rng(0)
+        s = np.float32(1.0 / math.sqrt(n))
+        a = ops.gputensor_from_numpy((rng.standard_normal((n, n), dtype=np.float32) * s).astype(bf), dev)
+        b = ops.gputensor_from_numpy((rng.standard_normal((n, n), dtype=np.float32) * s).astype(bf), dev)
+        c = ops._alloc((n, n), bf, dev)
+        flops_rank = 2.0 * n ** 3
+        flops_job = flops_rank * world
+
+        def step(timer=None, x_ptr=None):
+            if timer:
+                timer.start("gemm")
+            E.gemm(n, n, n, a.ptr if x_ptr is None else x_ptr, n, 0, b.ptr, n, 1, c.ptr, n, 2, 2,
+                   device=dev, stream=stream)
+            if timer:
+                timer.stop("gemm")
+        launches_per_step = 1
+        h2d_bytes = n * n * 2
+        d2h_bytes = n * n * 2
+    else:
+        Ms, N, K = args.size, 11008, 4096
+        rng = np.random.default_rng(0)
+        copies = 4  # rotate weight copies so each step streams W from HBM
+        Ws = [ops.gputensor_from_numpy((rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(bf), dev)
+              for _ in range(copies)]
+        xs = ops.gputensor_from_numpy(rng.standard_normal((Ms, K), dtype=np.float32).astype(bf), dev)
+        bias = ops.gputensor_from_numpy((rng.standard_normal(N, dtype=np.float32) * np.float32(0.02)).astype(bf), dev)
+        y = ops._alloc((Ms, N), bf, dev)
+        flops_rank = 2.0 * Ms * N * K
+        flops_job = flops_rank * world
+        it = [0]
+        epi = E.make_epilogue(bias_ptr=bias.ptr, bias_dt=2, act=2)
+
+        def step(timer=None, x_ptr=None):
+            W = Ws[it[0] % copies]
+            it[0] += 1
+            if timer:
+                timer.start("gemm")
+            E.gemm(Ms, N, K, xs.ptr if x_ptr is None else x_ptr, K, 0, W.ptr, K, 1, y.ptr, N, 2, 2,
+                   epi=epi, device=dev, stream=stream)
+            if timer:
+                timer.stop("gemm")
+        launches_per_step = 1
+        h2d_bytes = Ms * K * 2
+        d2h_bytes = Ms * N * 2
+
+    # ── warm-up
+    for _ in range(args.warmup):
+        l2_flush()
+        step()
+    E.stream_sync(stream)
+    E.check(lib.sf_device_synchronize(), "sync")
+
+    # ── timed region: exactly K steps, each between its own event pair
+    steps = EventTimer(lib, stream)
+    kern = EventTimer(lib, stream)
+    dist.barrier()
+    E.check(lib.sf_device_synchronize(), "sync")
+    with ClockSampler(range(world) if world > 1 else [dev]) as clocks:
+        t_wall = time.perf_counter()
+        for _ in range(args.steps):
+            l2_flush()
+            steps.start("step")
+            step(timer=kern)
+            steps.stop("step")
+        E.stream_sync(stream)
+        E.check(lib.sf_device_synchronize(), "sync")
+        t_wall = time.perf_counter() - t_wall
+        time.sleep(0.25)
+    dist.barrier()
+    step_ms = steps.collect()["step"]
+    kern_ms = kern.collect()
+    rank_s = sum(step_ms) / 1e3
+    job_s = dist.max(rank_s)
+    value = flops_job * args.steps / job_s / 1e12
+
+    # roofline of the dominant kernel (the tcgen05 GEMM; all launches of a step)
+    gemm_ms = sum(sum(v) for v in kern_ms.values())
+    n_launch = sum(len(v) for v in kern_ms.values())
+    achieved = flops_rank * args.steps / (gemm_ms / 1e3) / 1e12
+    hbm, burst, sustained, src = _peaks()
+    peak = sustained if job_s >= 1.0 else burst
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get(args.workload)
+        except Exception:
+            traffic = None
+
+    # ── end to end through the public API with host buffers (pinned), same steps
+    e2e = None
+    if not args.no_e2e:
+        pin_in = E.PinnedHostBuffer(h2d_bytes)
+        pin_out = E.PinnedHostBuffer(d2h_bytes)
+        dev_in = E.DeviceBuffer.alloc(h2d_bytes, dev)
+        src_ptr = (x.ptr if args.workload == "dit_block" else (a.ptr if args.workload == "square" else xs.ptr))
+        E.memcpy(pin_in.ptr, src_ptr, h2d_bytes, 1, stream)
+        res_ptr = (block.y.ptr if args.workload == "dit_block" else (c.ptr if args.workload == "square" else y.ptr))
+        e2e_t = EventTimer(lib, stream)
+        for _ in range(max(1, args.warmup // 2)):
+            E.memcpy(dev_in.ptr, pin_in.ptr, h2d_bytes, 0, stream)
+            step(x_ptr=dev_in.ptr)
+            E.memcpy(pin_out.ptr, res_ptr, d2h_bytes, 1, stream)
+        E.stream_sync(stream)
+        dist.barrier()
+        for _ in range(args.steps):
+            l2_flush()
+            e2e_t.start("e2e")
+            E.memcpy(dev_in.ptr, pin_in.ptr, h2d_bytes, 0, stream)
+            step(x_ptr=dev_in.ptr)
+            E.memcpy(pin_out.ptr, res_ptr, d2h_bytes, 1, stream)
+            e2e_t.stop("e2e")
+        E.stream_sync(stream)
+        dist.barrier()
+        e2e_s = dist.max(sum(e2e_t.collect()["e2e"]) / 1e3)
+        e2e = {"value": flops_job * args.steps / e2e_s / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d_bytes * world, "d2h_bytes_per_step": d2h_bytes * world,
+               "ms_per_step": e2e_s / args.steps * 1e3}
+
+    err = E.device_error_status(dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, cores = cpu_reference_sample(args.workload, budget_s=args.cpu_budget)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if comm is not None:
+        E.stream_sync(stream)
+        lib.sf_comm_destroy(C.c_void_p(comm))
+
+    if rank == 0:
+        line = {
+            "metric": _metric(args.workload), "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": job_s / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong" if args.workload == "dit_block" else "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": _config(args, world),
+            "pct_of_bf16_peak": value / world / burst,
+            "tokens_per_s": (M_TOTAL * args.steps / job_s) if args.workload == "dit_block" else None,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{src} ({'sustained' if peak == sustained else 'burst'} bf16)",
+                         "kernel": "sf::gemm_tc_kernel (tcgen05)",
+                         "launch_ms_mean": gemm_ms / max(1, n_launch)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+            "device_error_word": err,
+            "wall_s_timed": t_wall,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="dit_block", choices=["dit_block", "square", "skinny"])
+    ap.add_argument("--size", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.size is None:
+        args.size = {"dit_block": 0, "square": 8192, "skinny": 8}[args.workload]
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, dist)
+        else:
+            run_gpu_arm(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

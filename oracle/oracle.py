@@ -1,0 +1,356 @@
+"""NumPy restatement of the reference's CPU matmul path (TEST INFRASTRUCTURE).
+
+Every function names the reference file:line it restates.  Paths are relative
+to the reference project root (pictofeed/scaffolding).  On Linux the
+reference's CPU path *is* NumPy/OpenBLAS: its Cython CPU extensions are built
+only on macOS (``setup.py:306-352``), so ``_USE_CYTHON``/``_USE_MPS`` are
+False and every branch below is the one the reference itself executes.
+
+Reduced-precision inputs: the reference has no bf16 storage
+(``dtype.py:31`` maps bfloat16 to float32), so the bf16/fp16 oracle is the
+same fp32 NumPy code applied to inputs rounded to bf16/fp16 with
+round-to-nearest-even ("an fp32 reference computed on identically rounded
+inputs").
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs may
+import this module.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+__all__ = [
+    "round_bf16", "round_f16", "round_to", "bf16_bits", "bf16_from_bits",
+    "linear", "silu", "gelu_tanh", "activation", "linear_act",
+    "matmul", "matmul_nt", "batched_matmul", "batched_matmul_nt",
+    "softmax_rows", "sdpa", "dit_attention_chunked", "dit_layer", "dit_block_linears",
+    "config1_inputs", "square_inputs", "skinny_inputs", "dit_weights",
+    "rel_frobenius", "elementwise_rel_check", "ACT_NONE", "ACT_SILU",
+    "ACT_GELU_TANH",
+]
+
+ACT_NONE = "none"
+ACT_SILU = "silu"
+ACT_GELU_TANH = "gelu_tanh"
+
+
+# ───────────────────────── rounding helpers ──────────────────────────────
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to the nearest bf16 (ties to even); return fp32.
+
+    The reference cannot hold bf16 (``dtype.py:31``); this produces the
+    "identically rounded inputs" the bf16 parity bar is defined on.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    lsb = (u >> np.uint64(16)) & np.uint64(1)
+    r = ((u + np.uint64(0x7FFF) + lsb) & np.uint64(0xFFFF0000)).astype(np.uint32)
+    nan = np.isnan(x)
+    out = r.view(np.float32).copy()
+    if nan.any():
+        out[nan] = np.nan
+    return out
+
+
+def round_f16(x: np.ndarray) -> np.ndarray:
+    """Round fp32 values to fp16 (IEEE round-to-nearest-even); return fp32."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Round to the storage dtype named by ``dtype`` ('f32', 'bf16', 'f16')."""
+    if dtype == "bf16":
+        return round_bf16(x)
+    if dtype == "f16":
+        return round_f16(x)
+    if dtype == "f32":
+        return np.asarray(x, dtype=np.float32)
+    raise ValueError(f"unknown dtype {dtype!r}")
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Raw bf16 bit patterns (uint16) of ``round_bf16(x)``."""
+    return (round_bf16(x).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+
+
+def bf16_from_bits(bits: np.ndarray) -> np.ndarray:
+    """Widen raw bf16 bit patterns (uint16) to fp32."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32)
+            << np.uint32(16)).view(np.float32)
+
+
+# ───────────────────────── elementwise ops ───────────────────────────────
+
+def silu(z: np.ndarray) -> np.ndarray:
+    """SiLU, as ``nn/functional.py:57-59``: ``sig = 1/(1+exp(-x)); x*sig``."""
+    sig = 1.0 / (1.0 + np.exp(-z))
+    return z * sig
+
+
+def gelu_tanh(z: np.ndarray) -> np.ndarray:
+    """GELU (tanh form), as ``nn/functional.py:79-82``."""
+    return 0.5 * z * (1 + np.tanh(
+        math.sqrt(2.0 / math.pi) * (z + 0.044715 * z ** 3)))
+
+
+def activation(z: np.ndarray, act: str) -> np.ndarray:
+    if act == ACT_NONE:
+        return z
+    if act == ACT_SILU:
+        return silu(z)
+    if act == ACT_GELU_TANH:
+        return gelu_tanh(z)
+    raise ValueError(f"unknown activation {act!r}")
+
+
+# ───────────────────────── matmul family ─────────────────────────────────
+
+def linear(x: np.ndarray, W: np.ndarray, b: np.ndarray | None = None) -> np.ndarray:
+    """``nn.Linear`` CPU branch, ``nn/layers.py:129-131``: ``x @ W.T`` then ``+ b``.
+
+    ``F.linear`` (``nn/functional.py:388-391``) is the same arithmetic via
+    ``np.matmul(input, weight.T)``.
+    """
+    y = x @ W.T
+    if b is not None:
+        y = y + b
+    return y
+
+
+def linear_act(x, W, b=None, act: str = ACT_NONE):
+    """``Linear`` followed by the separate activation call the reference's
+    callers make (e.g. ``F.silu(lin(x))``: ``nn/layers.py:129-131`` then
+    ``nn/functional.py:57-59``)."""
+    return activation(linear(x, W, b), act)
+
+
+def matmul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """``sf.matmul`` CPU branch, ``tensor.py:1516-1519``: ``np.matmul``."""
+    return np.matmul(a, b)
+
+
+def matmul_nt(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """``sf.matmul_nt`` fallback, ``tensor.py:1538-1539``: ``matmul(a, b^T)``."""
+    return np.matmul(a, np.swapaxes(b, -2, -1))
+
+
+def batched_matmul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Batched NN product (``dev_batched_matmul`` semantics,
+    ``_cuda_ops.pyx:1122-1149``; CPU arithmetic is ``np.matmul``)."""
+    return np.matmul(a, b)
+
+
+def batched_matmul_nt(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Batched NT product (``dev_batched_matmul_nt``, ``_cuda_ops.pyx:1152-1190``)."""
+    return np.matmul(a, np.swapaxes(b, -2, -1))
+
+
+def softmax_rows(x: np.ndarray) -> np.ndarray:
+    """Row softmax, ``nn/functional.py:131-136``: max-subtract, exp, sum, divide."""
+    x_max = x.max(axis=-1, keepdims=True)
+    e = np.exp(x - x_max)
+    e_sum = e.sum(axis=-1, keepdims=True)
+    np.divide(e, e_sum, out=e)
+    return e
+
+
+def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray,
+         scale: float | None = None) -> np.ndarray:
+    """``F.scaled_dot_product_attention`` CPU branch, ``nn/functional.py:323-357``
+    (no mask, no dropout)."""
+    d = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    k_T = np.swapaxes(k, -2, -1)
+    scores = np.matmul(q, k_T)
+    scores *= scale
+    s_max = scores.max(axis=-1, keepdims=True)
+    scores -= s_max
+    np.exp(scores, out=scores)
+    s_sum = scores.sum(axis=-1, keepdims=True)
+    np.divide(scores, s_sum, out=scores)
+    return np.matmul(scores, v)
+
+
+def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
+                          head_dim: int, chunk: int = 2048,
+                          p_dtype: str = "f32") -> np.ndarray:
+    """Attention over a fused QKV activation, in query chunks.
+
+    ``qkv`` is ``[batch*tokens, 3*heads*head_dim]`` laid out as the reference
+    ``DiTBlock`` slices it (``diffusion/models.py:546-549``: q, k, v are
+    column blocks of ``to_qkv``'s output, head h at columns
+    ``h*head_dim:(h+1)*head_dim``).  Per (b, h) and query chunk:
+    ``S = (Q K^T) * scale``, row softmax in fp32, ``O = P V`` -- the SDPA
+    sequence of ``nn/functional.py:314-320`` / ``:323-357``.  ``p_dtype``
+    rounds P to the storage type the device path keeps it in.
+    Returns ``[batch*tokens, heads*head_dim]``.
+    """
+    rows, width = qkv.shape
+    C = heads * head_dim
+    assert width == 3 * C and rows % batch == 0
+    N = rows // batch
+    scale = 1.0 / math.sqrt(head_dim)
+    out = np.empty((rows, C), dtype=np.float32)
+    for b in range(batch):
+        blk = qkv[b * N:(b + 1) * N]
+        for h in range(heads):
+            q = blk[:, h * head_dim:(h + 1) * head_dim]
+            k = blk[:, C + h * head_dim:C + (h + 1) * head_dim]
+            v = blk[:, 2 * C + h * head_dim:2 * C + (h + 1) * head_dim]
+            for c0 in range(0, N, chunk):
+                c1 = min(c0 + chunk, N)
+                s = (q[c0:c1] @ k.T).astype(np.float32)
+                s *= np.float32(scale)
+                p = softmax_rows(s)
+                p = round_to(p, p_dtype)
+                out[b * N + c0:b * N + c1, h * head_dim:(h + 1) * head_dim] = p @ v
+    return out
+
+
+def dit_layer(x: np.ndarray, w: dict, batch: int, heads: int, head_dim: int,
+              chunk: int = 2048, dtype: str = "bf16") -> np.ndarray:
+    """One DiT layer as the B200 engine runs it (no adaLN / LayerNorm).
+
+    Follows ``DiTBlock.forward`` (``diffusion/models.py:538-590``) minus the
+    adaptive norms: ``qkv = to_qkv(x)`` (no bias, ``:508``), attention,
+    ``x = x + self_out(attn)``, ``x = x + ff_down(gelu(ff_up(x)))``.  The FFN
+    activation is GELU-tanh, as the benchmark configuration specifies (the
+    reference block's own FFN uses SiLU, ``:522-527``).  Intermediate
+    activations are rounded to ``dtype`` at the points where the device path
+    stores them.
+    """
+    r = lambda a: round_to(a, dtype)  # noqa: E731
+    qkv = r(linear(x, w["qkv_w"]))
+    attn = r(dit_attention_chunked(qkv, batch, heads, head_dim, chunk, p_dtype=dtype))
+    h = r(linear(attn, w["out_w"], w["out_b"]) + x)
+    f = r(gelu_tanh(linear(h, w["up_w"], w["up_b"])))
+    return r(linear(f, w["down_w"], w["down_b"]) + h)
+
+
+def dit_block_linears(x: np.ndarray, w: dict, dtype: str = "bf16") -> np.ndarray:
+    """The four DiT block linears as the benchmark's config-4 step chains them
+    (``diffusion/models.py:508-527`` shapes; bias, GELU-tanh and residual as
+    the device epilogues apply them):
+    ``qkv = x Wqkv^T``; ``h = qkv[:, :C] Wo^T + bo + x``;
+    ``f = gelu(h W1^T + b1)``; ``y = f W2^T + b2 + h``.  Intermediates are
+    rounded to ``dtype`` where the device stores them."""
+    C = w["out_w"].shape[0]
+    r = lambda a: round_to(a, dtype)  # noqa: E731
+    qkv = r(linear(x, w["qkv_w"]))
+    h = r(linear(qkv[:, :C], w["out_w"], w["out_b"]) + x)
+    f = r(gelu_tanh(linear(h, w["up_w"], w["up_b"])))
+    return r(linear(f, w["down_w"], w["down_b"]) + h)
+
+
+# ───────────────────────── seeded inputs ─────────────────────────────────
+# Draw order and distributions follow the benchmark configurations: one
+# ``np.random.default_rng(seed)`` stream, x then W then b, drawn in fp32 and
+# then rounded to the storage dtype.
+
+def config1_inputs(seed: int = 0, M: int = 512, K: int = 1024, N: int = 4096):
+    """Config 1: x ~ N(0,1); W, b ~ U(-1/sqrt(K), 1/sqrt(K)) -- the
+    ``nn.Linear`` Kaiming-uniform bound of ``nn/layers.py:66-74``."""
+    rng = np.random.default_rng(seed)
+    k = 1.0 / math.sqrt(K)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.uniform(-k, k, (N, K)).astype(np.float32)
+    b = rng.uniform(-k, k, (N,)).astype(np.float32)
+    return x, W, b
+
+
+def square_inputs(n: int, dtype: str = "bf16", seed: int = 0, m: int | None = None,
+                  k: int | None = None):
+    """Config 2: A [M,K], B [N,K] (``nn.Linear`` weight layout), ~N(0,1)/sqrt(K)."""
+    m = n if m is None else m
+    k = n if k is None else k
+    rng = np.random.default_rng(seed)
+    s = np.float32(1.0 / math.sqrt(k))
+    A = rng.standard_normal((m, k), dtype=np.float32) * s
+    B = rng.standard_normal((n, k), dtype=np.float32) * s
+    return round_to(A, dtype), round_to(B, dtype)
+
+
+def skinny_inputs(M: int, N: int, K: int = 4096, seed: int = 0, dtype: str = "bf16"):
+    """Config 3: x ~ N(0,1) [M,K], W ~ N(0,0.02) [N,K], b ~ N(0,0.02) [N]."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    b = rng.standard_normal((N,), dtype=np.float32) * np.float32(0.02)
+    return round_to(x, dtype), round_to(W, dtype), round_to(b, dtype)
+
+
+def dit_weights(hidden: int = 1920, seed: int = 1, dtype: str = "bf16",
+                zero_bias: bool = True) -> dict:
+    """Config 4/5 block weights: W ~ N(0, 0.02), biases 0 (or N(0,0.02))."""
+    rng = np.random.default_rng(seed)
+    C = hidden
+
+    def w(n, k):
+        return round_to(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02), dtype)
+
+    def b(n):
+        if zero_bias:
+            return np.zeros((n,), np.float32)
+        return round_to(rng.standard_normal((n,), dtype=np.float32) * np.float32(0.02), dtype)
+
+    return {
+        "qkv_w": w(3 * C, C),
+        "out_w": w(C, C), "out_b": b(C),
+        "up_w": w(4 * C, C), "up_b": b(4 * C),
+        "down_w": w(C, 4 * C), "down_b": b(C),
+    }
+
+
+# ───────────────────────── tolerance checks ──────────────────────────────
+
+def rel_frobenius(out: np.ndarray, ref: np.ndarray) -> float:
+    """``||out - ref||_F / ||ref||_F`` in float64 (the fp32 parity bar, 1e-5)."""
+    o = np.asarray(out, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    den = np.linalg.norm(r)
+    num = np.linalg.norm(o - r)
+    return float(num / den) if den > 0 else float(num)
+
+
+def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
+                          tau: float = 1e-2):
+    """Per-element relative check for bf16/fp16 outputs (bar: 1e-2).
+
+    An element passes when ``|out - ref| <= rtol * max(|ref|, tau * rms(ref row))``.
+    The floor ``tau * rms(row)`` only matters where the exact value cancels
+    to nearly zero (|ref| below 1% of the row's RMS), where a relative error
+    is undefined in practice.  Returns ``(ok, stats)`` with the worst pure
+    relative error, the worst error against the floored denominator, and the
+    number of elements that needed the floor.
+    """
+    o = np.asarray(out, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    if r.ndim == 0:
+        r = r.reshape(1)
+        o = o.reshape(1)
+    rr = r.reshape(-1, r.shape[-1]) if r.ndim > 1 else r.reshape(1, -1)
+    oo = o.reshape(rr.shape)
+    rms = np.sqrt(np.mean(rr * rr, axis=1, keepdims=True))
+    absr = np.abs(rr)
+    den = np.maximum(absr, tau * rms)
+    den = np.where(den > 0, den, 1.0)
+    err = np.abs(oo - rr)
+    floored = err / den
+    finite = np.isfinite(oo).all()
+    pure = err / np.where(absr > 0, absr, np.inf)
+    needed_floor = int(np.count_nonzero((pure > rtol) & (floored <= rtol)))
+    worst = float(floored.max()) if floored.size else 0.0
+    stats = {
+        "max_rel_floored": worst,
+        "max_rel_pure": float(np.nanmax(pure)) if pure.size else 0.0,
+        "n_needed_floor": needed_floor,
+        "n": int(rr.size),
+        "tau": tau,
+        "rtol": rtol,
+        "finite": bool(finite),
+    }
+    return bool(finite and worst <= rtol), stats

@@ -1,0 +1,39 @@
+// Internal declarations shared by the engine's translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/sf_engine.h"
+
+namespace sf {
+
+// Record `msg` as the calling thread's last error and return `code`.
+int32_t fail(int32_t code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Translate a CUDA runtime error into SF_ERR_CUDA (with context) or SF_OK.
+int32_t cuda_status(cudaError_t e, const char* what);
+
+#define SF_CUDA_TRY(expr)                                  \
+  do {                                                     \
+    cudaError_t _e = (expr);                               \
+    if (_e != cudaSuccess) return ::sf::cuda_status(_e, #expr); \
+  } while (0)
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t smem_optin = 0;
+  int* err_word = nullptr;  // device-side error word (cudaMalloc'd once per device)
+};
+
+// Lazily initialised per-device facts for the CURRENT device.
+int32_t current_device_info(DeviceInfo** out, int* device);
+
+// Global knobs.
+int fp32_mode();
+int kernel_override();
+
+}  // namespace sf

@@ -1,0 +1,656 @@
+// GEMM / softmax / elementwise entry points of the C ABI and their dispatch.
+//
+// Dispatch policy (sf_gemm / sf_gemm_batched):
+//   16-bit inputs, TMA-describable layout  -> tcgen05 GEMM
+//       * B stored [N,K] (trans_b = 1, nn.Linear weights): K-major B
+//       * B stored [K,N] (trans_b = 0): MN-major B, 64-wide swizzled slabs
+//       * M <= 256, unbatched, K-major B: swap-AB ("skinny-M"): the weight
+//         rows fill the 128-row UMMA tile, the few activation rows become
+//         the UMMA N extent, outputs are stored transposed; split-K over a
+//         zeroed fp32 workspace when there are too few tiles to cover the SMs
+//   fp32 inputs:
+//       * SF_FP32_ACCURATE (default): 3xTF32 -- operands are split into
+//         K-concatenated TF32 hi/lo panels in the workspace and multiplied
+//         by the tcgen05 kernel in kind::tf32
+//       * SF_FP32_TF32: single TF32 pass (direct when K-major and aligned)
+//       * SF_FP32_FFMA: IEEE fp32 SIMT kernel
+//   anything else (transposed A, strides TMA cannot describe) -> SIMT kernel.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.h"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "rowwise.cuh"
+
+namespace sf {
+
+// ───────────────────────────── TMA descriptors ─────────────────────────────
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// 4-D view: element (i0, i1, i2, i3) at base + i1*s1 + i2*s2 + i3*s3 (elements),
+// i0 contiguous.  Extent-1 batch dims get a packed stride.
+struct MapSpec {
+  const void* base;
+  int esize;
+  CUtensorMapDataType dt;
+  uint64_t d0, d1, d2, d3;
+  int64_t s1, s2, s3;
+  uint32_t box0, box1;
+};
+
+static int32_t encode_map(CUtensorMap* m, const MapSpec& s) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const uint64_t e = static_cast<uint64_t>(s.esize);
+  uint64_t st1 = static_cast<uint64_t>(s.s1) * e;
+  uint64_t st2 = s.d2 > 1 ? static_cast<uint64_t>(s.s2) * e : st1 * s.d1;
+  uint64_t st3 = s.d3 > 1 ? static_cast<uint64_t>(s.s3) * e : st2 * s.d2;
+  st2 = (st2 + 15) & ~15ull;
+  st3 = (st3 + 15) & ~15ull;
+  cuuint64_t dims[4] = {s.d0, s.d1, s.d2, s.d3};
+  cuuint64_t strides[3] = {st1, st2, st3};
+  cuuint32_t box[4] = {s.box0, s.box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(m, s.dt, 4, const_cast<void*>(s.base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(SF_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu,%llu} strides "
+                "{%llu,%llu,%llu} box {%u,%u}",
+                static_cast<int>(r), (unsigned long long)s.d0, (unsigned long long)s.d1,
+                (unsigned long long)s.d2, (unsigned long long)s.d3, (unsigned long long)st1,
+                (unsigned long long)st2, (unsigned long long)st3, s.box0, s.box1);
+  return SF_OK;
+}
+
+static CUtensorMapDataType tma_dtype(int dt) {
+  return dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+         : dt == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+static int esize(int dt) { return dt == kF32 ? 4 : 2; }
+
+// ───────────────────────────── problem / plan ─────────────────────────────
+
+struct Problem {
+  int64_t M, N, K;
+  const void* A;
+  int64_t lda;
+  int ta;
+  const void* B;
+  int64_t ldb;
+  int tb;
+  void* C;
+  int64_t ldc;
+  int in_dt, out_dt;
+  sf_epilogue epi;
+  int64_t nb0, nb1, as0, as1, bs0, bs1, cs0, cs1;
+  void* ws;
+  size_t ws_bytes;
+  cudaStream_t stream;
+};
+
+enum PlanKind { kPlanSimt, kPlanTc, kPlanTcSwap, kPlanTf32Split, kPlanTf32Direct };
+
+struct Plan {
+  PlanKind kind = kPlanSimt;
+  int bn = 128;
+  bool b_mn = false;
+  int splits = 1;
+  int64_t kk = 0;       // reduction length seen by the TC kernel (3K for 3xTF32)
+  int64_t ld_split = 0; // leading dimension of the split panels
+  size_t ws_bytes = 0;
+};
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool bytes16(int64_t elems, int es) { return ((elems * es) & 15) == 0; }
+static int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+static int pick_bn(int64_t n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+// `have_ptrs` = false when only sizing the workspace (pointers unknown, assumed aligned).
+static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
+  Plan pl;
+  const int ovr = kernel_override();
+  const int64_t batch = p.nb0 * p.nb1;
+  if (p.in_dt == kF32) {
+    const int mode = fp32_mode();
+    if (mode == SF_FP32_FFMA || ovr == SF_KERNEL_SIMT) return pl;
+    if (mode == SF_FP32_TF32) {
+      const bool direct = p.ta == 0 && p.tb == 1 && bytes16(p.lda, 4) && bytes16(p.ldb, 4) &&
+                          bytes16(p.as0, 4) && bytes16(p.as1, 4) && bytes16(p.bs0, 4) &&
+                          bytes16(p.bs1, 4) &&
+                          (!have_ptrs || (aligned16(p.A) && aligned16(p.B)));
+      if (direct) {
+        pl.kind = kPlanTf32Direct;
+        pl.kk = p.K;
+        pl.bn = pick_bn(p.N);
+        return pl;
+      }
+      pl.kk = p.K;
+    } else {
+      pl.kk = 3 * p.K;
+    }
+    pl.kind = kPlanTf32Split;
+    pl.ld_split = (pl.kk + 3) & ~int64_t(3);
+    pl.bn = pick_bn(p.N);
+    pl.ws_bytes = static_cast<size_t>(batch) * static_cast<size_t>(p.M + p.N) *
+                  static_cast<size_t>(pl.ld_split) * 4u;
+    return pl;
+  }
+  // 16-bit inputs
+  if (ovr == SF_KERNEL_SIMT || p.ta != 0) return pl;
+  const bool a_ok = bytes16(p.lda, 2) && bytes16(p.as0, 2) && bytes16(p.as1, 2) &&
+                    (!have_ptrs || aligned16(p.A));
+  const bool b_ok = bytes16(p.ldb, 2) && bytes16(p.bs0, 2) && bytes16(p.bs1, 2) &&
+                    (!have_ptrs || aligned16(p.B));
+  if (!a_ok || !b_ok) return pl;
+  if (p.tb == 0) {
+    pl.kind = kPlanTc;
+    pl.b_mn = true;
+    pl.bn = p.N <= 64 ? 64 : (p.N <= 128 ? 128 : 256);
+    return pl;
+  }
+  if (batch == 1 && p.M <= 256 && p.N >= 256) {
+    pl.kind = kPlanTcSwap;
+    pl.bn = pick_bn(p.M);
+    const int64_t tiles = ceil_div(p.N, 128);
+    const int64_t kb = ceil_div(p.K, 64);
+    int64_t splits = 1;
+    if (tiles * 2 <= sm_count && kb >= 8) {
+      splits = std::min<int64_t>(kb / 4, sm_count / tiles);
+      splits = std::max<int64_t>(splits, 1);
+      const int64_t per = ceil_div(kb, splits);
+      splits = ceil_div(kb, per);
+    }
+    pl.splits = static_cast<int>(splits);
+    if (pl.splits > 1) pl.ws_bytes = static_cast<size_t>(p.M) * static_cast<size_t>(p.N) * 4u;
+    return pl;
+  }
+  pl.kind = kPlanTc;
+  pl.bn = p.N > 128 ? 256 : pick_bn(p.N);
+  if (pl.bn < 64 && p.M > 4096) pl.bn = 64;
+  return pl;
+}
+
+static EpilogueArgs to_epi(const sf_epilogue& e) {
+  EpilogueArgs a;
+  a.alpha = e.alpha;
+  a.beta = e.beta;
+  a.bias = e.bias;
+  a.bias_dtype = e.bias_dtype;
+  a.bias_on_rows = 0;
+  a.act = e.activation;
+  a.residual = e.residual;
+  a.residual_dtype = e.residual_dtype;
+  a.ldr = e.ldr;
+  a.r_stride0 = e.r_stride0;
+  a.r_stride1 = e.r_stride1;
+  return a;
+}
+
+// ───────────────────────────── launchers ─────────────────────────────
+
+template <class Cfg>
+static int32_t launch_tc_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a,
+                             int grid, cudaStream_t s, int device) {
+  static bool attr_set[64] = {false};
+  if (device < 64 && !attr_set[device]) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::SMEM_BYTES));
+    attr_set[device] = true;
+  }
+  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ma, mb, a);
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
+// Stage counts per N tile: keep ~192-216 KB of operand ring per CTA.
+template <int FMT, bool BMN>
+static int32_t launch_tc(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a,
+                         int grid, cudaStream_t s, int device) {
+  if constexpr (BMN) {
+    switch (bn) {
+      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, true>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, true>>(ma, mb, a, grid, s, device);
+      case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, true>>(ma, mb, a, grid, s, device);
+      default: return fail(SF_ERR_UNSUPPORTED, "MN-major B tile width %d", bn);
+    }
+  } else {
+    switch (bn) {
+      case 16: return launch_tc_cfg<TcCfg<16, 12, FMT, false>>(ma, mb, a, grid, s, device);
+      case 32: return launch_tc_cfg<TcCfg<32, 10, FMT, false>>(ma, mb, a, grid, s, device);
+      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, false>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, false>>(ma, mb, a, grid, s, device);
+      case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, false>>(ma, mb, a, grid, s, device);
+      default: return fail(SF_ERR_UNSUPPORTED, "tile width %d", bn);
+    }
+  }
+}
+
+static int32_t dispatch_tc(int fmt, bool bmn, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                           const GemmTcArgs& a, int grid, cudaStream_t s, int device) {
+  if (fmt == kBF16) {
+    return bmn ? launch_tc<1, true>(bn, ma, mb, a, grid, s, device)
+               : launch_tc<1, false>(bn, ma, mb, a, grid, s, device);
+  }
+  if (fmt == kF16) {
+    return bmn ? launch_tc<0, true>(bn, ma, mb, a, grid, s, device)
+               : launch_tc<0, false>(bn, ma, mb, a, grid, s, device);
+  }
+  if (bmn) return fail(SF_ERR_UNSUPPORTED, "MN-major TF32 operand");
+  return launch_tc<2, false>(bn, ma, mb, a, grid, s, device);
+}
+
+static int grid_for(int64_t n, int sm_count) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), sm_count * 8LL)));
+}
+
+static int32_t run_simt(const Problem& p) {
+  GemmSimtArgs a;
+  a.M = static_cast<int>(p.M);
+  a.N = static_cast<int>(p.N);
+  a.K = static_cast<int>(p.K);
+  a.nb0 = static_cast<int>(p.nb0);
+  a.nb1 = static_cast<int>(p.nb1);
+  a.A = p.A;
+  a.a_dtype = p.in_dt;
+  a.a_rs = p.ta ? 1 : p.lda;
+  a.a_cs = p.ta ? p.lda : 1;
+  a.a_s0 = p.as0;
+  a.a_s1 = p.as1;
+  a.B = p.B;
+  a.b_dtype = p.in_dt;
+  a.b_ks = p.tb ? 1 : p.ldb;
+  a.b_ns = p.tb ? p.ldb : 1;
+  a.b_s0 = p.bs0;
+  a.b_s1 = p.bs1;
+  a.C = p.C;
+  a.out_dtype = p.out_dt;
+  a.ldc = p.ldc;
+  a.c_s0 = p.cs0;
+  a.c_s1 = p.cs1;
+  a.epi = to_epi(p.epi);
+  const int64_t batch = p.nb0 * p.nb1;
+  if (batch > 65535) return fail(SF_ERR_UNSUPPORTED, "SIMT GEMM batch %lld > 65535", (long long)batch);
+  dim3 grid(static_cast<unsigned>(ceil_div(p.N, kSimtBN)), static_cast<unsigned>(ceil_div(p.M, kSimtBM)),
+            static_cast<unsigned>(batch));
+  if (grid.y > 65535) return fail(SF_ERR_UNSUPPORTED, "SIMT GEMM M too large");
+  gemm_simt_kernel<<<grid, kSimtThreads, 0, p.stream>>>(a);
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
+static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, int device) {
+  const bool swap = pl.kind == kPlanTcSwap;
+  const bool tf32 = pl.kind == kPlanTf32Split || pl.kind == kPlanTf32Direct;
+  const int fmt = tf32 ? kF32 : p.in_dt;
+  const int es = tf32 ? 4 : 2;
+  const int bk = 128 / es;
+  const int64_t kk = tf32 ? pl.kk : p.K;
+
+  // Tile-orientation operands.
+  const void* ta_ptr = swap ? p.B : p.A;
+  int64_t ta_ld = swap ? p.ldb : p.lda;
+  int64_t ta_s0 = swap ? p.bs0 : p.as0, ta_s1 = swap ? p.bs1 : p.as1;
+  const void* tb_ptr = swap ? p.A : p.B;
+  int64_t tb_ld = swap ? p.lda : p.ldb;
+  int64_t tb_s0 = swap ? p.as0 : p.bs0, tb_s1 = swap ? p.as1 : p.bs1;
+  const int64_t tM = swap ? p.N : p.M;
+  const int64_t tN = swap ? p.M : p.N;
+
+  if (pl.kind == kPlanTf32Split) {
+    // Split / repack both operands into dense K-major TF32 panels.
+    float* ap = static_cast<float*>(p.ws);
+    float* bp = ap + static_cast<size_t>(p.nb0 * p.nb1) * p.M * pl.ld_split;
+    const int pattern_a = (pl.kk == p.K) ? 2 : 0;
+    const int pattern_b = (pl.kk == p.K) ? 2 : 1;
+    for (int64_t b1 = 0; b1 < p.nb1; ++b1)
+      for (int64_t b0 = 0; b0 < p.nb0; ++b0) {
+        const int64_t z = b1 * p.nb0 + b0;
+        const float* asrc = static_cast<const float*>(p.A) + b0 * p.as0 + b1 * p.as1;
+        const float* bsrc = static_cast<const float*>(p.B) + b0 * p.bs0 + b1 * p.bs1;
+        tf32_split_kernel<<<grid_for(p.M * p.K, dev.sm_count), 256, 0, p.stream>>>(
+            asrc, p.ta ? 1 : p.lda, p.ta ? p.lda : 1, static_cast<int>(p.M), static_cast<int>(p.K),
+            ap + z * p.M * pl.ld_split, pl.ld_split, pattern_a);
+        tf32_split_kernel<<<grid_for(p.N * p.K, dev.sm_count), 256, 0, p.stream>>>(
+            bsrc, p.tb ? p.ldb : 1, p.tb ? 1 : p.ldb, static_cast<int>(p.N), static_cast<int>(p.K),
+            bp + z * p.N * pl.ld_split, pl.ld_split, pattern_b);
+        SF_CUDA_TRY(cudaGetLastError());
+      }
+    ta_ptr = ap;
+    ta_ld = pl.ld_split;
+    ta_s0 = p.M * pl.ld_split;
+    ta_s1 = p.nb0 * p.M * pl.ld_split;
+    tb_ptr = bp;
+    tb_ld = pl.ld_split;
+    tb_s0 = p.N * pl.ld_split;
+    tb_s1 = p.nb0 * p.N * pl.ld_split;
+  }
+
+  CUtensorMap ma, mbm;
+  MapSpec sa{ta_ptr, es, tma_dtype(fmt), static_cast<uint64_t>(kk), static_cast<uint64_t>(tM),
+             static_cast<uint64_t>(p.nb0), static_cast<uint64_t>(p.nb1), ta_ld, ta_s0, ta_s1,
+             static_cast<uint32_t>(bk), 128u};
+  int32_t st = encode_map(&ma, sa);
+  if (st != SF_OK) return st;
+  if (pl.b_mn) {
+    MapSpec sb{tb_ptr, es, tma_dtype(fmt), static_cast<uint64_t>(tN), static_cast<uint64_t>(kk),
+               static_cast<uint64_t>(p.nb0), static_cast<uint64_t>(p.nb1), tb_ld, tb_s0, tb_s1,
+               64u, static_cast<uint32_t>(bk)};
+    st = encode_map(&mbm, sb);
+  } else {
+    MapSpec sb{tb_ptr, es, tma_dtype(fmt), static_cast<uint64_t>(kk), static_cast<uint64_t>(tN),
+               static_cast<uint64_t>(p.nb0), static_cast<uint64_t>(p.nb1), tb_ld, tb_s0, tb_s1,
+               static_cast<uint32_t>(bk), static_cast<uint32_t>(pl.bn)};
+    st = encode_map(&mbm, sb);
+  }
+  if (st != SF_OK) return st;
+
+  GemmTcArgs a;
+  a.M = static_cast<int>(tM);
+  a.N = static_cast<int>(tN);
+  a.K = static_cast<int>(kk);
+  a.nb0 = static_cast<int>(p.nb0);
+  a.nb1 = static_cast<int>(p.nb1);
+  a.m_tiles = static_cast<int>(ceil_div(tM, 128));
+  a.n_tiles = static_cast<int>(ceil_div(tN, pl.bn));
+  a.k_blocks = static_cast<int>(ceil_div(kk, bk));
+  const int64_t total = int64_t(a.m_tiles) * a.n_tiles * p.nb0 * p.nb1;
+  if (total * pl.splits > INT32_MAX) return fail(SF_ERR_UNSUPPORTED, "too many tiles");
+  a.total_tiles = static_cast<int>(total);
+  a.group_m = 8;
+  a.k_splits = pl.splits;
+  a.kb_per_split = static_cast<int>(ceil_div(a.k_blocks, pl.splits));
+  a.C = p.C;
+  a.out_dtype = p.out_dt;
+  a.ldc = p.ldc;
+  a.c_stride0 = p.cs0;
+  a.c_stride1 = p.cs1;
+  a.c_trans = swap ? 1 : 0;
+  const int oes = esize(p.out_dt);
+  a.vec_ok = (!swap && aligned16(p.C) && bytes16(p.ldc, oes) && bytes16(p.cs0, oes) &&
+              bytes16(p.cs1, oes))
+                 ? 1
+                 : 0;
+  a.ws = nullptr;
+  a.ldw = 0;
+  a.epi = to_epi(p.epi);
+  a.err = dev.err_word;
+  if (pl.splits > 1) {
+    a.ws = static_cast<float*>(p.ws);
+    a.ldw = p.N;  // output orientation [M][N]
+    SF_CUDA_TRY(cudaMemsetAsync(p.ws, 0, static_cast<size_t>(p.M) * p.N * 4u, p.stream));
+  }
+  const int64_t units = total * pl.splits;
+  const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
+  st = dispatch_tc(fmt, pl.b_mn, pl.bn, ma, mbm, a, grid, p.stream, device);
+  if (st != SF_OK) return st;
+  if (pl.splits > 1) {
+    epilogue_finalize_kernel<<<grid_for(p.M * p.N, dev.sm_count), 256, 0, p.stream>>>(
+        static_cast<const float*>(p.ws), p.N, static_cast<int>(p.M), static_cast<int>(p.N), p.C,
+        p.out_dt, p.ldc, to_epi(p.epi));
+    SF_CUDA_TRY(cudaGetLastError());
+  }
+  return SF_OK;
+}
+
+static int32_t validate(const Problem& p) {
+  if (p.M < 0 || p.N < 0 || p.K < 0) return fail(SF_ERR_INVALID_ARGUMENT, "negative dimension");
+  if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX)
+    return fail(SF_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  if (p.nb0 < 1 || p.nb1 < 1) return fail(SF_ERR_INVALID_ARGUMENT, "batch counts must be >= 1");
+  for (int dt : {p.in_dt, p.out_dt})
+    if (dt != kF32 && dt != kF16 && dt != kBF16)
+      return fail(SF_ERR_INVALID_ARGUMENT, "unknown dtype %d", dt);
+  if (p.ta != 0 && p.ta != 1) return fail(SF_ERR_INVALID_ARGUMENT, "trans_a must be 0 or 1");
+  if (p.tb != 0 && p.tb != 1) return fail(SF_ERR_INVALID_ARGUMENT, "trans_b must be 0 or 1");
+  if (p.epi.activation < SF_ACT_NONE || p.epi.activation > SF_ACT_GELU_TANH)
+    return fail(SF_ERR_INVALID_ARGUMENT, "unknown activation %d", p.epi.activation);
+  if (p.M == 0 || p.N == 0) return SF_OK;
+  if (!p.C) return fail(SF_ERR_INVALID_ARGUMENT, "null C");
+  if (p.K > 0 && (!p.A || !p.B)) return fail(SF_ERR_INVALID_ARGUMENT, "null A or B");
+  if (p.ldc < p.N) return fail(SF_ERR_INVALID_ARGUMENT, "ldc %lld < N %lld", (long long)p.ldc, (long long)p.N);
+  if (p.K > 0) {
+    if (p.lda < (p.ta ? p.M : p.K)) return fail(SF_ERR_INVALID_ARGUMENT, "lda too small");
+    if (p.ldb < (p.tb ? p.K : p.N)) return fail(SF_ERR_INVALID_ARGUMENT, "ldb too small");
+  }
+  if (p.epi.bias && p.epi.bias_dtype != kF32 && p.epi.bias_dtype != kF16 && p.epi.bias_dtype != kBF16)
+    return fail(SF_ERR_INVALID_ARGUMENT, "unknown bias dtype");
+  if (p.epi.residual && p.epi.ldr < p.N) return fail(SF_ERR_INVALID_ARGUMENT, "ldr < N");
+  return SF_OK;
+}
+
+static int32_t gemm_impl(Problem& p) {
+  int32_t st = validate(p);
+  if (st != SF_OK) return st;
+  if (p.M == 0 || p.N == 0) return SF_OK;
+  DeviceInfo* dev = nullptr;
+  int device = 0;
+  st = current_device_info(&dev, &device);
+  if (st != SF_OK) return st;
+  if (p.K == 0) {
+    // Empty reduction: D = epilogue(0) per batch.
+    for (int64_t b1 = 0; b1 < p.nb1; ++b1)
+      for (int64_t b0 = 0; b0 < p.nb0; ++b0) {
+        EpilogueArgs e = to_epi(p.epi);
+        if (e.residual) {
+          const int res_es = esize(e.residual_dtype);
+          e.residual = static_cast<const char*>(e.residual) + (b0 * e.r_stride0 + b1 * e.r_stride1) * res_es;
+        }
+        void* c = static_cast<char*>(p.C) + (b0 * p.cs0 + b1 * p.cs1) * esize(p.out_dt);
+        epilogue_finalize_kernel<<<grid_for(p.M * p.N, dev->sm_count), 256, 0, p.stream>>>(
+            nullptr, 0, static_cast<int>(p.M), static_cast<int>(p.N), c, p.out_dt, p.ldc, e);
+      }
+    SF_CUDA_TRY(cudaGetLastError());
+    return SF_OK;
+  }
+  const Plan pl = make_plan(p, dev->sm_count, true);
+  if (pl.ws_bytes > 0 && (p.ws == nullptr || p.ws_bytes < pl.ws_bytes))
+    return fail(SF_ERR_WORKSPACE, "workspace of %zu bytes required (%zu given)", pl.ws_bytes,
+                p.ws ? p.ws_bytes : size_t(0));
+  if (pl.kind == kPlanSimt) {
+    if (kernel_override() == SF_KERNEL_TCGEN05)
+      return fail(SF_ERR_UNSUPPORTED, "layout not supported by the tcgen05 kernel");
+    return run_simt(p);
+  }
+  return run_tc(p, pl, *dev, device);
+}
+
+static Problem make_problem(const sf_batch* batch, int64_t M, int64_t N, int64_t K, const void* A,
+                            int64_t lda, int32_t trans_a, const void* B, int64_t ldb,
+                            int32_t trans_b, void* C, int64_t ldc, int32_t in_dtype,
+                            int32_t out_dtype, const sf_epilogue* epi, void* ws, size_t ws_bytes,
+                            void* stream) {
+  Problem p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.A = A;
+  p.lda = lda;
+  p.ta = trans_a;
+  p.B = B;
+  p.ldb = ldb;
+  p.tb = trans_b;
+  p.C = C;
+  p.ldc = ldc;
+  p.in_dt = in_dtype;
+  p.out_dt = out_dtype;
+  if (epi) {
+    p.epi = *epi;
+  } else {
+    p.epi = sf_epilogue{};
+    p.epi.alpha = 1.0f;
+  }
+  if (batch) {
+    p.nb0 = batch->count0;
+    p.nb1 = batch->count1;
+    p.as0 = batch->a_stride0;
+    p.as1 = batch->a_stride1;
+    p.bs0 = batch->b_stride0;
+    p.bs1 = batch->b_stride1;
+    p.cs0 = batch->c_stride0;
+    p.cs1 = batch->c_stride1;
+  } else {
+    p.nb0 = p.nb1 = 1;
+    p.as0 = p.as1 = p.bs0 = p.bs1 = p.cs0 = p.cs1 = 0;
+  }
+  p.ws = ws;
+  p.ws_bytes = ws_bytes;
+  p.stream = static_cast<cudaStream_t>(stream);
+  return p;
+}
+
+}  // namespace sf
+
+using namespace sf;
+
+extern "C" {
+
+int32_t sf_gemm(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, int32_t trans_a,
+                const void* B, int64_t ldb, int32_t trans_b, void* C, int64_t ldc,
+                int32_t in_dtype, int32_t out_dtype, const sf_epilogue* epi, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  Problem p = make_problem(nullptr, M, N, K, A, lda, trans_a, B, ldb, trans_b, C, ldc, in_dtype,
+                           out_dtype, epi, workspace, workspace_bytes, stream);
+  return gemm_impl(p);
+}
+
+int32_t sf_gemm_batched(const sf_batch* batch, int64_t M, int64_t N, int64_t K, const void* A,
+                        int64_t lda, int32_t trans_a, const void* B, int64_t ldb, int32_t trans_b,
+                        void* C, int64_t ldc, int32_t in_dtype, int32_t out_dtype,
+                        const sf_epilogue* epi, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!batch) return fail(SF_ERR_INVALID_ARGUMENT, "null batch descriptor");
+  Problem p = make_problem(batch, M, N, K, A, lda, trans_a, B, ldb, trans_b, C, ldc, in_dtype,
+                           out_dtype, epi, workspace, workspace_bytes, stream);
+  return gemm_impl(p);
+}
+
+int32_t sf_gemm_workspace_size(const sf_batch* batch, int64_t M, int64_t N, int64_t K,
+                               int32_t trans_a, int32_t trans_b, int32_t in_dtype,
+                               int32_t out_dtype, size_t* bytes) {
+  if (!bytes) return fail(SF_ERR_INVALID_ARGUMENT, "null output");
+  *bytes = 0;
+  const int64_t lda = trans_a ? M : K, ldb = trans_b ? K : N;
+  Problem p = make_problem(batch, M, N, K, nullptr, lda, trans_a, nullptr, ldb, trans_b, nullptr,
+                           N, in_dtype, out_dtype, nullptr, nullptr, 0, nullptr);
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return SF_OK;
+  int sm = 148;
+  DeviceInfo* dev = nullptr;
+  int cnt = 0;
+  if (cudaGetDeviceCount(&cnt) == cudaSuccess && cnt > 0 && current_device_info(&dev, nullptr) == SF_OK)
+    sm = dev->sm_count;
+  else
+    cudaGetLastError();
+  *bytes = make_plan(p, sm, false).ws_bytes;
+  return SF_OK;
+}
+
+int32_t sf_softmax_rows(const void* x, int32_t x_dtype, int64_t ldx, void* y, int32_t y_dtype,
+                        int64_t ldy, int64_t rows, int64_t cols, float scale, void* stream) {
+  if (rows < 0 || cols < 0) return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
+  if (rows == 0 || cols == 0) return SF_OK;
+  if (!x || !y) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldx < cols || ldy < cols) return fail(SF_ERR_INVALID_ARGUMENT, "leading dimension < cols");
+  if (rows > INT32_MAX || cols > INT32_MAX) return fail(SF_ERR_UNSUPPORTED, "softmax size");
+  for (int dt : {x_dtype, y_dtype})
+    if (dt != kF32 && dt != kF16 && dt != kBF16) return fail(SF_ERR_INVALID_ARGUMENT, "dtype %d", dt);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t nv = cols / 4;
+  const bool vec = x_dtype == kF32 && (cols % 4) == 0 && aligned16(x) && (ldx % 4) == 0 &&
+                   (y_dtype == kF32 ? (aligned16(y) && ldy % 4 == 0)
+                                    : ((reinterpret_cast<uintptr_t>(y) & 7u) == 0 && ldy % 4 == 0));
+  const unsigned grid = static_cast<unsigned>(rows);
+  if (vec && nv <= int64_t(kSoftmaxThreads) * 16) {
+    const int64_t vpt = ceil_div(nv, kSoftmaxThreads);
+    const float* xf = static_cast<const float*>(x);
+    const int c = static_cast<int>(cols);
+    if (vpt <= 1)
+      softmax_rows_vec_kernel<1><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
+    else if (vpt <= 2)
+      softmax_rows_vec_kernel<2><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
+    else if (vpt <= 4)
+      softmax_rows_vec_kernel<4><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
+    else if (vpt <= 9)
+      softmax_rows_vec_kernel<9><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
+    else
+      softmax_rows_vec_kernel<16><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
+  } else {
+    softmax_rows_generic_kernel<<<grid, kSoftmaxThreads, 0, s>>>(x, x_dtype, ldx, y, y_dtype, ldy,
+                                                                 static_cast<int>(cols), scale);
+  }
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
+int32_t sf_unary(const void* x, int32_t x_dtype, void* y, int32_t y_dtype, int64_t n, float alpha,
+                 int32_t activation, void* stream) {
+  if (n < 0) return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
+  if (n == 0) return SF_OK;
+  if (!x || !y) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
+  if (activation < SF_ACT_NONE || activation > SF_ACT_GELU_TANH)
+    return fail(SF_ERR_INVALID_ARGUMENT, "unknown activation %d", activation);
+  for (int dt : {x_dtype, y_dtype})
+    if (dt != kF32 && dt != kF16 && dt != kBF16) return fail(SF_ERR_INVALID_ARGUMENT, "dtype %d", dt);
+  DeviceInfo* dev = nullptr;
+  int32_t st = current_device_info(&dev, nullptr);
+  if (st != SF_OK) return st;
+  unary_act_kernel<<<grid_for(n, dev->sm_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, x_dtype, y, y_dtype, n, alpha, activation);
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
+int32_t sf_selftest_bounded_wait(int64_t limit_ns, int32_t* device_code, void* stream) {
+  if (!device_code) return fail(SF_ERR_INVALID_ARGUMENT, "null output");
+  if (limit_ns <= 0 || limit_ns > 10000000000LL)
+    return fail(SF_ERR_INVALID_ARGUMENT, "limit must be in (0, 10 s]");
+  DeviceInfo* dev = nullptr;
+  int32_t st = current_device_info(&dev, nullptr);
+  if (st != SF_OK) return st;
+  int* word = dev->err_word + 32;  // private slot, separate from the GEMM error word
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SF_CUDA_TRY(cudaMemsetAsync(word, 0, sizeof(int), s));
+  bounded_wait_selftest_kernel<<<1, 32, 0, s>>>(word, static_cast<unsigned long long>(limit_ns));
+  SF_CUDA_TRY(cudaGetLastError());
+  int v = 0;
+  SF_CUDA_TRY(cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SF_CUDA_TRY(cudaStreamSynchronize(s));
+  *device_code = v;
+  return SF_OK;
+}
+
+}  // extern "C"

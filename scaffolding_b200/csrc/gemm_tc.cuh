@@ -1,0 +1,385 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[tile] = A[BM x K] * B[BN x K]^T   (fp32 accumulation in TMEM)
+//
+// Replaces the cuBLAS calls of the reference matmul path:
+//   cuda_sgemm / cuda_sgemm_batched      _cuda_kernels.cu:1175-1243
+//   (dev_matmul, dev_matmul_nt, dev_batched_matmul[_nt], dev_linear_forward:
+//    _cuda_ops.pyx:1088-1190, :1278-1302)
+// with the bias add (_cuda_kernels.cu:1490-1527), activation and scale
+// (_cuda_kernels.cu:237-277, :384, :428) fused into the epilogue.
+//
+// CTA layout (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer: one lane streams A/B k-blocks into a STAGES-deep
+//               ring of 128B-swizzled shared-memory stages (no multicast).
+//   warp 1      TMEM owner + MMA issuer: one lane issues tcgen05.mma
+//               (M=128, N=BN, K=16 or 8 per instruction) into one of two
+//               TMEM accumulators, committing stage releases and
+//               accumulator-ready signals to mbarriers.
+//   warps 2-5   epilogue: drain the finished accumulator with tcgen05.ld
+//               (each warp owns its 32-lane TMEM quadrant = 32 tile rows),
+//               apply alpha/bias/activation/residual, convert, store.
+// Two TMEM accumulators let the epilogue of tile t overlap the MMAs of t+1.
+//
+// Operand forms: A is always K-major (rows of K contiguous).  B is K-major
+// (the nn.Linear weight layout [N, K]) or, for 16-bit inputs, MN-major
+// (row-major [K, N], e.g. V in P.V), selected by B_MN.
+//
+// Split-K (k_splits > 1): each work unit covers a slice of the k-blocks of
+// one tile and adds its fp32 partial tile into a zero-initialised fp32
+// workspace with red.global.add; a finaliser kernel applies the epilogue.
+//
+// Tile rasterisation: tiles are visited in groups of `group_m` M-blocks
+// sweeping all N-blocks, so concurrently running CTAs share A and B panels
+// in L2.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "epilogue.cuh"
+#include "ptx.cuh"
+
+namespace sf {
+
+struct GemmTcArgs {
+  int M, N, K;          // tile-orientation problem: A is M x K, B is N x K
+  int nb0, nb1;         // batch extents (inner, outer); batch z = b1 * nb0 + b0
+  int m_tiles, n_tiles, k_blocks;
+  int total_tiles;
+  int group_m;
+  int k_splits, kb_per_split;
+  // output, in OUTPUT orientation: element (row r, col c) of batch (b0, b1)
+  // lives at C[b0*c_stride0 + b1*c_stride1 + r*ldc + c]
+  void* C;
+  int out_dtype;
+  int64_t ldc, c_stride0, c_stride1;
+  int c_trans;          // 1: tile element (i, j) is output (row j, col i) (swap-AB)
+  int vec_ok;           // 16-byte vector stores legal for the non-transposed path
+  float* ws;            // split-K fp32 accumulation buffer (output orientation)
+  int64_t ldw;
+  EpilogueArgs epi;
+  int* err;             // device error word
+};
+
+template <int BN_, int STAGES_, int FMT_, bool B_MN_>
+struct TcCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int FMT = FMT_;                 // 0 f16, 1 bf16, 2 tf32
+  static constexpr bool B_MN = B_MN_;
+  static constexpr int ELEM = (FMT == 2) ? 4 : 2;
+  static constexpr int BK = 128 / ELEM;            // one 128-byte swizzle row of K
+  static constexpr int UMMA_K = 32 / ELEM;         // K per tcgen05.mma
+  static constexpr int KSTEPS = BK / UMMA_K;       // 4
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  static constexpr int ACC_COLS = BN;
+  static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
+                                   : (2 * BN <= 64)  ? 64
+                                   : (2 * BN <= 128) ? 128
+                                   : (2 * BN <= 256) ? 256
+                                                     : 512;
+  static constexpr int THREADS = 192;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(!B_MN || (BN % 64 == 0 && ELEM == 2), "MN-major B: 64-wide 16-bit slabs");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, const GemmTcArgs& p, int& mb, int& nb,
+                                            int& b0, int& b1) {
+  const int per_batch = p.m_tiles * p.n_tiles;
+  const int bz = tile / per_batch;
+  const int r = tile - bz * per_batch;
+  b0 = bz % p.nb0;
+  b1 = bz / p.nb0;
+  const int group = p.group_m * p.n_tiles;
+  const int g = r / group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.m_tiles - first_m, p.group_m);
+  const int rr = r - g * group;
+  mb = first_m + rr % gm;
+  nb = rr / gm;
+}
+
+// Store 16 consecutive tile columns [j0, j0+16) of tile row i.
+template <int OUT_VEC>
+__device__ __forceinline__ void epilogue_store16(const GemmTcArgs& p, int i, int j0, int b0,
+                                                 int b1, const uint32_t (&r)[16]) {
+  const EpilogueArgs& e = p.epi;
+  if (p.k_splits > 1) {
+    // Partial sums: raw accumulator into the fp32 workspace.
+    if (p.c_trans) {
+      if (i >= p.M) return;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int j = j0 + t;
+        if (j < p.N) atomicAdd(p.ws + (int64_t)j * p.ldw + i, __uint_as_float(r[t]));
+      }
+    } else {
+      if (i >= p.M) return;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int j = j0 + t;
+        if (j < p.N) atomicAdd(p.ws + (int64_t)i * p.ldw + j, __uint_as_float(r[t]));
+      }
+    }
+    return;
+  }
+  if (i >= p.M) return;
+  const int64_t coff = (int64_t)b0 * p.c_stride0 + (int64_t)b1 * p.c_stride1;
+  const int64_t roff = (int64_t)b0 * e.r_stride0 + (int64_t)b1 * e.r_stride1;
+  if (p.c_trans) {
+    // Output (row j, col i): bias by output column i.
+    const float bias_v = e.bias ? load_as_f32(e.bias, i, e.bias_dtype) : 0.0f;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int j = j0 + t;
+      if (j < p.N) {
+        const float res_v =
+            e.residual ? load_as_f32(e.residual, roff + (int64_t)j * e.ldr + i, e.residual_dtype)
+                       : 0.0f;
+        const float v = epilogue_value(__uint_as_float(r[t]), e, bias_v, res_v);
+        store_from_f32(p.C, coff + (int64_t)j * p.ldc + i, p.out_dtype, v);
+      }
+    }
+    return;
+  }
+  float v[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const int j = j0 + t;
+    const float bias_v = (e.bias && j < p.N) ? load_as_f32(e.bias, j, e.bias_dtype) : 0.0f;
+    const float res_v = (e.residual && j < p.N)
+                            ? load_as_f32(e.residual, roff + (int64_t)i * e.ldr + j,
+                                          e.residual_dtype)
+                            : 0.0f;
+    v[t] = epilogue_value(__uint_as_float(r[t]), e, bias_v, res_v);
+  }
+  const int64_t base = coff + (int64_t)i * p.ldc + j0;
+  if (p.vec_ok && j0 + 16 <= p.N) {
+    if (p.out_dtype == kF32) {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + base);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.C) + base);
+      const int dt = p.out_dtype;
+      dst[0] = make_uint4(pack2(v[0], v[1], dt), pack2(v[2], v[3], dt), pack2(v[4], v[5], dt),
+                          pack2(v[6], v[7], dt));
+      dst[1] = make_uint4(pack2(v[8], v[9], dt), pack2(v[10], v[11], dt),
+                          pack2(v[12], v[13], dt), pack2(v[14], v[15], dt));
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (j0 + t < p.N) store_from_f32(p.C, base + t, p.out_dtype, v[t]);
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmTcArgs p) {
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  volatile int* abortp = &abort_flag;
+
+  const int units = p.total_tiles * p.k_splits;
+
+  if (warp == 0) {
+    // ───────────── TMA producer ─────────────
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tile = u / p.k_splits, split = u - (u / p.k_splits) * p.k_splits;
+        int mb, nb, b0, b1;
+        tile_coords(tile, p, mb, nb, b0, b1);
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          tma_load_4d(sa, &tmA, &full_bar[stage], kb * BK, mb * BM, b0, b1);
+          if constexpr (!Cfg::B_MN) {
+            tma_load_4d(sb, &tmB, &full_bar[stage], kb * BK, nb * BN, b0, b1);
+          } else {
+#pragma unroll
+            for (int s = 0; s < BN / 64; ++s)
+              tma_load_4d(sb + s * 8192, &tmB, &full_bar[stage], nb * BN + s * 64, kb * BK, b0,
+                          b1);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Abort: wait (bounded) for the copies this thread still has in flight.
+        const int n = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int j = 0; j < n; ++j) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1u;
+          }
+          if (!mbar_wait_quiet(&full_bar[s], ph, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ───────────── MMA issuer ─────────────
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(Cfg::FMT == 2 ? 2u : (Cfg::FMT == 1 ? 1u : 0u), BM, BN, 0u,
+                                        Cfg::B_MN ? 1u : 0u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int split = u - (u / p.k_splits) * p.k_splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kDevTimeoutMma, abortp)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::ACC_COLS);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, kDevTimeoutMma, abortp)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
+            const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
+            const uint64_t bd = Cfg::B_MN ? make_sw128_desc(b_addr + ks * 2048, 8192, 1024)
+                                          : make_sw128_desc(b_addr + ks * 32, 16, 1024);
+            const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
+            if constexpr (Cfg::FMT == 2)
+              umma_tf32(d_tmem, ad, bd, idesc, accum);
+            else
+              umma_f16(d_tmem, ad, bd, idesc, accum);
+          }
+          issued_any = true;
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        // Abort: make sure no tcgen05.mma is still writing TMEM before dealloc.
+        umma_commit(&drain_bar);
+        if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      }
+    }
+  } else {
+    // ───────────── epilogue (warps 2..5) ─────────────
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int tile = u / p.k_splits;
+      int mb, nb, b0, b1;
+      tile_coords(tile, p, mb, nb, b0, b1);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) break;
+      tc_fence_after();
+      const int i = mb * BM + row;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::ACC_COLS);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c, r);
+        tmem_ld_wait();
+        const int j0 = nb * BN + c;
+        if (j0 < p.N) epilogue_store16<0>(p, i, j0, b0, b1, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace sf

@@ -1,0 +1,224 @@
+// Bandwidth-bound companions of the GEMMs: row softmax, elementwise
+// activation/scale, the split-K finaliser, the 3xTF32 operand splitter and
+// the K == 0 epilogue.
+#pragma once
+#include <cstdint>
+
+#include "epilogue.cuh"
+#include "ptx.cuh"
+
+namespace sf {
+
+// ─────────────────────────── row softmax ───────────────────────────────────
+// y[r, :] = softmax(scale * x[r, :]) in fp32: max-subtract, exp, sum, divide,
+// as nn/functional.py:131-136 and the device kernels of
+// _cuda_kernels.cu:473-640 (there fused with the separate dev_muls scale of
+// nn/functional.py:315).  One CTA per row; the row is held in registers
+// (VPT float4 per thread) so HBM sees exactly one read of x and one write
+// of y.  Rows longer than the register budget use the three-pass variant.
+
+constexpr int kSoftmaxThreads = 512;
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < (int)(blockDim.x >> 5)) ? red[l] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (l == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+__device__ __forceinline__ void store4(void* y, int64_t idx, int dtype, float a, float b, float c,
+                                       float d) {
+  if (dtype == kF32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + idx) = make_float4(a, b, c, d);
+  } else {
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(y) + idx) =
+        make_uint2(pack2(a, b, dtype), pack2(c, d, dtype));
+  }
+}
+
+// Vectorised register-resident softmax: requires cols % 4 == 0 and 16-byte
+// aligned fp32 rows (x), 8-byte aligned rows (16-bit y) or 16-byte (fp32 y).
+template <int VPT>
+__global__ void __launch_bounds__(kSoftmaxThreads)
+    softmax_rows_vec_kernel(const float* __restrict__ x, int64_t ldx, void* __restrict__ y,
+                            int y_dtype, int64_t ldy, int cols, float scale) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
+  const int nv = cols >> 2;
+  float4 v[VPT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int t = 0; t < VPT; ++t) {
+    const int c = threadIdx.x + t * kSoftmaxThreads;
+    if (c < nv) {
+      float4 q = __ldcs(xr + c);
+      q.x *= scale; q.y *= scale; q.z *= scale; q.w *= scale;
+      v[t] = q;
+      m = fmaxf(m, fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
+    }
+  }
+  m = block_reduce_max(m, red);
+  float s = 0.0f;
+#pragma unroll
+  for (int t = 0; t < VPT; ++t) {
+    const int c = threadIdx.x + t * kSoftmaxThreads;
+    if (c < nv) {
+      v[t].x = expf(v[t].x - m);
+      v[t].y = expf(v[t].y - m);
+      v[t].z = expf(v[t].z - m);
+      v[t].w = expf(v[t].w - m);
+      s += (v[t].x + v[t].y) + (v[t].z + v[t].w);
+    }
+  }
+  s = block_reduce_sum(s, red);
+#pragma unroll
+  for (int t = 0; t < VPT; ++t) {
+    const int c = threadIdx.x + t * kSoftmaxThreads;
+    if (c < nv)
+      store4(y, r * ldy + 4 * (int64_t)c, y_dtype, v[t].x / s, v[t].y / s, v[t].z / s,
+             v[t].w / s);
+  }
+}
+
+// General three-pass softmax (any cols, any alignment, any input dtype).
+__global__ void __launch_bounds__(kSoftmaxThreads)
+    softmax_rows_generic_kernel(const void* __restrict__ x, int x_dtype, int64_t ldx,
+                                void* __restrict__ y, int y_dtype, int64_t ldy, int cols,
+                                float scale) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    m = fmaxf(m, scale * load_as_f32(x, r * ldx + c, x_dtype));
+  m = block_reduce_max(m, red);
+  float s = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    s += expf(scale * load_as_f32(x, r * ldx + c, x_dtype) - m);
+  s = block_reduce_sum(s, red);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    store_from_f32(y, r * ldy + c, y_dtype, expf(scale * load_as_f32(x, r * ldx + c, x_dtype) - m) / s);
+}
+
+// ─────────────────────── elementwise activation ───────────────────────────
+// y = act(alpha * x)  (dev_silu / dev_gelu / dev_muls of _cuda_ops.pyx:944-998)
+__global__ void unary_act_kernel(const void* __restrict__ x, int x_dtype, void* __restrict__ y,
+                                 int y_dtype, int64_t n, float alpha, int act) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    store_from_f32(y, i, y_dtype, act_apply(alpha * load_as_f32(x, i, x_dtype), act));
+}
+
+// ─────────────────────────── split-K finaliser ─────────────────────────────
+// out[r, c] = epilogue(ws[r, c]) for the split-K / K == 0 paths (ws == null => 0).
+__global__ void epilogue_finalize_kernel(const float* __restrict__ ws, int64_t ldw, int rows,
+                                         int cols, void* __restrict__ out, int out_dtype,
+                                         int64_t ldc, EpilogueArgs e) {
+  const int64_t total = (int64_t)rows * cols;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / cols), c = (int)(t - (t / cols) * cols);
+    const float acc = ws ? ws[(int64_t)r * ldw + c] : 0.0f;
+    const float bias_v = e.bias ? load_as_f32(e.bias, c, e.bias_dtype) : 0.0f;
+    const float res_v =
+        e.residual ? load_as_f32(e.residual, (int64_t)r * e.ldr + c, e.residual_dtype) : 0.0f;
+    store_from_f32(out, (int64_t)r * ldc + c, out_dtype, epilogue_value(acc, e, bias_v, res_v));
+  }
+}
+
+// ─────────────────────────── 3xTF32 splitter ───────────────────────────────
+// For an fp32 operand X (rows x K, element (r,k) at X[r*rs + k*ks]) write a
+// dense K-major panel with leading dimension ld_out:
+//   pattern 0: [X_hi | X_lo | X_hi]     pattern 1: [X_hi | X_hi | X_lo]
+//   pattern 2: [X]  (plain repack, single-pass TF32)
+// X_hi = tf32(X), X_lo = tf32(X - X_hi).  A'.B'^T over the 3K-long reduction
+// of (pattern 0, pattern 1) panels equals A_hi.B_hi + A_lo.B_hi + A_hi.B_lo,
+// the 3xTF32 product; the dropped A_lo.B_lo term is ~2^-22 relative.
+// Reading X through (rs, ks) lets the same pass transpose an MN-major operand
+// into K-major form.
+__device__ __forceinline__ float to_tf32(float f) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(f));
+  return __uint_as_float(r);
+}
+
+__global__ void tf32_split_kernel(const float* __restrict__ X, int64_t rs, int64_t ks, int rows,
+                                  int K, float* __restrict__ out, int64_t ld_out, int pattern) {
+  const int64_t total = (int64_t)rows * K;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / K), k = (int)(t - (t / K) * K);
+    const float v = X[(int64_t)r * rs + (int64_t)k * ks];
+    float* o = out + (int64_t)r * ld_out;
+    if (pattern == 2) {
+      o[k] = v;
+      continue;
+    }
+    const float hi = to_tf32(v);
+    const float lo = to_tf32(v - hi);
+    o[k] = hi;
+    o[K + k] = pattern == 0 ? lo : hi;
+    o[2 * K + k] = pattern == 0 ? hi : lo;
+  }
+}
+
+// Dense K-major copy of a strided 16-bit operand (used when a layout cannot
+// be described to TMA directly).
+__global__ void repack_k_major_kernel(const uint16_t* __restrict__ X, int64_t rs, int64_t ks,
+                                      int rows, int K, uint16_t* __restrict__ out, int64_t ld_out) {
+  const int64_t total = (int64_t)rows * K;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / K), k = (int)(t - (t / K) * K);
+    out[(int64_t)r * ld_out + k] = X[(int64_t)r * rs + (int64_t)k * ks];
+  }
+}
+
+}  // namespace sf
+
+namespace sf {
+// Waits on an mbarrier nothing ever arrives on, with a short limit: proves
+// that an expired wait records its code and returns instead of hanging.
+__global__ void bounded_wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    volatile int* ab = &abort_flag;
+    mbar_wait(&bar, 0, err, kDevTimeoutSelftest, ab, limit_ns);
+  }
+  __syncthreads();
+}
+}  // namespace sf
