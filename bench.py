@@ -501,6 +501,7 @@ def run_gpu_arm(args, dist):
                          "peak_source": f"{src} ({'sustained' if peak == sustained else 'burst'} bf16)",
                          "kernel": "sf::gemm_tc_kernel (tcgen05)",
                          "launch_ms_mean": gemm_ms / max(1, n_launch)},
+            "kernel_ms": {k: sum(v) / len(v) for k, v in kern_ms.items()},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,

@@ -276,7 +276,7 @@ def dev_linear_forward(gt_x: GpuTensor, gt_weight: GpuTensor, gt_bias: GpuTensor
     ``nn/functional.py:37-40``)."""
     _check_pair(gt_x, gt_weight)
     K = gt_x.shape[-1]
-    M = gt_x.numel // K if K else 0
+    M = int(np.prod(gt_x.shape[:-1], dtype=np.int64))
     N, Kw = gt_weight.shape
     if Kw != K:
         raise ValueError(f"linear shape mismatch: x {gt_x.shape}, W {gt_weight.shape}")

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.h"
@@ -123,6 +124,7 @@ struct Plan {
   int bn = 128;
   bool b_mn = false;
   int splits = 1;
+  bool promote = false; // fp32-accurate: chunked TMEM accumulation promoted to registers
   int64_t kk = 0;       // reduction length seen by the TC kernel (3K for 3xTF32)
   int64_t ld_split = 0; // leading dimension of the split panels
   size_t ws_bytes = 0;
@@ -137,7 +139,15 @@ static int pick_bn(int64_t n) {
   if (n <= 32) return 32;
   if (n <= 64) return 64;
   if (n <= 128) return 128;
-  return 256;
+  // 192 or 256: whichever pads the last N tile less (ties: the larger tile).
+  const int64_t w256 = ceil_div(n, 256) * 256 - n;
+  const int64_t w192 = ceil_div(n, 192) * 192 - n;
+  return w192 < w256 ? 192 : 256;
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
 }
 
 // `have_ptrs` = false when only sizing the workspace (pointers unknown, assumed aligned).
@@ -162,10 +172,11 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
       pl.kk = p.K;
     } else {
       pl.kk = 3 * p.K;
+      pl.promote = true;
     }
     pl.kind = kPlanTf32Split;
     pl.ld_split = (pl.kk + 3) & ~int64_t(3);
-    pl.bn = pick_bn(p.N);
+    pl.bn = pl.promote ? (p.N <= 64 ? 64 : 128) : pick_bn(p.N);
     pl.ws_bytes = static_cast<size_t>(batch) * static_cast<size_t>(p.M + p.N) *
                   static_cast<size_t>(pl.ld_split) * 4u;
     return pl;
@@ -180,7 +191,7 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   if (p.tb == 0) {
     pl.kind = kPlanTc;
     pl.b_mn = true;
-    pl.bn = p.N <= 64 ? 64 : (p.N <= 128 ? 128 : 256);
+    pl.bn = p.N <= 64 ? 64 : (p.N <= 128 ? 128 : (pick_bn(p.N) == 192 ? 192 : 256));
     return pl;
   }
   if (batch == 1 && p.M <= 256 && p.N >= 256) {
@@ -200,15 +211,27 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     return pl;
   }
   pl.kind = kPlanTc;
-  pl.bn = p.N > 128 ? 256 : pick_bn(p.N);
+  pl.bn = pick_bn(p.N);
   if (pl.bn < 64 && p.M > 4096) pl.bn = 64;
+  const int forced = env_int("SF_TILE_N", 0);  // tuning knob
+  if (forced == 64 || forced == 128 || forced == 192 || forced == 256) pl.bn = forced;
   return pl;
 }
 
-static EpilogueArgs to_epi(const sf_epilogue& e) {
+static EpilogueArgs to_epi(const sf_epilogue& e, int out_dt) {
   EpilogueArgs a;
   a.alpha = e.alpha;
   a.beta = e.beta;
+  a.fast_act = out_dt != kF32 ? 1 : 0;
+  a.bias_vec = (e.bias && (reinterpret_cast<uintptr_t>(e.bias) & 15u) == 0) ? 1 : 0;
+  {
+    const int res = e.residual_dtype == kF32 ? 4 : 2;
+    a.res_vec = (e.residual && (reinterpret_cast<uintptr_t>(e.residual) & 15u) == 0 &&
+                 ((e.ldr * res) & 15) == 0 && ((e.r_stride0 * res) & 15) == 0 &&
+                 ((e.r_stride1 * res) & 15) == 0)
+                    ? 1
+                    : 0;
+  }
   a.bias = e.bias;
   a.bias_dtype = e.bias_dtype;
   a.bias_on_rows = 0;
@@ -238,13 +261,20 @@ static int32_t launch_tc_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const
 }
 
 // Stage counts per N tile: keep ~192-216 KB of operand ring per CTA.
-template <int FMT, bool BMN>
+template <int FMT, bool BMN, int PKB>
 static int32_t launch_tc(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a,
                          int grid, cudaStream_t s, int device) {
-  if constexpr (BMN) {
+  if constexpr (PKB > 0) {
+    switch (bn) {
+      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, false, PKB>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, false, PKB>>(ma, mb, a, grid, s, device);
+      default: return fail(SF_ERR_UNSUPPORTED, "promoted tile width %d", bn);
+    }
+  } else if constexpr (BMN) {
     switch (bn) {
       case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, true>>(ma, mb, a, grid, s, device);
       case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, true>>(ma, mb, a, grid, s, device);
+      case 192: return launch_tc_cfg<TcCfg<192, 5, FMT, true>>(ma, mb, a, grid, s, device);
       case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, true>>(ma, mb, a, grid, s, device);
       default: return fail(SF_ERR_UNSUPPORTED, "MN-major B tile width %d", bn);
     }
@@ -254,24 +284,27 @@ static int32_t launch_tc(int bn, const CUtensorMap& ma, const CUtensorMap& mb, c
       case 32: return launch_tc_cfg<TcCfg<32, 10, FMT, false>>(ma, mb, a, grid, s, device);
       case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, false>>(ma, mb, a, grid, s, device);
       case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, false>>(ma, mb, a, grid, s, device);
+      case 192: return launch_tc_cfg<TcCfg<192, 5, FMT, false>>(ma, mb, a, grid, s, device);
       case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, false>>(ma, mb, a, grid, s, device);
       default: return fail(SF_ERR_UNSUPPORTED, "tile width %d", bn);
     }
   }
 }
 
-static int32_t dispatch_tc(int fmt, bool bmn, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
-                           const GemmTcArgs& a, int grid, cudaStream_t s, int device) {
+static int32_t dispatch_tc(int fmt, bool bmn, bool promote, int bn, const CUtensorMap& ma,
+                           const CUtensorMap& mb, const GemmTcArgs& a, int grid, cudaStream_t s,
+                           int device) {
   if (fmt == kBF16) {
-    return bmn ? launch_tc<1, true>(bn, ma, mb, a, grid, s, device)
-               : launch_tc<1, false>(bn, ma, mb, a, grid, s, device);
+    return bmn ? launch_tc<1, true, 0>(bn, ma, mb, a, grid, s, device)
+               : launch_tc<1, false, 0>(bn, ma, mb, a, grid, s, device);
   }
   if (fmt == kF16) {
-    return bmn ? launch_tc<0, true>(bn, ma, mb, a, grid, s, device)
-               : launch_tc<0, false>(bn, ma, mb, a, grid, s, device);
+    return bmn ? launch_tc<0, true, 0>(bn, ma, mb, a, grid, s, device)
+               : launch_tc<0, false, 0>(bn, ma, mb, a, grid, s, device);
   }
   if (bmn) return fail(SF_ERR_UNSUPPORTED, "MN-major TF32 operand");
-  return launch_tc<2, false>(bn, ma, mb, a, grid, s, device);
+  return promote ? launch_tc<2, false, 4>(bn, ma, mb, a, grid, s, device)
+                 : launch_tc<2, false, 0>(bn, ma, mb, a, grid, s, device);
 }
 
 static int grid_for(int64_t n, int sm_count) {
@@ -302,7 +335,7 @@ static int32_t run_simt(const Problem& p) {
   a.ldc = p.ldc;
   a.c_s0 = p.cs0;
   a.c_s1 = p.cs1;
-  a.epi = to_epi(p.epi);
+  a.epi = to_epi(p.epi, p.out_dt);
   const int64_t batch = p.nb0 * p.nb1;
   if (batch > 65535) return fail(SF_ERR_UNSUPPORTED, "SIMT GEMM batch %lld > 65535", (long long)batch);
   dim3 grid(static_cast<unsigned>(ceil_div(p.N, kSimtBN)), static_cast<unsigned>(ceil_div(p.M, kSimtBM)),
@@ -391,7 +424,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   const int64_t total = int64_t(a.m_tiles) * a.n_tiles * p.nb0 * p.nb1;
   if (total * pl.splits > INT32_MAX) return fail(SF_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
-  a.group_m = 8;
+  a.group_m = std::max(1, env_int("SF_GROUP_M", 8));  // raster group height (tuning knob)
   a.k_splits = pl.splits;
   a.kb_per_split = static_cast<int>(ceil_div(a.k_blocks, pl.splits));
   a.C = p.C;
@@ -407,7 +440,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
                  : 0;
   a.ws = nullptr;
   a.ldw = 0;
-  a.epi = to_epi(p.epi);
+  a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
   if (pl.splits > 1) {
     a.ws = static_cast<float*>(p.ws);
@@ -416,12 +449,12 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   }
   const int64_t units = total * pl.splits;
   const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
-  st = dispatch_tc(fmt, pl.b_mn, pl.bn, ma, mbm, a, grid, p.stream, device);
+  st = dispatch_tc(fmt, pl.b_mn, pl.promote, pl.bn, ma, mbm, a, grid, p.stream, device);
   if (st != SF_OK) return st;
   if (pl.splits > 1) {
     epilogue_finalize_kernel<<<grid_for(p.M * p.N, dev.sm_count), 256, 0, p.stream>>>(
         static_cast<const float*>(p.ws), p.N, static_cast<int>(p.M), static_cast<int>(p.N), p.C,
-        p.out_dt, p.ldc, to_epi(p.epi));
+        p.out_dt, p.ldc, to_epi(p.epi, p.out_dt));
     SF_CUDA_TRY(cudaGetLastError());
   }
   return SF_OK;
@@ -465,7 +498,7 @@ static int32_t gemm_impl(Problem& p) {
     // Empty reduction: D = epilogue(0) per batch.
     for (int64_t b1 = 0; b1 < p.nb1; ++b1)
       for (int64_t b0 = 0; b0 < p.nb0; ++b0) {
-        EpilogueArgs e = to_epi(p.epi);
+        EpilogueArgs e = to_epi(p.epi, p.out_dt);
         if (e.residual) {
           const int res_es = esize(e.residual_dtype);
           e.residual = static_cast<const char*>(e.residual) + (b0 * e.r_stride0 + b1 * e.r_stride1) * res_es;

@@ -30,6 +30,19 @@ __device__ __forceinline__ float act_apply(float z, int act) {
   return z;
 }
 
+// Fast forms for 16-bit outputs, where the result is rounded to 8 (bf16) or
+// 11 (fp16) significant bits anyway.  GELU-tanh uses the identity
+// 0.5 * (1 + tanh(u)) = 1 / (1 + exp(-2u)); both use the hardware exp2
+// intrinsic and a fast divide.
+__device__ __forceinline__ float act_apply_fast(float z, int act) {
+  if (act == kActSilu) return __fdividef(z, 1.0f + __expf(-z));
+  if (act == kActGeluTanh) {
+    const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
+    return __fdividef(z, 1.0f + __expf(-2.0f * u));
+  }
+  return z;
+}
+
 __device__ __forceinline__ float load_as_f32(const void* p, int64_t i, int dtype) {
   if (dtype == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
   if (dtype == kF16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
@@ -58,6 +71,9 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int dtype) {
 struct EpilogueArgs {
   float alpha;
   float beta;
+  int fast_act;          // 1: act_apply_fast (16-bit outputs)
+  int bias_vec;          // 1: bias rows may be read with 16-byte vector loads
+  int res_vec;           // 1: residual rows may be read with 16-byte vector loads
   const void* bias;      // indexed by output column (or by output row if bias_on_rows)
   int bias_dtype;
   int bias_on_rows;
@@ -71,7 +87,7 @@ struct EpilogueArgs {
 __device__ __forceinline__ float epilogue_value(float acc, const EpilogueArgs& e, float bias_v,
                                                 float res_v) {
   float v = e.alpha * acc + bias_v;
-  v = act_apply(v, e.act);
+  v = e.fast_act ? act_apply_fast(v, e.act) : act_apply(v, e.act);
   if (e.residual != nullptr) v += e.beta * res_v;
   return v;
 }

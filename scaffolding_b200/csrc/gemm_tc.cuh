@@ -9,17 +9,27 @@
 // with the bias add (_cuda_kernels.cu:1490-1527), activation and scale
 // (_cuda_kernels.cu:237-277, :384, :428) fused into the epilogue.
 //
-// CTA layout (192 threads, one CTA per SM, persistent over tiles):
+// CTA layout (320 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: one lane streams A/B k-blocks into a STAGES-deep
 //               ring of 128B-swizzled shared-memory stages (no multicast).
 //   warp 1      TMEM owner + MMA issuer: one lane issues tcgen05.mma
 //               (M=128, N=BN, K=16 or 8 per instruction) into one of two
 //               TMEM accumulators, committing stage releases and
 //               accumulator-ready signals to mbarriers.
-//   warps 2-5   epilogue: drain the finished accumulator with tcgen05.ld
-//               (each warp owns its 32-lane TMEM quadrant = 32 tile rows),
-//               apply alpha/bias/activation/residual, convert, store.
+//   warps 2-9   epilogue: two warps per 32-lane TMEM quadrant (a warp may
+//               only touch the quadrant warp_id % 4); the pair splits the
+//               tile's columns in interleaved 32-column chunks, loads them
+//               with tcgen05.ld, applies alpha/bias/activation/residual,
+//               converts and stores.
 // Two TMEM accumulators let the epilogue of tile t overlap the MMAs of t+1.
+//
+// PROMOTE mode (fp32-accurate 3xTF32): the MMA accumulates at most
+// PROMOTE_KB k-blocks into a TMEM accumulator, then hands it to the
+// epilogue warps, which add it into fp32 registers with IEEE adds and
+// release it.  The tensor core's own accumulation is not IEEE
+// round-to-nearest, so long K reductions held entirely in TMEM drift by
+// ~1e-5 relative; short TMEM chunks + register accumulation keep fp32
+// accuracy.
 //
 // Operand forms: A is always K-major (rows of K contiguous).  B is K-major
 // (the nn.Linear weight layout [N, K]) or, for 16-bit inputs, MN-major
@@ -62,13 +72,14 @@ struct GemmTcArgs {
   int* err;             // device error word
 };
 
-template <int BN_, int STAGES_, int FMT_, bool B_MN_>
+template <int BN_, int STAGES_, int FMT_, bool B_MN_, int PROMOTE_KB_ = 0>
 struct TcCfg {
   static constexpr int BM = 128;
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
   static constexpr int FMT = FMT_;                 // 0 f16, 1 bf16, 2 tf32
   static constexpr bool B_MN = B_MN_;
+  static constexpr int PROMOTE_KB = PROMOTE_KB_;   // 0: accumulate the whole K in TMEM
   static constexpr int ELEM = (FMT == 2) ? 4 : 2;
   static constexpr int BK = 128 / ELEM;            // one 128-byte swizzle row of K
   static constexpr int UMMA_K = 32 / ELEM;         // K per tcgen05.mma
@@ -83,9 +94,15 @@ struct TcCfg {
                                    : (2 * BN <= 128) ? 128
                                    : (2 * BN <= 256) ? 256
                                                      : 512;
-  static constexpr int THREADS = 192;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = 64 + EPI_THREADS;
+  static constexpr int CH = BN < 32 ? BN : 32;      // epilogue column chunk
+  // columns owned per epilogue thread (PROMOTE register accumulator)
+  static constexpr int OWN = (BN + 2 * CH - 1) / (2 * CH) * CH;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
   static_assert(!B_MN || (BN % 64 == 0 && ELEM == 2), "MN-major B: 64-wide 16-bit slabs");
+  static_assert(PROMOTE_KB == 0 || BN % (2 * CH) == 0, "promotion needs an even chunk split");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -105,80 +122,145 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmTcArgs& p, int& 
   nb = rr / gm;
 }
 
-// Store 16 consecutive tile columns [j0, j0+16) of tile row i.
-template <int OUT_VEC>
-__device__ __forceinline__ void epilogue_store16(const GemmTcArgs& p, int i, int j0, int b0,
-                                                 int b1, const uint32_t (&r)[16]) {
-  const EpilogueArgs& e = p.epi;
-  if (p.k_splits > 1) {
-    // Partial sums: raw accumulator into the fp32 workspace.
-    if (p.c_trans) {
-      if (i >= p.M) return;
+// Load CH consecutive values of a 16-bit or fp32 row into floats (vectorised
+// when `vec`; scalar otherwise).  Only called for chunks fully inside the row.
+template <int CH>
+__device__ __forceinline__ void load_row_chunk(const void* base, int64_t idx, int dtype, bool vec,
+                                               float* out) {
+  if (vec) {
+    if (dtype == kF32) {
+      const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int j = j0 + t;
-        if (j < p.N) atomicAdd(p.ws + (int64_t)j * p.ldw + i, __uint_as_float(r[t]));
+      for (int q = 0; q < CH / 4; ++q) {
+        const float4 f = s[q];
+        out[4 * q] = f.x; out[4 * q + 1] = f.y; out[4 * q + 2] = f.z; out[4 * q + 3] = f.w;
       }
     } else {
-      if (i >= p.M) return;
+      const uint4* s = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + idx);
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int j = j0 + t;
-        if (j < p.N) atomicAdd(p.ws + (int64_t)i * p.ldw + j, __uint_as_float(r[t]));
+      for (int q = 0; q < CH / 8; ++q) {
+        const uint4 u = s[q];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          if (dtype == kBF16) {
+            out[8 * q + 2 * h] = __uint_as_float(w[h] << 16);
+            out[8 * q + 2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
+          } else {
+            const __half2 hv = *reinterpret_cast<const __half2*>(&w[h]);
+            const float2 f = __half22float2(hv);
+            out[8 * q + 2 * h] = f.x;
+            out[8 * q + 2 * h + 1] = f.y;
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < CH; ++t) out[t] = load_as_f32(base, idx + t, dtype);
+  }
+}
+
+// Apply the epilogue to CH consecutive tile columns [j0, j0+CH) of tile row i
+// and store them.
+template <int CH>
+__device__ __forceinline__ void epilogue_store(const GemmTcArgs& p, int i, int j0, int b0, int b1,
+                                               const float* acc) {
+  const EpilogueArgs& e = p.epi;
+  if (i >= p.M) return;
+  if (p.k_splits > 1) {
+    // Partial sums: raw accumulator into the fp32 workspace.
+#pragma unroll
+    for (int t = 0; t < CH; ++t) {
+      const int j = j0 + t;
+      if (j < p.N) {
+        float* dst = p.c_trans ? p.ws + (int64_t)j * p.ldw + i : p.ws + (int64_t)i * p.ldw + j;
+        atomicAdd(dst, acc[t]);
       }
     }
     return;
   }
-  if (i >= p.M) return;
   const int64_t coff = (int64_t)b0 * p.c_stride0 + (int64_t)b1 * p.c_stride1;
   const int64_t roff = (int64_t)b0 * e.r_stride0 + (int64_t)b1 * e.r_stride1;
   if (p.c_trans) {
-    // Output (row j, col i): bias by output column i.
+    // Output (row j, col i): bias by output column i; lanes hold consecutive i,
+    // so every store instruction is coalesced across the warp.
     const float bias_v = e.bias ? load_as_f32(e.bias, i, e.bias_dtype) : 0.0f;
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
+    for (int t = 0; t < CH; ++t) {
       const int j = j0 + t;
       if (j < p.N) {
         const float res_v =
             e.residual ? load_as_f32(e.residual, roff + (int64_t)j * e.ldr + i, e.residual_dtype)
                        : 0.0f;
-        const float v = epilogue_value(__uint_as_float(r[t]), e, bias_v, res_v);
-        store_from_f32(p.C, coff + (int64_t)j * p.ldc + i, p.out_dtype, v);
+        store_from_f32(p.C, coff + (int64_t)j * p.ldc + i, p.out_dtype,
+                       epilogue_value(acc[t], e, bias_v, res_v));
       }
     }
     return;
   }
-  float v[16];
+  const bool full = j0 + CH <= p.N;
+  float bias_v[CH], res_v[CH], v[CH];
+  if (e.bias) {
+    if (full) {
+      load_row_chunk<CH>(e.bias, j0, e.bias_dtype, e.bias_vec != 0, bias_v);
+    } else {
 #pragma unroll
-  for (int t = 0; t < 16; ++t) {
-    const int j = j0 + t;
-    const float bias_v = (e.bias && j < p.N) ? load_as_f32(e.bias, j, e.bias_dtype) : 0.0f;
-    const float res_v = (e.residual && j < p.N)
-                            ? load_as_f32(e.residual, roff + (int64_t)i * e.ldr + j,
-                                          e.residual_dtype)
-                            : 0.0f;
-    v[t] = epilogue_value(__uint_as_float(r[t]), e, bias_v, res_v);
+      for (int t = 0; t < CH; ++t) bias_v[t] = (j0 + t < p.N) ? load_as_f32(e.bias, j0 + t, e.bias_dtype) : 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < CH; ++t) bias_v[t] = 0.0f;
   }
+  if (e.residual) {
+    const int64_t ridx = roff + (int64_t)i * e.ldr + j0;
+    if (full) {
+      load_row_chunk<CH>(e.residual, ridx, e.residual_dtype, e.res_vec != 0, res_v);
+    } else {
+#pragma unroll
+      for (int t = 0; t < CH; ++t)
+        res_v[t] = (j0 + t < p.N) ? load_as_f32(e.residual, ridx + t, e.residual_dtype) : 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < CH; ++t) res_v[t] = 0.0f;
+  }
+#pragma unroll
+  for (int t = 0; t < CH; ++t) v[t] = epilogue_value(acc[t], e, bias_v[t], res_v[t]);
   const int64_t base = coff + (int64_t)i * p.ldc + j0;
-  if (p.vec_ok && j0 + 16 <= p.N) {
+  if (p.vec_ok && full) {
     if (p.out_dtype == kF32) {
       float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + base);
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int q = 0; q < CH / 4; ++q)
         dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     } else {
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.C) + base);
       const int dt = p.out_dtype;
-      dst[0] = make_uint4(pack2(v[0], v[1], dt), pack2(v[2], v[3], dt), pack2(v[4], v[5], dt),
-                          pack2(v[6], v[7], dt));
-      dst[1] = make_uint4(pack2(v[8], v[9], dt), pack2(v[10], v[11], dt),
-                          pack2(v[12], v[13], dt), pack2(v[14], v[15], dt));
+#pragma unroll
+      for (int q = 0; q < CH / 8; ++q)
+        dst[q] = make_uint4(pack2(v[8 * q], v[8 * q + 1], dt), pack2(v[8 * q + 2], v[8 * q + 3], dt),
+                            pack2(v[8 * q + 4], v[8 * q + 5], dt), pack2(v[8 * q + 6], v[8 * q + 7], dt));
     }
   } else {
 #pragma unroll
-    for (int t = 0; t < 16; ++t)
+    for (int t = 0; t < CH; ++t)
       if (j0 + t < p.N) store_from_f32(p.C, base + t, p.out_dtype, v[t]);
   }
+}
+
+template <int CH>
+__device__ __forceinline__ void tmem_load_chunk(uint32_t taddr, float* out) {
+  uint32_t r[CH];
+  if constexpr (CH == 32) {
+    tmem_ld32(taddr, r);
+  } else {
+    uint32_t (&r16)[16] = *reinterpret_cast<uint32_t(*)[16]>(r);
+    tmem_ld16(taddr, r16);
+  }
+  tmem_ld_wait();
+#pragma unroll
+  for (int t = 0; t < CH; ++t) out[t] = __uint_as_float(r[t]);
 }
 
 template <class Cfg>
@@ -186,6 +268,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmTcArgs p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  constexpr int CH = Cfg::CH;
+  constexpr int PKB = Cfg::PROMOTE_KB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -208,7 +292,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], Cfg::EPI_THREADS);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -296,43 +380,47 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         const int split = u - (u / p.k_splits) * p.k_splits;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kDevTimeoutMma, abortp)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::ACC_COLS);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, kDevTimeoutMma, abortp)) {
+        const int chunk = PKB > 0 ? PKB : max(kb1 - kb0, 1);
+        for (int kc = kb0; kc < kb1 && ok; kc += chunk) {
+          const int kce = min(kb1, kc + chunk);
+          if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kDevTimeoutMma, abortp)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::ACC_COLS);
+          for (int kb = kc; kb < kce; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase, p.err, kDevTimeoutMma, abortp)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+            const uint32_t b_addr = a_addr + Cfg::A_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
-            const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
-            const uint64_t bd = Cfg::B_MN ? make_sw128_desc(b_addr + ks * 2048, 8192, 1024)
-                                          : make_sw128_desc(b_addr + ks * 32, 16, 1024);
-            const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
-            if constexpr (Cfg::FMT == 2)
-              umma_tf32(d_tmem, ad, bd, idesc, accum);
-            else
-              umma_f16(d_tmem, ad, bd, idesc, accum);
+            for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
+              const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
+              const uint64_t bd = Cfg::B_MN ? make_sw128_desc(b_addr + ks * 2048, 8192, 1024)
+                                            : make_sw128_desc(b_addr + ks * 32, 16, 1024);
+              const uint32_t accum = (kb > kc || ks > 0) ? 1u : 0u;
+              if constexpr (Cfg::FMT == 2)
+                umma_tf32(d_tmem, ad, bd, idesc, accum);
+              else
+                umma_f16(d_tmem, ad, bd, idesc, accum);
+            }
+            issued_any = true;
+            umma_commit(&empty_bar[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          issued_any = true;
-          umma_commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          if (!ok) break;
+          umma_commit(&tfull_bar[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
           }
-        }
-        if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
         }
       }
       if (!ok && issued_any) {
@@ -342,33 +430,73 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       }
     }
   } else {
-    // ───────────── epilogue (warps 2..5) ─────────────
+    // ───────────── epilogue (warps 2..9) ─────────────
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const int tile = u / p.k_splits;
       int mb, nb, b0, b1;
       tile_coords(tile, p, mb, nb, b0, b1);
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) break;
-      tc_fence_after();
       const int i = mb * BM + row;
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * Cfg::ACC_COLS);
+      if constexpr (PKB == 0) {
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) break;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                               static_cast<uint32_t>(acc * Cfg::ACC_COLS);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c, r);
-        tmem_ld_wait();
-        const int j0 = nb * BN + c;
-        if (j0 < p.N) epilogue_store16<0>(p, i, j0, b0, b1, r);
-      }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
+        for (int c = half * CH; c < BN; c += 2 * CH) {
+          float v[CH];
+          tmem_load_chunk<CH>(tbase + c, v);
+          const int j0 = nb * BN + c;
+          if (j0 < p.N) epilogue_store<CH>(p, i, j0, b0, b1, v);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      } else {
+        // Promotion: sum TMEM chunks of <= PKB k-blocks into fp32 registers.
+        constexpr int OWN = Cfg::OWN;
+        float racc[OWN];
+#pragma unroll
+        for (int t = 0; t < OWN; ++t) racc[t] = 0.0f;
+        const int split = u - tile * p.k_splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+        for (int kc = kb0; kc < kb1; kc += PKB) {
+          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                 static_cast<uint32_t>(acc * Cfg::ACC_COLS);
+#pragma unroll
+          for (int q = 0; q < OWN / CH; ++q) {
+            float v[CH];
+            tmem_load_chunk<CH>(tbase + half * CH + q * 2 * CH, v);
+#pragma unroll
+            for (int t = 0; t < CH; ++t) racc[q * CH + t] += v[t];
+          }
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int q = 0; q < OWN / CH; ++q) {
+          const int j0 = nb * BN + half * CH + q * 2 * CH;
+          if (j0 < p.N) epilogue_store<CH>(p, i, j0, b0, b1, &racc[q * CH]);
+        }
       }
     }
   }

@@ -41,12 +41,26 @@ def test_sdpa_fp32_golden(gpu, ops, golden):
     assert_close_fp32(o, golden["sdpa_o"], "sdpa fp32")
 
 
+def _sdpa_p_rounded(q, k, v, scale):
+    """Oracle SDPA with the probabilities rounded to bf16, the storage type
+    the device keeps P in before the P.V product (its bf16 operand)."""
+    s = O.batched_matmul_nt(q, k) * np.float32(scale)
+    p = O.round_bf16(O.softmax_rows(s))
+    return O.batched_matmul(p, v)
+
+
 def test_sdpa_bf16_golden(gpu, ops, golden):
+    """bf16 SDPA.  Per-element bar (1e-2) against the oracle on identically
+    rounded GEMM operands (Q, K, V and the stored bf16 P); against the
+    reference's fp32-P output the bf16 rounding of P is visible on outputs
+    that cancel to ~0, so that comparison uses the aggregate bar."""
     from scaffolding_b200.nn import functional as F
     bf = np_dtype("bf16")
-    q, k, v = (ops.gputensor_from_numpy(golden[f"sdpa8_{s}"].astype(bf)) for s in "qkv")
+    qh, kh, vh = (golden[f"sdpa8_{s}"] for s in "qkv")
+    q, k, v = (ops.gputensor_from_numpy(t.astype(bf)) for t in (qh, kh, vh))
     o = to_host32(ops, F.scaled_dot_product_attention(q, k, v, scale=0.125))
-    assert_close_16bit(o, golden["sdpa8_o"], "sdpa bf16")
+    assert_close_16bit(o, _sdpa_p_rounded(qh, kh, vh, 0.125), "sdpa bf16 vs P-rounded oracle")
+    assert O.rel_frobenius(o, golden["sdpa8_o"]) < 1e-2
 
 
 def test_dev_muls_silu_gelu(gpu, ops, golden):
@@ -54,6 +68,8 @@ def test_dev_muls_silu_gelu(gpu, ops, golden):
     gz = ops.gputensor_from_numpy(z)
     np.testing.assert_allclose(ops.gputensor_to_numpy(ops.dev_silu(gz)), golden["act_silu"],
                                rtol=2e-6, atol=1e-7)
+    # 1 + tanh(u) cancels for u << 0: the reference's own formula carries an
+    # absolute error of ~|z| * eps(fp32) there, hence the absolute floor.
     np.testing.assert_allclose(ops.gputensor_to_numpy(ops.dev_gelu(gz)), golden["act_gelu"],
-                               rtol=2e-6, atol=1e-7)
+                               rtol=2e-6, atol=1e-6)
     np.testing.assert_array_equal(ops.gputensor_to_numpy(ops.dev_muls(gz, 0.125)), z * np.float32(0.125))
