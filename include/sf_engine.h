@@ -139,6 +139,20 @@ int32_t sf_gemm_workspace_size(const sf_batch* batch, int64_t M, int64_t N, int6
                                int32_t trans_a, int32_t trans_b,
                                int32_t in_dtype, int32_t out_dtype, size_t* bytes);
 
+/* y[M,N] = act(x[M,K] . W[N,K]^T + bias) for M <= 256 with bf16/fp16 x and W,
+ * WITHOUT allocating: for callers that own all device memory themselves or
+ * must not call cudaMalloc, and so cannot pass sf_gemm a workspace.  The
+ * split-K partial sums live in a 4 MiB array compiled into the library
+ * (M * N <= 1048576, larger sizes are rejected); calls on one device share
+ * it, so calls that overlap on the GPU race.  The first call on a device
+ * looks the array up (make it before any stream capture).  No counterpart
+ * in the reference. */
+int32_t sf_linear_skinny_noalloc(int64_t M, int64_t N, int64_t K,
+                                 const void* x, int64_t ldx, const void* W, int64_t ldw,
+                                 const void* bias, int32_t bias_dtype,
+                                 void* y, int64_t ldy, int32_t in_dtype, int32_t out_dtype,
+                                 int32_t activation, void* stream);
+
 /* fp32 arithmetic mode (per process).  Replaces cuda_set_tf32
  * (_cuda_ops_decl.h:153, _cuda_kernels.cu:1928-1936). */
 int32_t sf_set_fp32_mode(int32_t mode);

@@ -8,11 +8,20 @@ multi-GPU path that replaces ``nn/parallel.py``'s host round-trips.
 Modules:
   _cuda_ops   the reference ``_cuda_ops`` surface (GpuTensor, dev_*, cuda_*, runtime)
   nn          Linear / functional.linear / scaled_dot_product_attention on GpuTensors
-  parallel    token (M) sharding over one process per GPU + NCCL all-gather
-  dit         DiT block linears and the 30-layer DiT stack used by the benchmark
+  dit         DiT block linears used by the benchmark
   engine      thin wrappers over the C ABI (include/sf_engine.h)
-"""
-from . import _cuda_ops  # noqa: F401  (loads libsf_engine.so; raises if it is missing)
-from ._cuda_ops import GpuTensor, gputensor_from_numpy, gputensor_to_numpy  # noqa: F401
+  build       compiles libsf_engine.so (importable without the library)
 
+Importing any module that touches the engine loads ``libsf_engine.so`` and
+raises ``ImportError`` if it has not been built; there is no CPU fallback.
+"""
 __version__ = "0.1.0"
+
+_LAZY = {"GpuTensor", "gputensor_from_numpy", "gputensor_to_numpy"}
+
+
+def __getattr__(name):
+    if name in _LAZY:
+        from . import _cuda_ops
+        return getattr(_cuda_ops, name)
+    raise AttributeError(name)

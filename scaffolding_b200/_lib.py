@@ -70,6 +70,8 @@ SIGNATURES: dict[str, list] = {
                 _P(Epilogue), _vp, _sz, _vp],
     "sf_gemm_batched": [_P(Batch), _i64, _i64, _i64, _vp, _i64, _i32, _vp, _i64, _i32, _vp, _i64,
                         _i32, _i32, _P(Epilogue), _vp, _sz, _vp],
+    "sf_linear_skinny_noalloc": [_i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i32, _vp, _i64,
+                                 _i32, _i32, _i32, _vp],
     "sf_gemm_workspace_size": [_P(Batch), _i64, _i64, _i64, _i32, _i32, _i32, _i32, _P(_sz)],
     "sf_set_fp32_mode": [_i32],
     "sf_get_fp32_mode": [_P(_i32)],

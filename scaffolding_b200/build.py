@@ -23,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libsf_engine.so")
 
-SOURCES = ["runtime.cu", "engine.cu", "comm.cpp"]
+SOURCES = ["runtime.cu", "engine.cu", "noalloc.cu", "comm.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -37,7 +37,7 @@ struct GemmSimtArgs {
 
 constexpr int kSimtBM = 128, kSimtBN = 128, kSimtBK = 8, kSimtThreads = 256;
 
-__global__ void __launch_bounds__(kSimtThreads)
+static __global__ void __launch_bounds__(kSimtThreads)
     gemm_simt_kernel(const GemmSimtArgs p) {
   __shared__ float As[2][kSimtBK][kSimtBM];
   __shared__ float Bs[2][kSimtBK][kSimtBN];

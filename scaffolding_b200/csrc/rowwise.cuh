@@ -66,7 +66,7 @@ __device__ __forceinline__ void store4(void* y, int64_t idx, int dtype, float a,
 // Vectorised register-resident softmax: requires cols % 4 == 0 and 16-byte
 // aligned fp32 rows (x), 8-byte aligned rows (16-bit y) or 16-byte (fp32 y).
 template <int VPT>
-__global__ void __launch_bounds__(kSoftmaxThreads)
+static __global__ void __launch_bounds__(kSoftmaxThreads)
     softmax_rows_vec_kernel(const float* __restrict__ x, int64_t ldx, void* __restrict__ y,
                             int y_dtype, int64_t ldy, int cols, float scale) {
   __shared__ float red[32];
@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads)
 }
 
 // General three-pass softmax (any cols, any alignment, any input dtype).
-__global__ void __launch_bounds__(kSoftmaxThreads)
+static __global__ void __launch_bounds__(kSoftmaxThreads)
     softmax_rows_generic_kernel(const void* __restrict__ x, int x_dtype, int64_t ldx,
                                 void* __restrict__ y, int y_dtype, int64_t ldy, int cols,
                                 float scale) {
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads)
 
 // ─────────────────────── elementwise activation ───────────────────────────
 // y = act(alpha * x)  (dev_silu / dev_gelu / dev_muls of _cuda_ops.pyx:944-998)
-__global__ void unary_act_kernel(const void* __restrict__ x, int x_dtype, void* __restrict__ y,
+static __global__ void unary_act_kernel(const void* __restrict__ x, int x_dtype, void* __restrict__ y,
                                  int y_dtype, int64_t n, float alpha, int act) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -138,7 +138,7 @@ __global__ void unary_act_kernel(const void* __restrict__ x, int x_dtype, void* 
 
 // ─────────────────────────── split-K finaliser ─────────────────────────────
 // out[r, c] = epilogue(ws[r, c]) for the split-K / K == 0 paths (ws == null => 0).
-__global__ void epilogue_finalize_kernel(const float* __restrict__ ws, int64_t ldw, int rows,
+static __global__ void epilogue_finalize_kernel(const float* __restrict__ ws, int64_t ldw, int rows,
                                          int cols, void* __restrict__ out, int out_dtype,
                                          int64_t ldc, EpilogueArgs e) {
   const int64_t total = (int64_t)rows * cols;
@@ -169,7 +169,7 @@ __device__ __forceinline__ float to_tf32(float f) {
   return __uint_as_float(r);
 }
 
-__global__ void tf32_split_kernel(const float* __restrict__ X, int64_t rs, int64_t ks, int rows,
+static __global__ void tf32_split_kernel(const float* __restrict__ X, int64_t rs, int64_t ks, int rows,
                                   int K, float* __restrict__ out, int64_t ld_out, int pattern) {
   const int64_t total = (int64_t)rows * K;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
@@ -191,7 +191,7 @@ __global__ void tf32_split_kernel(const float* __restrict__ X, int64_t rs, int64
 
 // Dense K-major copy of a strided 16-bit operand (used when a layout cannot
 // be described to TMA directly).
-__global__ void repack_k_major_kernel(const uint16_t* __restrict__ X, int64_t rs, int64_t ks,
+static __global__ void repack_k_major_kernel(const uint16_t* __restrict__ X, int64_t rs, int64_t ks,
                                       int rows, int K, uint16_t* __restrict__ out, int64_t ld_out) {
   const int64_t total = (int64_t)rows * K;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
@@ -206,7 +206,7 @@ __global__ void repack_k_major_kernel(const uint16_t* __restrict__ X, int64_t rs
 namespace sf {
 // Waits on an mbarrier nothing ever arrives on, with a short limit: proves
 // that an expired wait records its code and returns instead of hanging.
-__global__ void bounded_wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+static __global__ void bounded_wait_selftest_kernel(int* err, unsigned long long limit_ns) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
