@@ -175,6 +175,8 @@ def cpu_reference_sample(workload: str, budget_s: float = 10.0, rows: int = 1024
     sample of the workload; returns (TFLOP/s, description)."""
     from oracle import oracle as O
     cores = len(os.sched_getaffinity(0))
+    if workload == "dit_stack":
+        return _cpu_stack_sample(budget_s)
     if workload == "dit_block":
         w = {k: O.round_bf16(v) for k, v in _dit_weights_np().items()}
         x = O.round_bf16(np.random.default_rng(2).standard_normal((rows, HIDDEN), dtype=np.float32))
@@ -202,6 +204,45 @@ def cpu_reference_sample(workload: str, budget_s: float = 10.0, rows: int = 1024
     return flops / best / 1e12, f"{what}; best of {n} runs; {cores} threads", cores
 
 
+def _cpu_stack_sample(budget_s: float, rows: int = 128, layers: int = 30):
+    """tokens/s of the reference's CPU path on the DiT stack, from a bounded
+    sample: one layer for `rows` query tokens (linears on those rows,
+    attention of those rows against all 17776 keys of their sample, 30
+    heads), extrapolated linearly (cost per query token is independent of
+    which token it is) to all tokens and `layers` layers."""
+    from oracle import oracle as O
+    cores = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(3)
+    w = _dit_weights_np()
+    H, D, C = 30, 64, HIDDEN
+    x = rng.standard_normal((rows, C), dtype=np.float32)
+    kv = rng.standard_normal((TOKENS, 2 * C), dtype=np.float32)
+
+    def one():
+        qkv = O.linear(x, w["qkv_w"])
+        q = qkv[:, :C]
+        attn = np.empty((rows, C), np.float32)
+        for h in range(H):
+            k = kv[:, h * D:(h + 1) * D]
+            v = kv[:, C + h * D:C + (h + 1) * D]
+            attn[:, h * D:(h + 1) * D] = O.sdpa(q[None, :, h * D:(h + 1) * D], k[None], v[None])[0]
+        hh = O.linear(attn, w["out_w"], w["out_b"]) + x
+        f = O.gelu_tanh(O.linear(hh, w["up_w"], w["up_b"]))
+        return O.linear(f, w["down_w"], w["down_b"]) + hh
+
+    one()
+    best, t_end, n = float("inf"), time.perf_counter() + budget_s, 0
+    while time.perf_counter() < t_end or n < 2:
+        t0 = time.perf_counter()
+        one()
+        best = min(best, time.perf_counter() - t0)
+        n += 1
+    tok_s = rows / (best * layers)
+    what = (f"one DiT layer for {rows} query tokens (linears + attention over {TOKENS} keys, "
+            f"30 heads), fp32 NumPy; tokens/s extrapolated to {layers} layers; best of {n}; {cores} threads")
+    return tok_s, what, cores
+
+
 def run_reference_arm(args, dist):
     if dist.rank != 0:
         return
@@ -211,6 +252,23 @@ def run_reference_arm(args, dist):
     for _ in range(args.warmup):
         cpu_reference_sample(args.workload, budget_s=0.0, rows=rows)
     times = []
+    if args.workload == "dit_stack":
+        vals = []
+        for _ in range(args.steps):
+            v, sample, _ = _cpu_stack_sample(0.0)
+            vals.append(v)
+        value = sum(vals) / len(vals)
+        line = {"impl": "reference", "metric": _metric(args.workload), "value": value,
+                "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": M_TOTAL / value * 1e3,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                "config": _config(args, 1),
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if args.workload == "dit_block":
         from oracle import oracle as O2
         w = {k: O2.round_bf16(v) for k, v in _dit_weights_np().items()}
@@ -227,7 +285,7 @@ def run_reference_arm(args, dist):
     t = sum(times) / len(times)
     value = flops / t / 1e12
     line = {"impl": "reference", "metric": _metric(args.workload), "value": value,
-            "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "unit": _unit(args.workload), "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t * 1e3, "higher_is_better": True, "dtype": "f32",
             "data": "synthetic", "config": _config(args, 1),
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
@@ -238,12 +296,22 @@ def run_reference_arm(args, dist):
 
 
 def _metric(workload):
-    return {"dit_block": "GEMM TFLOP/s (DiT-block linears, bf16, M-sharded)",
+    return {"dit_stack": "DiT-stack tokens/s (30-layer forward, bf16, token-sharded)",
+            "dit_block": "GEMM TFLOP/s (DiT-block linears, bf16, M-sharded)",
             "square": "GEMM TFLOP/s (square NT GEMM, bf16)",
             "skinny": "GEMM TFLOP/s (skinny-M linear, bf16)"}[workload]
 
 
+def _unit(workload):
+    return "tokens/s" if workload == "dit_stack" else "TFLOP/s"
+
+
 def _config(args, world):
+    if args.workload == "dit_stack":
+        return {"workload": f"dit_stack (config 5): {args.layers} layers, 30 heads x 64, query chunks of 2048",
+                "tokens": M_TOTAL, "hidden": HIDDEN, "global_batch": BATCH, "seq_len": TOKENS,
+                "layers": args.layers, "parallelism": f"token-shard{world}",
+                "l2": "inputs and per-chunk scores (>= 4 GB) larger than L2; 512 MiB write between steps"}
     if args.workload == "dit_block":
         return {"workload": "dit_block_linears (config 4)", "tokens": M_TOTAL, "hidden": HIDDEN,
                 "global_batch": BATCH, "seq_len": TOKENS, "parallelism": f"m-shard{world}",
@@ -331,7 +399,34 @@ def run_gpu_arm(args, dist):
                 "sf_memset")
 
     # ── workload
-    if args.workload == "dit_block":
+    stack = None
+    if args.workload == "dit_stack":
+        plan = dit.ShardPlan(BATCH, TOKENS, world, rank)
+        kv_comm = None
+        if comm is not None and plan.kv_exchange:
+            kp = C.c_void_p()
+            E.check(lib.sf_comm_split(C.c_void_p(comm), plan.group_color, rank, C.byref(kp)),
+                    "sf_comm_split")
+            kv_comm = kp.value
+        stack = dit.DitStack(plan, HIDDEN, 30, args.layers, dev, chunk=2048, seed=7,
+                             kv_comm=kv_comm, world_comm=comm)
+        x_full = ops._alloc((M_TOTAL, HIDDEN), bf, dev)
+        E.check(lib.sf_fill_normal(C.c_void_p(x_full.ptr), 2, M_TOTAL * HIDDEN, 11, 0.0, 1.0, None),
+                "sf_fill_normal")
+        x = ops.GpuTensor(x_full.buffer, (plan.m, HIDDEN), bf, dev)
+        x_off = plan.row0 * HIDDEN * 2
+        m = plan.m
+        flops_job = dit.stack_flops(BATCH, TOKENS, HIDDEN, 30, args.layers)
+        flops_rank = flops_job / world
+        out_ptr = [0]
+
+        def step(timer=None, x_ptr=None):
+            out_ptr[0] = stack.forward((x_full.ptr + x_off) if x_ptr is None else x_ptr,
+                                       stream=stream, timer=timer)
+        launches_per_step = stack.launches_per_forward()
+        h2d_bytes = m * HIDDEN * 2
+        d2h_bytes = m * HIDDEN * 2
+    elif args.workload == "dit_block":
         assert M_TOTAL % world == 0
         m = M_TOTAL // world
         w = {k: v for k, v in _dit_weights_np().items()}
@@ -430,13 +525,50 @@ def run_gpu_arm(args, dist):
     rank_s = sum(step_ms) / 1e3
     job_s = dist.max(rank_s)
     value = flops_job * args.steps / job_s / 1e12
+    tflops_job = value
+    if args.workload == "dit_stack":
+        value = M_TOTAL * args.steps / job_s
 
-    # roofline of the dominant kernel (the tcgen05 GEMM; all launches of a step)
+    # roofline of the dominant kernel
+    hbm, burst, sustained, src = _peaks()
+    peak = sustained if job_s >= 1.0 else burst
     gemm_ms = sum(sum(v) for v in kern_ms.values())
     n_launch = sum(len(v) for v in kern_ms.values())
     achieved = flops_rank * args.steps / (gemm_ms / 1e3) / 1e12
-    hbm, burst, sustained, src = _peaks()
-    peak = sustained if job_s >= 1.0 else burst
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "kernel": "sf::gemm_tc_kernel (tcgen05)",
+            "launch_ms_mean": gemm_ms / max(1, n_launch),
+            "peak_source": f"{src} ({'sustained' if peak == sustained else 'burst'} bf16)"}
+    if stack is not None:
+        totals = {k: sum(v) for k, v in kern_ms.items()}
+        top = max(totals, key=totals.get)
+        p = stack.plan
+        rows_q = p.tokens if p.whole_samples else p.m
+        per_chunk_rows = [min(2048, rows_q - c) for c in range(0, rows_q, 2048)]
+        S_elems = sum(p.samples_per_rank * 30 * r * TOKENS for r in per_chunk_rows)  # per layer
+        lin_flops = dit.block_flops(p.m) * args.layers
+        bytes_per_layer = {"softmax": S_elems * (4 + 2), "qk": S_elems * 4, "pv": S_elems * 2}
+        n_top = len(kern_ms[top])
+        ms_top = totals[top] / n_top
+        if top in bytes_per_layer:
+            byt = bytes_per_layer[top] * args.layers * args.steps / n_top
+            roof = {"bound": "hbm", "achieved": byt / (ms_top / 1e3) / 1e9, "peak": hbm,
+                    "unit": "GB/s", "frac": byt / (ms_top / 1e3) / 1e9 / hbm,
+                    "kernel": {"softmax": "sf::softmax_rows_vec_kernel",
+                               "qk": "sf::gemm_tc_kernel (QK^T, fp32 scores)",
+                               "pv": "sf::gemm_tc_kernel (P.V)"}[top],
+                    "algorithmic_bytes_per_launch": byt, "launch_ms_mean": ms_top,
+                    "peak_source": f"{src} HBM copy"}
+        else:
+            fl = {"q": 2.0 * p.m * HIDDEN * HIDDEN, "kv": 4.0 * p.m * HIDDEN * HIDDEN,
+                  "out": 2.0 * p.m * HIDDEN * HIDDEN, "up": 8.0 * p.m * HIDDEN * HIDDEN,
+                  "down": 8.0 * p.m * HIDDEN * HIDDEN}.get(top, 0.0)
+            roof["achieved"] = fl / (ms_top / 1e3) / 1e12
+            roof["frac"] = roof["achieved"] / peak
+            roof["launch_ms_mean"] = ms_top
+        roof["kernel_share"] = totals[top] / sum(totals.values())
+        roof["top_kernel"] = top
+        del lin_flops
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -451,9 +583,15 @@ def run_gpu_arm(args, dist):
         pin_in = E.PinnedHostBuffer(h2d_bytes)
         pin_out = E.PinnedHostBuffer(d2h_bytes)
         dev_in = E.DeviceBuffer.alloc(h2d_bytes, dev)
-        src_ptr = (x.ptr if args.workload == "dit_block" else (a.ptr if args.workload == "square" else xs.ptr))
+        if args.workload == "dit_stack":
+            src_ptr = x_full.ptr + x_off
+        else:
+            src_ptr = (x.ptr if args.workload == "dit_block" else (a.ptr if args.workload == "square" else xs.ptr))
         E.memcpy(pin_in.ptr, src_ptr, h2d_bytes, 1, stream)
-        res_ptr = (block.y.ptr if args.workload == "dit_block" else (c.ptr if args.workload == "square" else y.ptr))
+        if args.workload == "dit_stack":
+            res_ptr = stack.y[(args.layers - 1) % 2].ptr
+        else:
+            res_ptr = (block.y.ptr if args.workload == "dit_block" else (c.ptr if args.workload == "square" else y.ptr))
         e2e_t = EventTimer(lib, stream)
         for _ in range(max(1, args.warmup // 2)):
             E.memcpy(dev_in.ptr, pin_in.ptr, h2d_bytes, 0, stream)
@@ -471,7 +609,8 @@ def run_gpu_arm(args, dist):
         E.stream_sync(stream)
         dist.barrier()
         e2e_s = dist.max(sum(e2e_t.collect()["e2e"]) / 1e3)
-        e2e = {"value": flops_job * args.steps / e2e_s / 1e12, "unit": "TFLOP/s",
+        e2e_val = (M_TOTAL * args.steps / e2e_s) if args.workload == "dit_stack" else flops_job * args.steps / e2e_s / 1e12
+        e2e = {"value": e2e_val, "unit": _unit(args.workload),
                "h2d_bytes_per_step": h2d_bytes * world, "d2h_bytes_per_step": d2h_bytes * world,
                "ms_per_step": e2e_s / args.steps * 1e3}
 
@@ -479,28 +618,27 @@ def run_gpu_arm(args, dist):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, cores = cpu_reference_sample(args.workload, budget_s=args.cpu_budget)
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+        cpu = {"value": v, "unit": _unit(args.workload), "cores": cores, "kind": "port", "sample": sample}
 
     if comm is not None:
         E.stream_sync(stream)
+        if stack is not None and stack.kv_comm:
+            lib.sf_comm_destroy(C.c_void_p(stack.kv_comm))
         lib.sf_comm_destroy(C.c_void_p(comm))
 
     if rank == 0:
         line = {
-            "metric": _metric(args.workload), "value": value, "unit": "TFLOP/s",
+            "metric": _metric(args.workload), "value": value, "unit": _unit(args.workload),
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": job_s / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "strong" if args.workload == "dit_block" else "weak",
+            "scaling": "strong" if args.workload.startswith("dit") else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": _config(args, world),
-            "pct_of_bf16_peak": value / world / burst,
-            "tokens_per_s": (M_TOTAL * args.steps / job_s) if args.workload == "dit_block" else None,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{src} ({'sustained' if peak == sustained else 'burst'} bf16)",
-                         "kernel": "sf::gemm_tc_kernel (tcgen05)",
-                         "launch_ms_mean": gemm_ms / max(1, n_launch)},
+            "tflops": tflops_job,
+            "pct_of_bf16_peak": tflops_job / world / burst,
+            "tokens_per_s": (M_TOTAL * args.steps / job_s) if args.workload.startswith("dit") else None,
+            "roofline": dict(roof, traffic=traffic),
             "kernel_ms": {k: sum(v) / len(v) for k, v in kern_ms.items()},
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -518,14 +656,15 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="dit_block", choices=["dit_block", "square", "skinny"])
+    ap.add_argument("--workload", default="dit_block", choices=["dit_stack", "dit_block", "square", "skinny"])
+    ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()
     if args.size is None:
-        args.size = {"dit_block": 0, "square": 8192, "skinny": 8}[args.workload]
+        args.size = {"dit_stack": 0, "dit_block": 0, "square": 8192, "skinny": 8}[args.workload]
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()

@@ -253,6 +253,13 @@ int32_t sf_device_error_status(int32_t device, int32_t* code, int32_t clear);
  * in the reference). */
 int32_t sf_selftest_bounded_wait(int64_t limit_ns, int32_t* device_code, void* stream);
 
+/* x[i] = mean + std * N(0,1) sample, i < n, from a counter-based generator
+ * keyed by (seed, i): the same seed gives the same values on every device.
+ * Synthetic weight/activation initialisation for benchmarks and tests (the
+ * reference draws its inits on the host, nn/layers.py:66-74). */
+int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float mean, float std,
+                       void* stream);
+
 const char* sf_last_error(void);
 const char* sf_version(void);
 
@@ -263,6 +270,9 @@ const char* sf_version(void);
  * (NVLink/NVSwitch); NCCL is loaded at run time. */
 int32_t sf_comm_unique_id(uint8_t id_out[128]);
 int32_t sf_comm_init(void** comm, int32_t nranks, int32_t rank, const uint8_t id[128]);
+/* Sub-communicator of the ranks passing the same `color`, ordered by `key`
+ * (e.g. the ranks holding tokens of one sample, which exchange K/V). */
+int32_t sf_comm_split(void* comm, int32_t color, int32_t key, void** out);
 /* recv[r * bytes_per_rank ...] = send of rank r, for every rank r. */
 int32_t sf_comm_allgather(void* comm, const void* send, void* recv, size_t bytes_per_rank,
                           void* stream);

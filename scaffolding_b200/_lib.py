@@ -107,10 +107,12 @@ SIGNATURES: dict[str, list] = {
     "sf_enable_peer_access_all": [],
     "sf_device_error_status": [_i32, _P(_i32), _i32],
     "sf_selftest_bounded_wait": [_i64, _P(_i32), _vp],
+    "sf_fill_normal": [_vp, _i32, _i64, C.c_uint64, C.c_float, C.c_float, _vp],
     "sf_last_error": [],
     "sf_version": [],
     "sf_comm_unique_id": [_P(C.c_uint8)],
     "sf_comm_init": [_P(_vp), _i32, _i32, _P(C.c_uint8)],
+    "sf_comm_split": [_vp, _i32, _i32, _P(_vp)],
     "sf_comm_allgather": [_vp, _vp, _vp, _sz, _vp],
     "sf_comm_allreduce_f32": [_vp, _P(C.c_float), _sz, _i32, _vp],
     "sf_comm_async_error": [_vp, _P(_i32)],

@@ -35,6 +35,7 @@ struct NcclApi {
   NcclResult (*comm_destroy)(NcclComm) = nullptr;
   NcclResult (*comm_abort)(NcclComm) = nullptr;
   NcclResult (*get_async_error)(NcclComm, NcclResult*) = nullptr;
+  NcclResult (*comm_split)(NcclComm, int, int, NcclComm*, void*) = nullptr;
   const char* (*error_string)(NcclResult) = nullptr;
   bool ok = false;
   std::string why;
@@ -64,6 +65,7 @@ NcclApi& api() {
     SF_SYM(comm_abort, "ncclCommAbort");
     SF_SYM(get_async_error, "ncclCommGetAsyncError");
     SF_SYM(error_string, "ncclGetErrorString");
+    SF_SYM(comm_split, "ncclCommSplit");
 #undef SF_SYM
     a.ok = true;
   });
@@ -106,6 +108,16 @@ int32_t sf_comm_init(void** comm, int32_t nranks, int32_t rank, const uint8_t id
   NcclResult r = api().comm_init_rank(&c, nranks, uid, rank);
   if (r != 0) return nccl_fail(r, "ncclCommInitRank");
   *comm = c;
+  return SF_OK;
+}
+
+int32_t sf_comm_split(void* comm, int32_t color, int32_t key, void** out) {
+  if (!comm || !out) return sf::fail(SF_ERR_INVALID_ARGUMENT, "null argument");
+  SF_NCCL_READY();
+  NcclComm c = nullptr;
+  NcclResult r = api().comm_split(comm, color, key, &c, nullptr);
+  if (r != 0) return nccl_fail(r, "ncclCommSplit");
+  *out = c;
   return SF_OK;
 }
 

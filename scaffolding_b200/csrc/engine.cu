@@ -145,6 +145,9 @@ static int pick_bn(int64_t n) {
   return w192 < w256 ? 192 : 256;
 }
 
+// Reduction length from which narrow 16-bit GEMMs promote their accumulators.
+constexpr int64_t kPromoteMinK = 8192;
+
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return (v && *v) ? atoi(v) : dflt;
@@ -192,6 +195,10 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     pl.kind = kPlanTc;
     pl.b_mn = true;
     pl.bn = p.N <= 64 ? 64 : (p.N <= 128 ? 128 : (pick_bn(p.N) == 192 ? 192 : 256));
+    // Long reductions into narrow outputs (attention P.V: K = keys, N = head
+    // dim) average thousands of small terms; keep them IEEE-accurate by
+    // promoting TMEM partial sums into fp32 registers every 4 k-blocks.
+    if (p.K >= kPromoteMinK && pl.bn <= 128) pl.promote = true;
     return pl;
   }
   if (batch == 1 && p.M <= 256 && p.N >= 256) {
@@ -291,14 +298,26 @@ static int32_t launch_tc(int bn, const CUtensorMap& ma, const CUtensorMap& mb, c
   }
 }
 
+template <int FMT>
+static int32_t launch_tc_mn_promoted(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                                     const GemmTcArgs& a, int grid, cudaStream_t s, int device) {
+  switch (bn) {
+    case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, true, 4>>(ma, mb, a, grid, s, device);
+    case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, true, 4>>(ma, mb, a, grid, s, device);
+    default: return fail(SF_ERR_UNSUPPORTED, "promoted MN-major tile width %d", bn);
+  }
+}
+
 static int32_t dispatch_tc(int fmt, bool bmn, bool promote, int bn, const CUtensorMap& ma,
                            const CUtensorMap& mb, const GemmTcArgs& a, int grid, cudaStream_t s,
                            int device) {
   if (fmt == kBF16) {
+    if (bmn && promote) return launch_tc_mn_promoted<1>(bn, ma, mb, a, grid, s, device);
     return bmn ? launch_tc<1, true, 0>(bn, ma, mb, a, grid, s, device)
                : launch_tc<1, false, 0>(bn, ma, mb, a, grid, s, device);
   }
   if (fmt == kF16) {
+    if (bmn && promote) return launch_tc_mn_promoted<0>(bn, ma, mb, a, grid, s, device);
     return bmn ? launch_tc<0, true, 0>(bn, ma, mb, a, grid, s, device)
                : launch_tc<0, false, 0>(bn, ma, mb, a, grid, s, device);
   }
@@ -683,6 +702,21 @@ int32_t sf_selftest_bounded_wait(int64_t limit_ns, int32_t* device_code, void* s
   SF_CUDA_TRY(cudaMemcpyAsync(&v, word, sizeof(int), cudaMemcpyDeviceToHost, s));
   SF_CUDA_TRY(cudaStreamSynchronize(s));
   *device_code = v;
+  return SF_OK;
+}
+
+int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float mean, float std,
+                       void* stream) {
+  if (n < 0) return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
+  if (n == 0) return SF_OK;
+  if (!x) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16) return fail(SF_ERR_INVALID_ARGUMENT, "dtype %d", dtype);
+  DeviceInfo* dev = nullptr;
+  int32_t st = current_device_info(&dev, nullptr);
+  if (st != SF_OK) return st;
+  fill_normal_kernel<<<grid_for(n, dev->sm_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, dtype, n, seed, mean, std);
+  SF_CUDA_TRY(cudaGetLastError());
   return SF_OK;
 }
 

@@ -189,6 +189,30 @@ static __global__ void tf32_split_kernel(const float* __restrict__ X, int64_t rs
   }
 }
 
+// ─────────────────────────── seeded normal fill ─────────────────────────────
+// Counter-based: element i gets a standard normal sample from two 32-bit
+// uniforms produced by the SplitMix64 finaliser applied to (seed, i), turned
+// into a normal by the Box-Muller transform.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+static __global__ void fill_normal_kernel(void* x, int dtype, int64_t n, uint64_t seed, float mean,
+                                          float stdv) {
+  const uint64_t key = splitmix64(seed);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = splitmix64(key ^ static_cast<uint64_t>(i));
+    const float u1 = (static_cast<float>(r >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+    const float u2 = static_cast<float>((r >> 16) & 0xFFFFFFull) * (1.0f / 16777216.0f);
+    const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    store_from_f32(x, i, dtype, mean + stdv * z);
+  }
+}
+
 // Dense K-major copy of a strided 16-bit operand (used when a layout cannot
 // be described to TMA directly).
 static __global__ void repack_k_major_kernel(const uint16_t* __restrict__ X, int64_t rs, int64_t ks,

@@ -17,6 +17,8 @@ block is exactly four tcgen05 GEMM launches.
 """
 from __future__ import annotations
 
+import math
+
 import numpy as np
 
 from . import _cuda_ops as ops
@@ -84,3 +86,245 @@ class DitLinears:
             if timer is not None:
                 timer.stop(name)
 
+
+
+# ───────────────────────────── token sharding ─────────────────────────────
+
+class ShardPlan:
+    """Token (M) sharding of a ``[batch * tokens, hidden]`` activation over
+    ``world`` ranks, one process per GPU, contiguous row blocks.
+
+    * ``world <= batch``: every rank holds whole samples; attention needs no
+      exchange (keys and queries of a sample live on the same rank).
+    * ``world > batch``: every rank holds a slice of one sample; the ranks of
+      a sample form a K/V group that all-gathers its K/V rows once per layer.
+
+    Replaces ``DataParallel``'s host scatter (``nn/parallel.py:111-147``):
+    rows never leave the device.
+    """
+
+    def __init__(self, batch: int, tokens: int, world: int, rank: int):
+        if not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside world {world}")
+        M = batch * tokens
+        if M % world:
+            raise ValueError(f"{M} token rows do not split over {world} ranks")
+        self.batch, self.tokens, self.world, self.rank = batch, tokens, world, rank
+        self.m = M // world
+        self.row0 = rank * self.m
+        if world <= batch:
+            if batch % world:
+                raise ValueError(f"batch {batch} does not split over {world} ranks")
+            self.samples_per_rank = batch // world
+            self.whole_samples = True
+            self.kv_exchange = False
+            self.sample0 = rank * self.samples_per_rank
+            self.group_color, self.group_size, self.group_rank = rank, 1, 0
+            self.token0 = 0
+        else:
+            if world % batch or tokens % (world // batch):
+                raise ValueError(f"{world} ranks do not tile {batch} samples of {tokens} tokens")
+            self.samples_per_rank = 1
+            self.whole_samples = False
+            self.kv_exchange = True
+            self.group_size = world // batch
+            self.sample0 = self.row0 // tokens
+            self.token0 = self.row0 % tokens
+            self.group_color = self.sample0
+            self.group_rank = rank % self.group_size
+
+    def rows(self) -> tuple[int, int]:
+        return self.row0, self.row0 + self.m
+
+
+class DitStack:
+    """The benchmark's config 5: ``layers`` DiT layers (attention + block
+    linears) over a token shard, bf16 storage, fp32 accumulation.
+
+    Per layer (all on one stream):
+      q  = x Wq^T, kv = x Wkv^T          (Wq, Wkv = row blocks of to_qkv)
+      [kv all-gather inside the K/V group when the sample is split]
+      per query chunk of <= ``chunk`` rows, for every (sample, head):
+        S = (Q K^T) / sqrt(d)  fp32   -- one batched GEMM, scale in the epilogue
+        P = softmax(S)         bf16   -- row softmax in fp32
+        O = P V                       -- one batched GEMM, V read MN-major in place
+      h = O Wo^T + bo + x
+      y = gelu(h W1^T + b1) W2^T + b2 + h
+    The reference runs the same sequence with separate scale / softmax /
+    bmm launches and the attention on the host (``nn/functional.py:310-321``,
+    ``diffusion/models.py:529-590``).
+    """
+
+    def __init__(self, plan: ShardPlan, hidden: int, heads: int, layers: int, device: int,
+                 chunk: int = 2048, weights: list | None = None, seed: int = 1,
+                 kv_comm=None, world_comm=None):
+        import ctypes as C
+
+        from ._lib import check, lib
+        self.plan, self.C, self.H, self.L = plan, hidden, heads, layers
+        self.D = hidden // heads
+        self.dev = device
+        self.chunk = chunk
+        self.kv_comm, self.world_comm = kv_comm, world_comm
+        bf = E.bfloat16
+        m, Cw = plan.m, hidden
+        shapes = {"qkv_w": (3 * Cw, Cw), "out_w": (Cw, Cw), "out_b": (Cw,),
+                  "up_w": (4 * Cw, Cw), "up_b": (4 * Cw,), "down_w": (Cw, 4 * Cw),
+                  "down_b": (Cw,)}
+        self.w = []
+        for li in range(layers):
+            if weights is not None:
+                self.w.append({k: ops.gputensor_from_numpy(np.ascontiguousarray(v).astype(bf), device)
+                               for k, v in weights[li].items()})
+                continue
+            lw = {}
+            for j, (k, shp) in enumerate(shapes.items()):
+                t = ops._alloc(shp, bf, device)
+                if k.endswith("_b"):
+                    check(lib.sf_memset(C.c_void_p(t.ptr), 0, t.numel * 2, None), "sf_memset")
+                else:
+                    check(lib.sf_fill_normal(C.c_void_p(t.ptr), DT_BF16, t.numel,
+                                             seed * 1000003 + li * 16 + j, 0.0, 0.02, None),
+                          "sf_fill_normal")
+                lw[k] = t
+            self.w.append(lw)
+        spr = plan.samples_per_rank
+        keys = plan.tokens
+        self.q = ops._alloc((m, Cw), bf, device)
+        self.kv_local = ops._alloc((m, 2 * Cw), bf, device)
+        self.kv_full = (ops._alloc((keys, 2 * Cw), bf, device) if plan.kv_exchange
+                        else self.kv_local)
+        q_rows = plan.tokens if plan.whole_samples else m
+        crow = min(chunk, q_rows)
+        self.S = ops._alloc((spr, heads, crow, keys), np.float32, device)
+        self.P = ops._alloc((spr, heads, crow, keys), bf, device)
+        self.attn = ops._alloc((m, Cw), bf, device)
+        self.h = ops._alloc((m, Cw), bf, device)
+        self.f = ops._alloc((m, 4 * Cw), bf, device)
+        self.y = [ops._alloc((m, Cw), bf, device), ops._alloc((m, Cw), bf, device)]
+        self.out_full = (ops._alloc((plan.batch * plan.tokens, Cw), bf, device)
+                         if plan.world > 1 else None)
+
+    # ── launches
+    def _gemm(self, name, timer, stream, *args, **kw):
+        if timer is not None:
+            timer.start(name)
+        E.gemm(*args, device=self.dev, stream=stream, **kw)
+        if timer is not None:
+            timer.stop(name)
+
+    def _attention(self, stream, timer):
+        import ctypes as C
+
+        from ._lib import check, lib
+        p, Cw, H, D = self.plan, self.C, self.H, self.D
+        keys = p.tokens
+        spr = p.samples_per_rank
+        q_rows = p.tokens if p.whole_samples else p.m
+        scale = 1.0 / math.sqrt(D)
+        bf = DT_BF16
+        for c0 in range(0, q_rows, self.chunk):
+            rows = min(self.chunk, q_rows - c0)
+            s_batch = rows * keys
+            bt = E.make_batch(H, spr, a=(D, keys * Cw), b=(D, keys * 2 * Cw),
+                              c=(s_batch, H * s_batch))
+            self._gemm("qk", timer, stream, rows, keys, D, self.q.ptr + c0 * Cw * 2, Cw, 0,
+                       self.kv_full.ptr, 2 * Cw, 1, self.S.ptr, keys, bf, 0,
+                       epi=E.make_epilogue(alpha=scale), batch=bt)
+            if timer is not None:
+                timer.start("softmax")
+            E.softmax_rows(self.S.ptr, 0, keys, self.P.ptr, bf, keys, spr * H * rows, keys, 1.0,
+                           stream=stream, device=self.dev)
+            if timer is not None:
+                timer.stop("softmax")
+            bt2 = E.make_batch(H, spr, a=(s_batch, H * s_batch), b=(D, keys * 2 * Cw),
+                               c=(D, keys * Cw))
+            self._gemm("pv", timer, stream, rows, D, keys, self.P.ptr, keys, 0,
+                       self.kv_full.ptr + Cw * 2, 2 * Cw, 0, self.attn.ptr + c0 * Cw * 2, Cw,
+                       bf, bf, batch=bt2)
+
+    def qkv(self, li: int, x_ptr: int, stream=None, timer=None) -> None:
+        """q and the local K/V rows of layer ``li``."""
+        p, Cw, w = self.plan, self.C, self.w[li]
+        m, bf = p.m, DT_BF16
+        self._gemm("q", timer, stream, m, Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr, Cw, 1,
+                   self.q.ptr, Cw, bf, bf)
+        self._gemm("kv", timer, stream, m, 2 * Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr + Cw * Cw * 2,
+                   Cw, 1, self.kv_local.ptr, 2 * Cw, bf, bf)
+
+    def exchange(self, stream=None, timer=None) -> None:
+        """All-gather the K/V rows of this rank's sample inside its K/V group."""
+        import ctypes as C
+
+        from ._lib import check, lib
+        p = self.plan
+        if not p.kv_exchange:
+            return
+        if timer is not None:
+            timer.start("kv_allgather")
+        check(lib.sf_comm_allgather(C.c_void_p(self.kv_comm), C.c_void_p(self.kv_local.ptr),
+                                    C.c_void_p(self.kv_full.ptr), p.m * 2 * self.C * 2,
+                                    C.c_void_p(stream) if stream else None),
+              "sf_comm_allgather")
+        if timer is not None:
+            timer.stop("kv_allgather")
+
+    def post(self, li: int, x_ptr: int, out_ptr: int, stream=None, timer=None) -> None:
+        """Output projection + residual, FFN + residual."""
+        p, Cw, w = self.plan, self.C, self.w[li]
+        m, bf = p.m, DT_BF16
+        self._gemm("out", timer, stream, m, Cw, Cw, self.attn.ptr, Cw, 0, w["out_w"].ptr, Cw, 1,
+                   self.h.ptr, Cw, bf, bf,
+                   epi=E.make_epilogue(bias_ptr=w["out_b"].ptr, bias_dt=bf, residual_ptr=x_ptr,
+                                       residual_dt=bf, ldr=Cw))
+        self._gemm("up", timer, stream, m, 4 * Cw, Cw, self.h.ptr, Cw, 0, w["up_w"].ptr, Cw, 1,
+                   self.f.ptr, 4 * Cw, bf, bf,
+                   epi=E.make_epilogue(bias_ptr=w["up_b"].ptr, bias_dt=bf, act=ACT_GELU_TANH))
+        self._gemm("down", timer, stream, m, Cw, 4 * Cw, self.f.ptr, 4 * Cw, 0, w["down_w"].ptr,
+                   4 * Cw, 1, out_ptr, Cw, bf, bf,
+                   epi=E.make_epilogue(bias_ptr=w["down_b"].ptr, bias_dt=bf,
+                                       residual_ptr=self.h.ptr, residual_dt=bf, ldr=Cw))
+
+    def layer(self, li: int, x_ptr: int, out_ptr: int, stream=None, timer=None) -> None:
+        self.qkv(li, x_ptr, stream, timer)
+        self.exchange(stream, timer)
+        self._attention(stream, timer)
+        self.post(li, x_ptr, out_ptr, stream, timer)
+
+    def forward(self, x_ptr: int, stream=None, timer=None) -> int:
+        """Run all layers on the local rows starting from ``x_ptr``; return the
+        device pointer of the output (the gathered ``[batch*tokens, C]`` on
+        multi-rank runs, the local rows otherwise)."""
+        import ctypes as C
+
+        from ._lib import check, lib
+        cur = x_ptr
+        for li in range(self.L):
+            out = self.y[li % 2].ptr
+            self.layer(li, cur, out, stream, timer)
+            cur = out
+        if self.out_full is not None:
+            if timer is not None:
+                timer.start("out_allgather")
+            check(lib.sf_comm_allgather(C.c_void_p(self.world_comm), C.c_void_p(cur),
+                                        C.c_void_p(self.out_full.ptr),
+                                        self.plan.m * self.C * 2,
+                                        C.c_void_p(stream) if stream else None),
+                  "sf_comm_allgather")
+            if timer is not None:
+                timer.stop("out_allgather")
+            return self.out_full.ptr
+        return cur
+
+    def launches_per_forward(self) -> int:
+        p = self.plan
+        q_rows = p.tokens if p.whole_samples else p.m
+        chunks = (q_rows + self.chunk - 1) // self.chunk
+        return self.L * (5 + 3 * chunks)
+
+
+def stack_flops(batch: int, tokens: int, hidden: int, heads: int, layers: int) -> float:
+    """Algorithmic FLOPs of one forward: block linears + QK^T and P.V."""
+    M = batch * tokens
+    attn = 2 * (2.0 * batch * heads * tokens * tokens * (hidden // heads))
+    return layers * (block_flops(M, hidden) + attn)

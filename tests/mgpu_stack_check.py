@@ -1,0 +1,87 @@
+"""Multi-GPU check of the token-sharded DiT stack (run under torchrun, one
+process per GPU; driven by tests/test_multi_gpu.py).
+
+For batch 2 (whole samples per rank) and batch 1 (a sample split across
+ranks, K/V all-gathered inside the sample's group) the gathered output of the
+sharded run must match the output of the same stack run on one GPU: every
+row goes through the same kernels over the same keys, except that small
+shards may take the split-K small-M GEMM path, whose fp32 atomics can flip a
+bf16 output by one ulp -- so the bar is the per-element bf16 one with at most
+0.1 % of the outputs differing at all.
+"""
+import ctypes as C
+import datetime
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import torch.distributed as td  # noqa: E402  (gloo bootstrap only)
+
+from oracle import oracle as O  # noqa: E402
+from scaffolding_b200 import _cuda_ops as ops  # noqa: E402
+from scaffolding_b200 import dit  # noqa: E402
+from scaffolding_b200 import engine as E  # noqa: E402
+from scaffolding_b200._lib import lib  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = int(os.environ.get("LOCAL_RANK", rank))
+    td.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    E.set_device(dev)
+    uid = (C.c_uint8 * 128)()
+    if rank == 0:
+        E.check(lib.sf_comm_unique_id(uid), "uid")
+    obj = [bytes(uid) if rank == 0 else None]
+    td.broadcast_object_list(obj, src=0)
+    uid = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+    cp = C.c_void_p()
+    E.check(lib.sf_comm_init(C.byref(cp), world, rank, uid), "comm init")
+    comm = cp.value
+    bf = E.bfloat16
+    Cw, H, L, N = 256, 4, 2, 256
+    failures = 0
+    for B in (2, 1):
+        if (B * N) % world:
+            continue
+        ws = [O.dit_weights(hidden=Cw, seed=60 + i, dtype="bf16", zero_bias=False) for i in range(L)]
+        x = O.round_bf16(np.random.default_rng(61).standard_normal((B * N, Cw), dtype=np.float32))
+        plan = dit.ShardPlan(B, N, world, rank)
+        kv = None
+        if plan.kv_exchange:
+            kp = C.c_void_p()
+            E.check(lib.sf_comm_split(C.c_void_p(comm), plan.group_color, rank, C.byref(kp)), "split")
+            kv = kp.value
+        st = dit.DitStack(plan, Cw, H, L, dev, chunk=96, weights=ws, kv_comm=kv, world_comm=comm)
+        gx = ops.gputensor_from_numpy(x[plan.row0:plan.row0 + plan.m].astype(bf), dev)
+        out_ptr = st.forward(gx.ptr)
+        E.check(lib.sf_device_synchronize(), "sync")
+        got = ops.gputensor_to_numpy(st.out_full).astype(np.float32)
+        if rank == 0:
+            one = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, L, dev, chunk=96, weights=ws)
+            gx1 = ops.gputensor_from_numpy(x.astype(bf), dev)
+            p1 = one.forward(gx1.ptr)
+            ref = ops.gputensor_to_numpy(ops.GpuTensor(one.y[(L - 1) % 2].buffer, (B * N, Cw), bf, dev)).astype(np.float32)
+            assert p1 == one.y[(L - 1) % 2].ptr
+            same = np.array_equal(got, ref)
+            ok, stats = O.elementwise_rel_check(got, ref, rtol=1e-2, tau=1e-2)
+            differ = int(np.count_nonzero(got != ref))
+            print(f"[mgpu] world={world} batch={B} kv_exchange={plan.kv_exchange} bitwise_equal={same} "
+                  f"differing={differ}/{got.size} max_abs_diff={float(np.abs(got - ref).max()):.3e} "
+                  f"bf16_bar_ok={ok}", flush=True)
+            failures += 0 if (ok and differ <= got.size // 1000) else 1
+        if kv:
+            lib.sf_comm_destroy(C.c_void_p(kv))
+        td.barrier()
+    lib.sf_comm_destroy(C.c_void_p(comm))
+    td.destroy_process_group()
+    if rank == 0:
+        print("[mgpu] OK" if failures == 0 else f"[mgpu] FAILED ({failures})", flush=True)
+    sys.exit(1 if failures else 0)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+"""DiT stack (benchmark config 5) on the GPU against the oracle (-m gpu)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.gpu_util import assert_close_16bit, np_dtype, to_host32
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(layers, hidden, seed):
+    return [O.dit_weights(hidden=hidden, seed=seed + i, dtype="bf16", zero_bias=False)
+            for i in range(layers)]
+
+
+def _upload_x(ops, x):
+    return ops.gputensor_from_numpy(x.astype(np_dtype("bf16")))
+
+
+def _host(ops, t, shape=None):
+    if shape is not None:
+        t = ops.GpuTensor(t.buffer, shape, t.dtype, t.device_id)
+    return to_host32(ops, t)
+
+
+def _attention_ref(q, kv, B, N, H, D, chunk):
+    """Oracle attention from the device's own bf16 Q/K/V (P rounded to bf16)."""
+    Cw = H * D
+    qkv = np.concatenate([q, kv], axis=1)
+    return O.dit_attention_chunked(qkv, B, H, D, chunk=chunk, p_dtype="bf16")
+
+
+def test_stack_small_matches_oracle(gpu, ops):
+    """Two layers, 2 samples x 200 tokens, 4 heads x 64, ragged query chunks
+    of 64.  Each GEMM / attention stage is checked against the oracle run on
+    the device's own (identically rounded) stage inputs with the per-element
+    bf16 bar; the two-layer output against the pure oracle composition with
+    the aggregate bar (bf16 intermediates re-rounded at every stage make
+    single-element flips of one ulp unavoidable where outputs cancel)."""
+    from scaffolding_b200 import dit
+    B, N, Cw, H, L, chunk = 2, 200, 256, 4, 2, 64
+    D = Cw // H
+    ws = _weights(L, Cw, 40)
+    x = O.round_bf16(np.random.default_rng(41).standard_normal((B * N, Cw), dtype=np.float32))
+    plan = dit.ShardPlan(B, N, 1, 0)
+    st = dit.DitStack(plan, Cw, H, L, 0, chunk=chunk, weights=ws)
+    gx = _upload_x(ops, x)
+    cur_ptr, cur = gx.ptr, x
+    for li in range(L):
+        w = ws[li]
+        st.qkv(li, cur_ptr)
+        q, kv = _host(ops, st.q), _host(ops, st.kv_local)
+        assert_close_16bit(q, O.linear(cur, w["qkv_w"][:Cw]), f"L{li} q")
+        assert_close_16bit(kv, O.linear(cur, w["qkv_w"][Cw:]), f"L{li} kv")
+        st._attention(None, None)
+        attn = _host(ops, st.attn)
+        assert_close_16bit(attn, _attention_ref(q, kv, B, N, H, D, chunk), f"L{li} attention")
+        out = st.y[li % 2]
+        st.post(li, cur_ptr, out.ptr)
+        h, f, y = _host(ops, st.h), _host(ops, st.f), _host(ops, out)
+        assert_close_16bit(h, O.linear(attn, w["out_w"], w["out_b"]) + cur, f"L{li} out-proj")
+        assert_close_16bit(f, O.gelu_tanh(O.linear(h, w["up_w"], w["up_b"])), f"L{li} ffn-up")
+        assert_close_16bit(y, O.linear(f, w["down_w"], w["down_b"]) + h, f"L{li} ffn-down")
+        cur_ptr, cur = out.ptr, y
+    ref = x
+    for li in range(L):
+        ref = O.dit_layer(ref, ws[li], B, H, D, chunk=chunk, dtype="bf16")
+    assert O.rel_frobenius(cur, ref) < 1e-2
+    # forward() runs the same launches end to end
+    gy = st.forward(gx.ptr)
+    assert gy == st.y[(L - 1) % 2].ptr
+    np.testing.assert_array_equal(_host(ops, st.y[(L - 1) % 2]), cur)
+
+
+def test_sliced_ranks_equal_whole_sample(gpu, ops):
+    """Four emulated ranks holding half a sample each (K/V exchanged between
+    the two ranks of a sample) reproduce the one-rank result.  Shards of 100
+    rows take the small-M GEMM path (split-K with fp32 atomics, a different
+    summation order), so a few outputs may differ by one bf16 ulp; the bar
+    is the per-element bf16 one, and at most 0.1 % of the outputs may differ
+    at all."""
+    from scaffolding_b200 import dit
+    from scaffolding_b200 import engine as E
+    B, N, Cw, H, chunk = 2, 200, 256, 4, 64
+    ws = _weights(1, Cw, 50)
+    x = O.round_bf16(np.random.default_rng(51).standard_normal((B * N, Cw), dtype=np.float32))
+    gx = _upload_x(ops, x)
+    whole = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, 1, 0, chunk=chunk, weights=ws)
+    whole.forward(gx.ptr)
+    ref = _host(ops, whole.y[0])
+    world = 4
+    ranks = [dit.DitStack(dit.ShardPlan(B, N, world, r), Cw, H, 1, 0, chunk=chunk, weights=ws)
+             for r in range(world)]
+    outs = []
+    for r, st in enumerate(ranks):
+        st.qkv(0, gx.ptr + st.plan.row0 * Cw * 2)
+    for st in ranks:  # emulate the K/V all-gather inside each sample's group
+        p = st.plan
+        peers = [o for o in ranks if o.plan.group_color == p.group_color]
+        for q, o in enumerate(sorted(peers, key=lambda s: s.plan.rank)):
+            nbytes = o.plan.m * 2 * Cw * 2
+            E.memcpy(st.kv_full.ptr + q * nbytes, o.kv_local.ptr, nbytes, 2)
+    for r, st in enumerate(ranks):
+        st._attention(None, None)
+        st.post(0, gx.ptr + st.plan.row0 * Cw * 2, st.y[0].ptr)
+        outs.append(_host(ops, st.y[0]))
+    got = np.concatenate(outs)
+    assert_close_16bit(got, ref, "sharded vs whole")
+    assert np.count_nonzero(got != ref) <= got.size // 1000
+
+
+def test_full_size_attention_sampled_rows(gpu, ops):
+    """Config 5 attention at full size (2 x 17776 tokens, 30 heads, 9 query
+    chunks of <= 2048): the oracle recomputes sampled query rows (including
+    the ragged last chunk) from the device's own bf16 Q/K/V."""
+    from scaffolding_b200 import dit
+    B, N, Cw, H = 2, 17776, 1920, 30
+    D = Cw // H
+    plan = dit.ShardPlan(B, N, 1, 0)
+    st = dit.DitStack(plan, Cw, H, 1, 0, chunk=2048, seed=3)
+    xt = ops._alloc((B * N, Cw), np_dtype("bf16"), 0)
+    from scaffolding_b200._lib import lib
+    assert lib.sf_fill_normal(C.c_void_p(xt.ptr), 2, B * N * Cw, 5, 0.0, 1.0, None) == 0
+    st.qkv(0, xt.ptr)
+    st._attention(None, None)
+    q = to_host32(ops, st.q)
+    kv = to_host32(ops, st.kv_full)
+    attn = to_host32(ops, st.attn)
+    rng = np.random.default_rng(0)
+    rows = np.concatenate([rng.choice(B * N, 20, replace=False), [0, N - 1, N, 16384, N + 16390]])
+    for r in rows:
+        b = r // N
+        keys = kv[b * N:(b + 1) * N]
+        ref = np.empty(Cw, np.float32)
+        for h in range(H):
+            s = (q[r, h * D:(h + 1) * D] @ keys[:, h * D:(h + 1) * D].T) * np.float32(0.125)
+            p = O.round_bf16(O.softmax_rows(s[None]))[0]
+            ref[h * D:(h + 1) * D] = p @ keys[:, Cw + h * D:Cw + (h + 1) * D]
+        assert_close_16bit(attn[r][None], ref[None], f"attention row {r}")
+    assert np.isfinite(attn).all()

@@ -1,0 +1,29 @@
+"""Token-sharded DiT stack across real GPUs (-m gpu; needs >= 2 GPUs).
+
+Launches tests/mgpu_stack_check.py under torchrun (one process per GPU,
+NCCL for the data path, gloo only for bootstrap) and requires the gathered
+sharded output to equal the single-GPU output bit for bit.
+"""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def test_sharded_stack_equals_single_gpu(gpu, ops):
+    n = ops.get_device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    world = 4 if n >= 4 else 2
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
+           "--master-port", "29533", os.path.join(HERE, "mgpu_stack_check.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "[mgpu] OK" in r.stdout
