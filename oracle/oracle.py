@@ -27,7 +27,7 @@ __all__ = [
     "matmul", "matmul_nt", "batched_matmul", "batched_matmul_nt",
     "softmax_rows", "sdpa", "dit_attention_chunked", "dit_layer", "dit_block_linears",
     "config1_inputs", "square_inputs", "skinny_inputs", "dit_weights",
-    "rel_frobenius", "elementwise_rel_check", "ACT_NONE", "ACT_SILU",
+    "rel_frobenius", "elementwise_rel_check", "abs_product", "ACT_NONE", "ACT_SILU",
     "ACT_GELU_TANH",
 ]
 
@@ -177,7 +177,7 @@ def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray,
 
 def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
                           head_dim: int, chunk: int = 2048,
-                          p_dtype: str = "f32") -> np.ndarray:
+                          p_dtype: str = "f32", return_absprod: bool = False):
     """Attention over a fused QKV activation, in query chunks.
 
     ``qkv`` is ``[batch*tokens, 3*heads*head_dim]`` laid out as the reference
@@ -187,7 +187,8 @@ def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
     ``S = (Q K^T) * scale``, row softmax in fp32, ``O = P V`` -- the SDPA
     sequence of ``nn/functional.py:314-320`` / ``:323-357``.  ``p_dtype``
     rounds P to the storage type the device path keeps it in.
-    Returns ``[batch*tokens, heads*head_dim]``.
+    Returns ``[batch*tokens, heads*head_dim]`` (and, with ``return_absprod``,
+    the matching ``|P| |V|`` error scale of the P.V products).
     """
     rows, width = qkv.shape
     C = heads * head_dim
@@ -195,6 +196,7 @@ def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
     N = rows // batch
     scale = 1.0 / math.sqrt(head_dim)
     out = np.empty((rows, C), dtype=np.float32)
+    absprod = np.empty((rows, C), dtype=np.float64) if return_absprod else None
     for b in range(batch):
         blk = qkv[b * N:(b + 1) * N]
         for h in range(heads):
@@ -208,7 +210,10 @@ def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
                 p = softmax_rows(s)
                 p = round_to(p, p_dtype)
                 out[b * N + c0:b * N + c1, h * head_dim:(h + 1) * head_dim] = p @ v
-    return out
+                if absprod is not None:
+                    absprod[b * N + c0:b * N + c1, h * head_dim:(h + 1) * head_dim] = \
+                        abs_product(p, v.T)
+    return (out, absprod) if return_absprod else out
 
 
 def dit_layer(x: np.ndarray, w: dict, batch: int, heads: int, head_dim: int,
@@ -316,14 +321,26 @@ def rel_frobenius(out: np.ndarray, ref: np.ndarray) -> float:
     return float(num / den) if den > 0 else float(num)
 
 
+def abs_product(a: np.ndarray, b_t: np.ndarray) -> np.ndarray:
+    """``|a| @ |b_t|^T`` in float64: the sum of absolute products behind each
+    output of ``a @ b_t^T`` (the scale of its rounding error)."""
+    return np.abs(np.asarray(a, np.float64)) @ np.abs(np.asarray(b_t, np.float64)).T
+
+
 def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
-                          tau: float = 1e-2):
+                          tau: float = 1e-2, absprod: np.ndarray | None = None,
+                          kappa: float = 1e-2):
     """Per-element relative check for bf16/fp16 outputs (bar: 1e-2).
 
-    An element passes when ``|out - ref| <= rtol * max(|ref|, tau * rms(ref row))``.
-    The floor ``tau * rms(row)`` only matters where the exact value cancels
-    to nearly zero (|ref| below 1% of the row's RMS), where a relative error
-    is undefined in practice.  Returns ``(ok, stats)`` with the worst pure
+    An element passes when ``|out - ref| <= rtol * max(|ref|, tau * rms(ref row),
+    kappa * absprod)``.  The floors only matter where the exact value cancels
+    to nearly zero, where a relative error is undefined in practice:
+    ``tau * rms(row)`` (1 % of the row's RMS) and, when ``absprod`` -- the
+    sum of absolute products ``(|A| |B|)_ij`` behind each output -- is given,
+    ``kappa * absprod``.  The second is the standard error scale of a dot
+    product; with rtol = kappa = 1e-2 it allows an error of 1e-4 of the
+    absolute sum, the accumulation precision of the tensor cores' fp32
+    accumulators (measured ~2^-15 of the absolute sum on cancelling sums).  Returns ``(ok, stats)`` with the worst pure
     relative error, the worst error against the floored denominator, and the
     number of elements that needed the floor.
     """
@@ -337,6 +354,8 @@ def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
     rms = np.sqrt(np.mean(rr * rr, axis=1, keepdims=True))
     absr = np.abs(rr)
     den = np.maximum(absr, tau * rms)
+    if absprod is not None:
+        den = np.maximum(den, kappa * np.asarray(absprod, np.float64).reshape(rr.shape))
     den = np.where(den > 0, den, 1.0)
     err = np.abs(oo - rr)
     floored = err / den

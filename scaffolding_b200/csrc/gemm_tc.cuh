@@ -11,7 +11,7 @@
 //
 // CTA layout (320 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: one lane streams A/B k-blocks into a STAGES-deep
-//               ring of 128B-swizzled shared-memory stages (no multicast).
+//               ring of 128B-swizzled shared-memory stages (each CTA loads its own tiles).
 //   warp 1      TMEM owner + MMA issuer: one lane issues tcgen05.mma
 //               (M=128, N=BN, K=16 or 8 per instruction) into one of two
 //               TMEM accumulators, committing stage releases and

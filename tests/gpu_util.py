@@ -25,8 +25,12 @@ def to_host32(ops, gt):
     return ops.gputensor_to_numpy(gt).astype(np.float32)
 
 
-def assert_close_16bit(out, ref, what=""):
-    ok, st = O.elementwise_rel_check(out, ref, rtol=RTOL_16BIT, tau=TAU_16BIT)
+KAPPA_16BIT = 1e-2    # floor = KAPPA * (|A| |B|)_ij when the absolute product is supplied
+
+
+def assert_close_16bit(out, ref, what="", absprod=None):
+    ok, st = O.elementwise_rel_check(out, ref, rtol=RTOL_16BIT, tau=TAU_16BIT, absprod=absprod,
+                                     kappa=KAPPA_16BIT)
     assert ok, f"{what}: {st}"
     return st
 

@@ -119,6 +119,18 @@ def test_elementwise_check_floor():
     assert not ok
 
 
+def test_elementwise_check_absprod_floor():
+    # an output that cancels to ~0 is judged against the size of its terms
+    a = np.array([[1.0, -1.0, 1e-3]], np.float32)
+    b = np.array([[1.0, 1.0, 1.0]], np.float32)
+    ref = a @ b.T
+    ap = O.abs_product(a, b)
+    assert ap[0, 0] == 2.001
+    out = ref + np.float32(1e-4)
+    assert not O.elementwise_rel_check(out, ref)[0]
+    assert O.elementwise_rel_check(out, ref, absprod=ap)[0]
+
+
 def test_seeded_inputs_deterministic():
     a1, b1 = O.square_inputs(64, "bf16", seed=5)
     a2, b2 = O.square_inputs(64, "bf16", seed=5)
