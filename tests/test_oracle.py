@@ -125,7 +125,7 @@ def test_elementwise_check_absprod_floor():
     b = np.array([[1.0, 1.0, 1.0]], np.float32)
     ref = a @ b.T
     ap = O.abs_product(a, b)
-    assert ap[0, 0] == 2.001
+    assert abs(ap[0, 0] - 2.001) < 1e-6
     out = ref + np.float32(1e-4)
     assert not O.elementwise_rel_check(out, ref)[0]
     assert O.elementwise_rel_check(out, ref, absprod=ap)[0]
