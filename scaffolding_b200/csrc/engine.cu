@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.h"
@@ -253,6 +254,9 @@ static EpilogueArgs to_epi(const sf_epilogue& e, int out_dt) {
 
 // ───────────────────────────── launchers ─────────────────────────────
 
+// C-operand map for the TMA-store epilogue (set by run_tc before launching).
+static thread_local CUtensorMap t_map_c;
+
 template <class Cfg>
 static int32_t launch_tc_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a,
                              int grid, cudaStream_t s, int device) {
@@ -262,7 +266,7 @@ static int32_t launch_tc_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const
                                      Cfg::SMEM_BYTES));
     attr_set[device] = true;
   }
-  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ma, mb, a);
+  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ma, mb, t_map_c, a);
   SF_CUDA_TRY(cudaGetLastError());
   return SF_OK;
 }
@@ -273,26 +277,26 @@ static int32_t launch_tc(int bn, const CUtensorMap& ma, const CUtensorMap& mb, c
                          int grid, cudaStream_t s, int device) {
   if constexpr (PKB > 0) {
     switch (bn) {
-      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, false, PKB>>(ma, mb, a, grid, s, device);
-      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, false, PKB>>(ma, mb, a, grid, s, device);
+      case 64: return launch_tc_cfg<TcCfg<64, tc_stages<64>(), FMT, false, PKB>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, tc_stages<128>(), FMT, false, PKB>>(ma, mb, a, grid, s, device);
       default: return fail(SF_ERR_UNSUPPORTED, "promoted tile width %d", bn);
     }
   } else if constexpr (BMN) {
     switch (bn) {
-      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, true>>(ma, mb, a, grid, s, device);
-      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, true>>(ma, mb, a, grid, s, device);
-      case 192: return launch_tc_cfg<TcCfg<192, 5, FMT, true>>(ma, mb, a, grid, s, device);
-      case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, true>>(ma, mb, a, grid, s, device);
+      case 64: return launch_tc_cfg<TcCfg<64, tc_stages<64>(), FMT, true>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, tc_stages<128>(), FMT, true>>(ma, mb, a, grid, s, device);
+      case 192: return launch_tc_cfg<TcCfg<192, tc_stages<192>(), FMT, true>>(ma, mb, a, grid, s, device);
+      case 256: return launch_tc_cfg<TcCfg<256, tc_stages<256>(), FMT, true>>(ma, mb, a, grid, s, device);
       default: return fail(SF_ERR_UNSUPPORTED, "MN-major B tile width %d", bn);
     }
   } else {
     switch (bn) {
-      case 16: return launch_tc_cfg<TcCfg<16, 12, FMT, false>>(ma, mb, a, grid, s, device);
-      case 32: return launch_tc_cfg<TcCfg<32, 10, FMT, false>>(ma, mb, a, grid, s, device);
-      case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, false>>(ma, mb, a, grid, s, device);
-      case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, false>>(ma, mb, a, grid, s, device);
-      case 192: return launch_tc_cfg<TcCfg<192, 5, FMT, false>>(ma, mb, a, grid, s, device);
-      case 256: return launch_tc_cfg<TcCfg<256, 4, FMT, false>>(ma, mb, a, grid, s, device);
+      case 16: return launch_tc_cfg<TcCfg<16, tc_stages<16>(), FMT, false>>(ma, mb, a, grid, s, device);
+      case 32: return launch_tc_cfg<TcCfg<32, tc_stages<32>(), FMT, false>>(ma, mb, a, grid, s, device);
+      case 64: return launch_tc_cfg<TcCfg<64, tc_stages<64>(), FMT, false>>(ma, mb, a, grid, s, device);
+      case 128: return launch_tc_cfg<TcCfg<128, tc_stages<128>(), FMT, false>>(ma, mb, a, grid, s, device);
+      case 192: return launch_tc_cfg<TcCfg<192, tc_stages<192>(), FMT, false>>(ma, mb, a, grid, s, device);
+      case 256: return launch_tc_cfg<TcCfg<256, tc_stages<256>(), FMT, false>>(ma, mb, a, grid, s, device);
       default: return fail(SF_ERR_UNSUPPORTED, "tile width %d", bn);
     }
   }
@@ -302,8 +306,8 @@ template <int FMT>
 static int32_t launch_tc_mn_promoted(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
                                      const GemmTcArgs& a, int grid, cudaStream_t s, int device) {
   switch (bn) {
-    case 64: return launch_tc_cfg<TcCfg<64, 8, FMT, true, 4>>(ma, mb, a, grid, s, device);
-    case 128: return launch_tc_cfg<TcCfg<128, 6, FMT, true, 4>>(ma, mb, a, grid, s, device);
+    case 64: return launch_tc_cfg<TcCfg<64, tc_stages<64>(), FMT, true, 4>>(ma, mb, a, grid, s, device);
+    case 128: return launch_tc_cfg<TcCfg<128, tc_stages<128>(), FMT, true, 4>>(ma, mb, a, grid, s, device);
     default: return fail(SF_ERR_UNSUPPORTED, "promoted MN-major tile width %d", bn);
   }
 }
@@ -461,6 +465,35 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   a.ldw = 0;
   a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
+  a.tma_store = 0;
+  memset(&t_map_c, 0, sizeof(t_map_c));
+  if (!swap && pl.splits == 1 && a.vec_ok && env_int("SF_TMA_STORE", 1)) {
+    // Epilogue chunks of CH columns x 32 rows, stored by TMA with the swizzle
+    // matching the chunk's row bytes.
+    const int ch = pl.bn < 32 ? pl.bn : 32;
+    const int row_bytes = ch * oes;
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+    const uint64_t e = static_cast<uint64_t>(oes);
+    uint64_t st1 = static_cast<uint64_t>(p.ldc) * e;
+    uint64_t st2 = p.nb0 > 1 ? static_cast<uint64_t>(p.cs0) * e : st1 * static_cast<uint64_t>(p.M);
+    uint64_t st3 = p.nb1 > 1 ? static_cast<uint64_t>(p.cs1) * e : st2 * static_cast<uint64_t>(p.nb0);
+    st2 = (st2 + 15) & ~15ull;
+    st3 = (st3 + 15) & ~15ull;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.N), static_cast<cuuint64_t>(p.M),
+                          static_cast<cuuint64_t>(p.nb0), static_cast<cuuint64_t>(p.nb1)};
+    cuuint64_t strides[3] = {st1, st2, st3};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(ch), 32u, 1u, 1u};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                    : CU_TENSOR_MAP_SWIZZLE_32B;
+    CUresult r = fn(&t_map_c, tma_dtype(p.out_dt), 4, p.C, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled (C) failed (%d)", static_cast<int>(r));
+    a.tma_store = 1;
+  }
   if (pl.splits > 1) {
     a.ws = static_cast<float*>(p.ws);
     a.ldw = p.N;  // output orientation [M][N]

@@ -66,6 +66,7 @@ struct GemmTcArgs {
   int64_t ldc, c_stride0, c_stride1;
   int c_trans;          // 1: tile element (i, j) is output (row j, col i) (swap-AB)
   int vec_ok;           // 16-byte vector stores legal for the non-transposed path
+  int tma_store;        // 1: stores go through shared memory + TMA (map tmC)
   float* ws;            // split-K fp32 accumulation buffer (output orientation)
   int64_t ldw;
   EpilogueArgs epi;
@@ -87,7 +88,9 @@ struct TcCfg {
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  static constexpr int EPI_SLOT_BYTES = 4096;       // per epilogue warp: 32 rows x <= 128 B
+  static constexpr int STAGING_BYTES = 8 * EPI_SLOT_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + 1024;  // + alignment slack
   static constexpr int ACC_COLS = BN;
   static constexpr int TMEM_COLS = (2 * BN <= 32)    ? 32
                                    : (2 * BN <= 64)  ? 64
@@ -105,6 +108,13 @@ struct TcCfg {
   static_assert(PROMOTE_KB == 0 || BN % (2 * CH) == 0, "promotion needs an even chunk split");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
+
+// Operand-ring depth per N tile: ~180-196 KB of stages plus 32 KB of
+// epilogue staging fit the 227 KB per-CTA shared memory.
+template <int BN>
+constexpr int tc_stages() {
+  return BN >= 192 ? 4 : BN >= 128 ? 6 : BN >= 64 ? 8 : BN >= 32 ? 9 : 10;
+}
 
 __device__ __forceinline__ void tile_coords(int tile, const GemmTcArgs& p, int& mb, int& nb,
                                             int& b0, int& b1) {
@@ -161,8 +171,55 @@ __device__ __forceinline__ void load_row_chunk(const void* base, int64_t idx, in
   }
 }
 
+// Epilogue arithmetic for CH consecutive output columns [j0, j0+CH) of tile
+// row i (non-transposed output):  v = act(alpha * acc + bias) + beta * res.
+// Every data-dependent choice is made once per chunk, outside the per-element
+// loops.
+template <int CH>
+__device__ __forceinline__ void epilogue_compute(const GemmTcArgs& p, int i, int j0, int64_t roff,
+                                                 const float* acc, float* v) {
+  const EpilogueArgs& e = p.epi;
+  const bool full = j0 + CH <= p.N;
+#pragma unroll
+  for (int t = 0; t < CH; ++t) v[t] = e.alpha * acc[t];
+  if (e.bias) {
+    float b[CH];
+    if (full) {
+      load_row_chunk<CH>(e.bias, j0, e.bias_dtype, e.bias_vec != 0, b);
+    } else {
+#pragma unroll
+      for (int t = 0; t < CH; ++t) b[t] = (j0 + t < p.N) ? load_as_f32(e.bias, j0 + t, e.bias_dtype) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < CH; ++t) v[t] += b[t];
+  }
+  if (e.act != kActNone) {
+    if (e.fast_act) {
+#pragma unroll
+      for (int t = 0; t < CH; ++t) v[t] = act_apply_fast(v[t], e.act);
+    } else {
+#pragma unroll
+      for (int t = 0; t < CH; ++t) v[t] = act_apply(v[t], e.act);
+    }
+  }
+  if (e.residual && i < p.M) {
+    float r[CH];
+    const int64_t ridx = roff + (int64_t)i * e.ldr + j0;
+    if (full) {
+      load_row_chunk<CH>(e.residual, ridx, e.residual_dtype, e.res_vec != 0, r);
+    } else {
+#pragma unroll
+      for (int t = 0; t < CH; ++t)
+        r[t] = (j0 + t < p.N) ? load_as_f32(e.residual, ridx + t, e.residual_dtype) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < CH; ++t) v[t] += e.beta * r[t];
+  }
+}
+
 // Apply the epilogue to CH consecutive tile columns [j0, j0+CH) of tile row i
-// and store them.
+// and store them with per-thread global stores (split-K, swap-AB, and
+// outputs TMA cannot describe).
 template <int CH>
 __device__ __forceinline__ void epilogue_store(const GemmTcArgs& p, int i, int j0, int b0, int b1,
                                                const float* acc) {
@@ -199,34 +256,9 @@ __device__ __forceinline__ void epilogue_store(const GemmTcArgs& p, int i, int j
     }
     return;
   }
+  float v[CH];
+  epilogue_compute<CH>(p, i, j0, roff, acc, v);
   const bool full = j0 + CH <= p.N;
-  float bias_v[CH], res_v[CH], v[CH];
-  if (e.bias) {
-    if (full) {
-      load_row_chunk<CH>(e.bias, j0, e.bias_dtype, e.bias_vec != 0, bias_v);
-    } else {
-#pragma unroll
-      for (int t = 0; t < CH; ++t) bias_v[t] = (j0 + t < p.N) ? load_as_f32(e.bias, j0 + t, e.bias_dtype) : 0.0f;
-    }
-  } else {
-#pragma unroll
-    for (int t = 0; t < CH; ++t) bias_v[t] = 0.0f;
-  }
-  if (e.residual) {
-    const int64_t ridx = roff + (int64_t)i * e.ldr + j0;
-    if (full) {
-      load_row_chunk<CH>(e.residual, ridx, e.residual_dtype, e.res_vec != 0, res_v);
-    } else {
-#pragma unroll
-      for (int t = 0; t < CH; ++t)
-        res_v[t] = (j0 + t < p.N) ? load_as_f32(e.residual, ridx + t, e.residual_dtype) : 0.0f;
-    }
-  } else {
-#pragma unroll
-    for (int t = 0; t < CH; ++t) res_v[t] = 0.0f;
-  }
-#pragma unroll
-  for (int t = 0; t < CH; ++t) v[t] = epilogue_value(acc[t], e, bias_v[t], res_v[t]);
   const int64_t base = coff + (int64_t)i * p.ldc + j0;
   if (p.vec_ok && full) {
     if (p.out_dtype == kF32) {
@@ -249,6 +281,49 @@ __device__ __forceinline__ void epilogue_store(const GemmTcArgs& p, int i, int j
   }
 }
 
+// Same epilogue, stored through the warp's shared-memory slot with one TMA
+// bulk tensor store per 32-row x CH-column chunk (warp-collective).  The slot
+// holds the chunk in the swizzled layout the tensor map of C declares
+// (128/64/32-byte swizzle for 128/64/32-byte rows), which also keeps the
+// row-per-lane shared-memory writes free of bank conflicts.  The box is
+// clipped by the hardware at the matrix edges.
+template <int CH>
+__device__ __forceinline__ void epilogue_store_tma(const GemmTcArgs& p, const CUtensorMap* tmC,
+                                                   uint8_t* slot, int lane, int i, int box_row0,
+                                                   int j0, int b0, int b1, const float* acc) {
+  const EpilogueArgs& e = p.epi;
+  const int64_t roff = (int64_t)b0 * e.r_stride0 + (int64_t)b1 * e.r_stride1;
+  float v[CH];
+  epilogue_compute<CH>(p, i, j0, roff, acc, v);
+  if (lane == 0) bulk_wait_group_read0();  // previous store from this slot has read it
+  __syncwarp();
+  if (p.out_dtype == kF32) {
+    constexpr int R = CH * 4;
+    uint8_t* row = slot + lane * R;
+    const int sw = (R == 128) ? (lane & 7) : (R == 64) ? ((lane >> 1) & 3) : ((lane >> 2) & 1);
+#pragma unroll
+    for (int q = 0; q < R / 16; ++q)
+      *reinterpret_cast<float4*>(row + ((q ^ sw) << 4)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+    constexpr int R = CH * 2;
+    uint8_t* row = slot + lane * R;
+    const int sw = (R == 128) ? (lane & 7) : (R == 64) ? ((lane >> 1) & 3) : ((lane >> 2) & 1);
+    const int dt = p.out_dtype;
+#pragma unroll
+    for (int q = 0; q < R / 16; ++q)
+      *reinterpret_cast<uint4*>(row + ((q ^ sw) << 4)) =
+          make_uint4(pack2(v[8 * q], v[8 * q + 1], dt), pack2(v[8 * q + 2], v[8 * q + 3], dt),
+                     pack2(v[8 * q + 4], v[8 * q + 5], dt), pack2(v[8 * q + 6], v[8 * q + 7], dt));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_4d(tmC, slot, j0, box_row0, b0, b1);
+    bulk_commit_group();
+  }
+}
+
 template <int CH>
 __device__ __forceinline__ void tmem_load_chunk(uint32_t taddr, float* out) {
   uint32_t r[CH];
@@ -266,7 +341,7 @@ __device__ __forceinline__ void tmem_load_chunk(uint32_t taddr, float* out) {
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmTcArgs p) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmTcArgs p) {
   constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
   constexpr int CH = Cfg::CH;
   constexpr int PKB = Cfg::PROMOTE_KB;
@@ -301,6 +376,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(&tmem_slot, Cfg::TMEM_COLS);
@@ -434,6 +510,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
+    uint8_t* slot = smem + STAGES * Cfg::STAGE_BYTES + (warp - 2) * Cfg::EPI_SLOT_BYTES;
+    const bool tma_out = p.tma_store != 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
@@ -448,11 +526,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                static_cast<uint32_t>(acc * Cfg::ACC_COLS);
 #pragma unroll 1
+        // Warp-uniform: does any row of this warp's 32-row quadrant exist?
+        const bool rows_live = mb * BM + quad * 32 < p.M;
         for (int c = half * CH; c < BN; c += 2 * CH) {
           float v[CH];
           tmem_load_chunk<CH>(tbase + c, v);
           const int j0 = nb * BN + c;
-          if (j0 < p.N) epilogue_store<CH>(p, i, j0, b0, b1, v);
+          if (j0 < p.N && rows_live) {
+            if (tma_out)
+              epilogue_store_tma<CH>(p, &tmC, slot, lane, i, mb * BM + quad * 32, j0, b0, b1, v);
+            else
+              epilogue_store<CH>(p, i, j0, b0, b1, v);
+          }
         }
         tc_fence_before();
         mbar_arrive(&tempty_bar[acc]);
@@ -493,14 +578,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         }
         if (!ok) break;
 #pragma unroll
+        const bool rows_live = mb * BM + quad * 32 < p.M;
         for (int q = 0; q < OWN / CH; ++q) {
           const int j0 = nb * BN + half * CH + q * 2 * CH;
-          if (j0 < p.N) epilogue_store<CH>(p, i, j0, b0, b1, &racc[q * CH]);
+          if (j0 < p.N && rows_live) {
+            if (tma_out)
+              epilogue_store_tma<CH>(p, &tmC, slot, lane, i, mb * BM + quad * 32, j0, b0, b1,
+                                     &racc[q * CH]);
+            else
+              epilogue_store<CH>(p, i, j0, b0, b1, &racc[q * CH]);
+          }
         }
       }
     }
   }
 
+  if (warp >= 2 && p.tma_store && lane == 0) bulk_wait_group0();
   __syncwarp();
   tc_fence_before();
   __syncthreads();

@@ -63,11 +63,11 @@ int32_t set_smem_attr() {
 
 template <int FMT>
 int32_t set_attrs_fmt() {
-  int32_t st = set_smem_attr<TcCfg<16, 12, FMT, false>>();
-  if (st == SF_OK) st = set_smem_attr<TcCfg<32, 10, FMT, false>>();
-  if (st == SF_OK) st = set_smem_attr<TcCfg<64, 8, FMT, false>>();
-  if (st == SF_OK) st = set_smem_attr<TcCfg<128, 6, FMT, false>>();
-  if (st == SF_OK) st = set_smem_attr<TcCfg<256, 4, FMT, false>>();
+  int32_t st = set_smem_attr<TcCfg<16, tc_stages<16>(), FMT, false>>();
+  if (st == SF_OK) st = set_smem_attr<TcCfg<32, tc_stages<32>(), FMT, false>>();
+  if (st == SF_OK) st = set_smem_attr<TcCfg<64, tc_stages<64>(), FMT, false>>();
+  if (st == SF_OK) st = set_smem_attr<TcCfg<128, tc_stages<128>(), FMT, false>>();
+  if (st == SF_OK) st = set_smem_attr<TcCfg<256, tc_stages<256>(), FMT, false>>();
   return st;
 }
 
@@ -131,16 +131,16 @@ int32_t encode_rows(CUtensorMap* m, const void* base, int dtype, uint64_t K, uin
 template <int FMT>
 int32_t launch(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a, int grid,
                cudaStream_t s) {
-#define SF_NOALLOC_LAUNCH(BN, ST)                                                          \
-  gemm_tc_kernel<TcCfg<BN, ST, FMT, false>><<<grid, TcCfg<BN, ST, FMT, false>::THREADS,    \
-                                              TcCfg<BN, ST, FMT, false>::SMEM_BYTES, s>>>( \
-      ma, mb, a)
+#define SF_NOALLOC_LAUNCH(BN)                                                               \
+  gemm_tc_kernel<TcCfg<BN, tc_stages<BN>(), FMT, false>>                                      \
+      <<<grid, TcCfg<BN, tc_stages<BN>(), FMT, false>::THREADS,                              \
+         TcCfg<BN, tc_stages<BN>(), FMT, false>::SMEM_BYTES, s>>>(ma, mb, ma, a)
   switch (bn) {
-    case 16: SF_NOALLOC_LAUNCH(16, 12); break;
-    case 32: SF_NOALLOC_LAUNCH(32, 10); break;
-    case 64: SF_NOALLOC_LAUNCH(64, 8); break;
-    case 128: SF_NOALLOC_LAUNCH(128, 6); break;
-    case 256: SF_NOALLOC_LAUNCH(256, 4); break;
+    case 16: SF_NOALLOC_LAUNCH(16); break;
+    case 32: SF_NOALLOC_LAUNCH(32); break;
+    case 64: SF_NOALLOC_LAUNCH(64); break;
+    case 128: SF_NOALLOC_LAUNCH(128); break;
+    case 256: SF_NOALLOC_LAUNCH(256); break;
     default: return fail(SF_ERR_UNSUPPORTED, "tile width %d", bn);
   }
 #undef SF_NOALLOC_LAUNCH
@@ -232,6 +232,7 @@ extern "C" int32_t sf_linear_skinny_noalloc(int64_t M, int64_t N, int64_t K, con
   a.ldc = ldy;
   a.c_trans = 1;
   a.vec_ok = 0;
+  a.tma_store = 0;  // transposed (swap-AB) output: per-thread stores
   a.epi = e;
   a.err = d->err;
   const int grid = static_cast<int>(std::min<int64_t>(tiles * splits, d->sm_count));
