@@ -236,6 +236,15 @@ int32_t sf_event_record(void* event, void* stream);
 int32_t sf_event_synchronize(void* event);
 int32_t sf_event_elapsed_ms(void* start, void* end, float* ms);
 
+/* CUDA graphs: capture the launches issued on `stream` between begin and end
+ * (relaxed capture mode) into an executable graph, then replay it.  For
+ * launch-bound sequences such as skinny-M GEMMs.  New (the reference has no
+ * graph support).  Workspaces must already be sized before capture. */
+int32_t sf_graph_begin(void* stream);
+int32_t sf_graph_end(void* stream, void** exec);
+int32_t sf_graph_launch(void* exec, void* stream);
+int32_t sf_graph_destroy(void* exec);
+
 /* Peer access (_cuda_ops.pyx:550-587). */
 int32_t sf_can_access_peer(int32_t device, int32_t peer, int32_t* can);
 int32_t sf_enable_peer_access_all(void);

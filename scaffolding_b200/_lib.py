@@ -103,6 +103,10 @@ SIGNATURES: dict[str, list] = {
     "sf_event_record": [_vp, _vp],
     "sf_event_synchronize": [_vp],
     "sf_event_elapsed_ms": [_vp, _vp, _P(C.c_float)],
+    "sf_graph_begin": [_vp],
+    "sf_graph_end": [_vp, _P(_vp)],
+    "sf_graph_launch": [_vp, _vp],
+    "sf_graph_destroy": [_vp],
     "sf_can_access_peer": [_i32, _i32, _P(_i32)],
     "sf_enable_peer_access_all": [],
     "sf_device_error_status": [_i32, _P(_i32), _i32],

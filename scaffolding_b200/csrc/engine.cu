@@ -679,7 +679,16 @@ int32_t sf_softmax_rows(const void* x, int32_t x_dtype, int64_t ldx, void* y, in
                    (y_dtype == kF32 ? (aligned16(y) && ldy % 4 == 0)
                                     : ((reinterpret_cast<uintptr_t>(y) & 7u) == 0 && ldy % 4 == 0));
   const unsigned grid = static_cast<unsigned>(rows);
-  if (vec && nv <= int64_t(kSoftmaxThreads) * 16) {
+  const int variant = env_int("SF_SOFTMAX", 0);  // 0: streaming two-pass, 1: register-resident
+  if (vec && variant == 0) {
+    const float* xf = static_cast<const float*>(x);
+    if (y_dtype == kF32)
+      softmax_rows_online_kernel<false><<<grid, kSoftmaxOnlineThreads, 0, s>>>(
+          xf, ldx, y, y_dtype, ldy, static_cast<int>(cols), scale);
+    else
+      softmax_rows_online_kernel<true><<<grid, kSoftmaxOnlineThreads, 0, s>>>(
+          xf, ldx, y, y_dtype, ldy, static_cast<int>(cols), scale);
+  } else if (vec && nv <= int64_t(kSoftmaxThreads) * 16) {
     const int64_t vpt = ceil_div(nv, kSoftmaxThreads);
     const float* xf = static_cast<const float*>(x);
     const int c = static_cast<int>(cols);

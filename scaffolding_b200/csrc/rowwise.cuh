@@ -108,6 +108,96 @@ static __global__ void __launch_bounds__(kSoftmaxThreads)
   }
 }
 
+// Two-pass streaming softmax for long fp32 rows (cols % 4 == 0, aligned):
+// pass 1 streams the row once from HBM keeping a running (max, sum of exp)
+// pair per thread -- on a new maximum the sum is rescaled by exp(old - new) --
+// and reduces the pairs across the block; pass 2 re-reads the row (from L2)
+// and writes exp(x - max) / sum.  HBM sees one read and one write of the row
+// while each CTA holds no row in registers, so many rows are in flight per
+// SM.  The exponentials of pass 2 are the reference's exp(x - max) exactly;
+// only the sum's rounding order differs.  FAST (16-bit outputs) uses the
+// hardware exp2 intrinsic (__expf) and a reciprocal multiply.
+constexpr int kSoftmaxOnlineThreads = 256;
+
+template <bool FAST>
+__device__ __forceinline__ float sm_exp(float v) {
+  return FAST ? __expf(v) : expf(v);
+}
+
+template <bool FAST>
+__device__ __forceinline__ void sm_combine(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;  // both empty
+  const float a = (m == -INFINITY) ? 0.0f : s * sm_exp<FAST>(m - mn);
+  const float b = (m2 == -INFINITY) ? 0.0f : s2 * sm_exp<FAST>(m2 - mn);
+  m = mn;
+  s = a + b;
+}
+
+template <bool FAST>
+static __global__ void __launch_bounds__(kSoftmaxOnlineThreads)
+    softmax_rows_online_kernel(const float* __restrict__ x, int64_t ldx, void* __restrict__ y,
+                               int y_dtype, int64_t ldy, int cols, float scale) {
+  __shared__ float red_m[32], red_s[32];
+  __shared__ float fin[2];
+  const int64_t r = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
+  const int nv = cols >> 2;
+  float m = -INFINITY, s = 0.0f;
+#pragma unroll 4
+  for (int c = threadIdx.x; c < nv; c += kSoftmaxOnlineThreads) {
+    const float4 q = __ldcg(xr + c);
+    const float a = q.x * scale, b = q.y * scale, cc = q.z * scale, d = q.w * scale;
+    const float lm = fmaxf(fmaxf(a, b), fmaxf(cc, d));
+    if (lm > m) {
+      s = (m == -INFINITY) ? 0.0f : s * sm_exp<FAST>(m - lm);
+      m = lm;
+    }
+    s += (sm_exp<FAST>(a - m) + sm_exp<FAST>(b - m)) + (sm_exp<FAST>(cc - m) + sm_exp<FAST>(d - m));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    sm_combine<FAST>(m, s, m2, s2);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    red_m[w] = m;
+    red_s[w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    m = (l < kSoftmaxOnlineThreads / 32) ? red_m[l] : -INFINITY;
+    s = (l < kSoftmaxOnlineThreads / 32) ? red_s[l] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      sm_combine<FAST>(m, s, m2, s2);
+    }
+    if (l == 0) {
+      fin[0] = m;
+      fin[1] = s;
+    }
+  }
+  __syncthreads();
+  const float mx = fin[0], sum = fin[1];
+  const float inv = 1.0f / sum;
+#pragma unroll 4
+  for (int c = threadIdx.x; c < nv; c += kSoftmaxOnlineThreads) {
+    const float4 q = __ldcs(xr + c);
+    float e0 = sm_exp<FAST>(q.x * scale - mx), e1 = sm_exp<FAST>(q.y * scale - mx);
+    float e2 = sm_exp<FAST>(q.z * scale - mx), e3 = sm_exp<FAST>(q.w * scale - mx);
+    if (FAST) {
+      e0 *= inv; e1 *= inv; e2 *= inv; e3 *= inv;
+    } else {
+      e0 /= sum; e1 /= sum; e2 /= sum; e3 /= sum;
+    }
+    store4(y, r * ldy + 4 * (int64_t)c, y_dtype, e0, e1, e2, e3);
+  }
+}
+
 // General three-pass softmax (any cols, any alignment, any input dtype).
 static __global__ void __launch_bounds__(kSoftmaxThreads)
     softmax_rows_generic_kernel(const void* __restrict__ x, int x_dtype, int64_t ldx,

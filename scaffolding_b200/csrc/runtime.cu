@@ -377,6 +377,35 @@ int32_t sf_event_elapsed_ms(void* start, void* end, float* ms) {
   return SF_OK;
 }
 
+int32_t sf_graph_begin(void* stream) {
+  if (!stream) return fail(SF_ERR_INVALID_ARGUMENT, "graph capture needs a non-default stream");
+  SF_CUDA_TRY(cudaStreamBeginCapture(static_cast<cudaStream_t>(stream), cudaStreamCaptureModeRelaxed));
+  return SF_OK;
+}
+
+int32_t sf_graph_end(void* stream, void** exec) {
+  if (!stream || !exec) return fail(SF_ERR_INVALID_ARGUMENT, "null argument");
+  cudaGraph_t g = nullptr;
+  SF_CUDA_TRY(cudaStreamEndCapture(static_cast<cudaStream_t>(stream), &g));
+  cudaGraphExec_t e = nullptr;
+  cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  if (err != cudaSuccess) return cuda_status(err, "cudaGraphInstantiate");
+  *exec = e;
+  return SF_OK;
+}
+
+int32_t sf_graph_launch(void* exec, void* stream) {
+  if (!exec) return fail(SF_ERR_INVALID_ARGUMENT, "null graph");
+  SF_CUDA_TRY(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), static_cast<cudaStream_t>(stream)));
+  return SF_OK;
+}
+
+int32_t sf_graph_destroy(void* exec) {
+  if (exec) SF_CUDA_TRY(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec)));
+  return SF_OK;
+}
+
 int32_t sf_can_access_peer(int32_t device, int32_t peer, int32_t* can) {
   if (!can) return fail(SF_ERR_INVALID_ARGUMENT, "null output");
   int c = 0;
