@@ -229,3 +229,35 @@ def test_zero_k_gives_bias_only(gpu, ops):
 
 def test_no_device_errors_recorded(gpu):
     assert device_error(0) == 0
+
+
+def test_graph_capture_replays_gemm(gpu, ops):
+    """A GEMM captured into a CUDA graph and replayed gives the same result as
+    the direct launch (used for launch-bound skinny shapes)."""
+    import ctypes as C
+
+    from scaffolding_b200 import engine as E
+    from scaffolding_b200._lib import lib
+    rng = np.random.default_rng(77)
+    M, N, K = 8, 4096, 4096
+    ga, a = to_device(ops, _rand(rng, M, K), "bf16")
+    gb, b = to_device(ops, _rand(rng, N, K, scale=0.02), "bf16")
+    sp = C.c_void_p()
+    assert lib.sf_stream_create(0, 1, C.byref(sp)) == 0
+    s = sp.value
+    y1 = ops._alloc((M, N), np_dtype("bf16"), 0)
+    y2 = ops._alloc((M, N), np_dtype("bf16"), 0)
+    E.gemm(M, N, K, ga.ptr, K, 0, gb.ptr, K, 1, y1.ptr, N, 2, 2, stream=s)  # sizes the workspace
+    E.stream_sync(s)
+    g = C.c_void_p()
+    assert lib.sf_graph_begin(C.c_void_p(s)) == 0
+    E.gemm(M, N, K, ga.ptr, K, 0, gb.ptr, K, 1, y2.ptr, N, 2, 2, stream=s)
+    assert lib.sf_graph_end(C.c_void_p(s), C.byref(g)) == 0
+    for _ in range(3):
+        assert lib.sf_graph_launch(g, C.c_void_p(s)) == 0
+    E.stream_sync(s)
+    assert lib.sf_graph_destroy(g) == 0
+    lib.sf_stream_destroy(C.c_void_p(s))
+    r1, r2 = to_host32(ops, y1), to_host32(ops, y2)
+    assert_close_16bit(r2, O.matmul_nt(a, b), "graph replay")
+    assert_close_16bit(r1, r2, "direct vs graph")
