@@ -26,6 +26,7 @@
 #include "common.h"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemv.cuh"
 #include "rowwise.cuh"
 
 namespace sf {
@@ -118,7 +119,7 @@ struct Problem {
   cudaStream_t stream;
 };
 
-enum PlanKind { kPlanSimt, kPlanTc, kPlanTcSwap, kPlanTf32Split, kPlanTf32Direct };
+enum PlanKind { kPlanSimt, kPlanTc, kPlanTcSwap, kPlanTf32Split, kPlanTf32Direct, kPlanGemv };
 
 struct Plan {
   PlanKind kind = kPlanSimt;
@@ -200,6 +201,12 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     // dim) average thousands of small terms; keep them IEEE-accurate by
     // promoting TMEM partial sums into fp32 registers every 4 k-blocks.
     if (p.K >= kPromoteMinK && pl.bn <= 128) pl.promote = true;
+    return pl;
+  }
+  if (batch == 1 && p.M <= 4 && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
+      ovr != SF_KERNEL_TCGEN05 && env_int("SF_GEMV", 1)) {
+    // Decode-style shapes: a pure weight stream, served by the GEMV kernel.
+    pl.kind = kPlanGemv;
     return pl;
   }
   if (batch == 1 && p.M <= 256 && p.N >= 256) {
@@ -512,6 +519,42 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   return SF_OK;
 }
 
+template <int MM, int R>
+static void launch_gemv_mr(const Problem& p, const EpilogueArgs& e, cudaStream_t s) {
+  const int warps = static_cast<int>(ceil_div(p.N, R));
+  const int grid = static_cast<int>(ceil_div(warps, kGemvWarps));
+  const uint16_t* x = static_cast<const uint16_t*>(p.A);
+  const uint16_t* w = static_cast<const uint16_t*>(p.B);
+  if (p.in_dt == kBF16)
+    gemv_kernel<MM, R, true><<<grid, kGemvWarps * 32, 0, s>>>(
+        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
+  else
+    gemv_kernel<MM, R, false><<<grid, kGemvWarps * 32, 0, s>>>(
+        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
+}
+
+template <int MM>
+static void launch_gemv_m(const Problem& p, const EpilogueArgs& e, cudaStream_t s, int sm_count) {
+  // Four weight rows per warp when that still gives >= 2 CTAs per SM, else two.
+  if (ceil_div(p.N, 4 * kGemvWarps) >= 2 * sm_count)
+    launch_gemv_mr<MM, 4>(p, e, s);
+  else
+    launch_gemv_mr<MM, 2>(p, e, s);
+}
+
+static int32_t run_gemv(const Problem& p, const DeviceInfo& dev) {
+  const EpilogueArgs e = to_epi(p.epi, p.out_dt);
+  switch (p.M) {
+    case 1: launch_gemv_m<1>(p, e, p.stream, dev.sm_count); break;
+    case 2: launch_gemv_m<2>(p, e, p.stream, dev.sm_count); break;
+    case 3: launch_gemv_m<3>(p, e, p.stream, dev.sm_count); break;
+    case 4: launch_gemv_m<4>(p, e, p.stream, dev.sm_count); break;
+    default: return fail(SF_ERR_UNSUPPORTED, "GEMV path needs M <= 4");
+  }
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
 static int32_t validate(const Problem& p) {
   if (p.M < 0 || p.N < 0 || p.K < 0) return fail(SF_ERR_INVALID_ARGUMENT, "negative dimension");
   if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX)
@@ -566,6 +609,7 @@ static int32_t gemm_impl(Problem& p) {
   if (pl.ws_bytes > 0 && (p.ws == nullptr || p.ws_bytes < pl.ws_bytes))
     return fail(SF_ERR_WORKSPACE, "workspace of %zu bytes required (%zu given)", pl.ws_bytes,
                 p.ws ? p.ws_bytes : size_t(0));
+  if (pl.kind == kPlanGemv) return run_gemv(p, *dev);
   if (pl.kind == kPlanSimt) {
     if (kernel_override() == SF_KERNEL_TCGEN05)
       return fail(SF_ERR_UNSUPPORTED, "layout not supported by the tcgen05 kernel");

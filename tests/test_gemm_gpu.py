@@ -261,3 +261,24 @@ def test_graph_capture_replays_gemm(gpu, ops):
     r1, r2 = to_host32(ops, y1), to_host32(ops, y2)
     assert_close_16bit(r2, O.matmul_nt(a, b), "graph replay")
     assert_close_16bit(r1, r2, "direct vs graph")
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_gemv_small_m(gpu, ops, M, dt):
+    """M <= 4 runs on the warp-shuffle GEMV kernel: ragged N, bias + GELU and
+    a residual, against the oracle."""
+    from scaffolding_b200 import engine as E
+    rng = np.random.default_rng(90 + M)
+    N, K = 1003, 1024
+    gx, x = to_device(ops, _rand(rng, M, K), dt)
+    gw, w = to_device(ops, _rand(rng, N, K, scale=0.03), dt)
+    gb, b = to_device(ops, _rand(rng, N, scale=0.1), dt)
+    gr, res = to_device(ops, _rand(rng, M, N), dt)
+    out = ops._alloc((M, N), np_dtype(dt), 0)
+    code = E.dtype_code(np_dtype(dt))
+    epi = E.make_epilogue(bias_ptr=gb.ptr, bias_dt=code, act=2, residual_ptr=gr.ptr,
+                          residual_dt=code, ldr=N)
+    E.gemm(M, N, K, gx.ptr, K, 0, gw.ptr, K, 1, out.ptr, N, code, code, epi=epi)
+    ref = O.gelu_tanh(O.linear(x, w, b)) + res
+    assert_close_16bit(to_host32(ops, out), ref, f"gemv M={M} {dt}")
