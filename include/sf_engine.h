@@ -65,8 +65,9 @@ extern "C" {
 
 /* Kernel selection override (tuning / tests only; AUTO in production). */
 #define SF_KERNEL_AUTO 0
-#define SF_KERNEL_TCGEN05 1
+#define SF_KERNEL_TCGEN05 1      /* tensor-core kernels only (no GEMV) */
 #define SF_KERNEL_SIMT 2
+#define SF_KERNEL_TCGEN05_1CTA 3 /* tensor-core kernels without CTA pairs */
 
 /* Fused epilogue:  D = act(alpha * (op(A) . op(B)) + bias) + beta * R.
  * Replaces the separate bias-add (cuda_bias_add_row_f32,

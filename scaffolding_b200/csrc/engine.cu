@@ -26,6 +26,7 @@
 #include "common.h"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "gemv.cuh"
 #include "rowwise.cuh"
 
@@ -127,6 +128,7 @@ struct Plan {
   bool b_mn = false;
   int splits = 1;
   bool promote = false; // fp32-accurate: chunked TMEM accumulation promoted to registers
+  bool pair = false;    // 2-CTA cluster (cta_group::2) kernel, 256-row pair tiles
   int64_t kk = 0;       // reduction length seen by the TC kernel (3K for 3xTF32)
   int64_t ld_split = 0; // leading dimension of the split panels
   size_t ws_bytes = 0;
@@ -204,7 +206,7 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     return pl;
   }
   if (batch == 1 && p.M <= 4 && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
-      ovr != SF_KERNEL_TCGEN05 && env_int("SF_GEMV", 1)) {
+      ovr != SF_KERNEL_TCGEN05 && ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_GEMV", 1)) {
     // Decode-style shapes: a pure weight stream, served by the GEMV kernel.
     pl.kind = kPlanGemv;
     return pl;
@@ -230,6 +232,15 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   if (pl.bn < 64 && p.M > 4096) pl.bn = 64;
   const int forced = env_int("SF_TILE_N", 0);  // tuning knob
   if (forced == 64 || forced == 128 || forced == 192 || forced == 256) pl.bn = forced;
+  // CTA pairs over 256-row tiles: a third less operand traffic per SM than
+  // 1-CTA 128-row tiles.  Measured on B200 they win only for wide (BN = 256),
+  // tall GEMMs (the DiT FFN-up shape); elsewhere the 1-CTA kernel is as fast
+  // or faster, so AUTO picks pairs for that class only.  SF_PAIR=1 forces
+  // pairs for every eligible GEMM, SF_PAIR=0 disables them.
+  if (pl.bn >= 128 && p.M >= 1024 && p.K >= 256 && ovr != SF_KERNEL_TCGEN05_1CTA) {
+    const int knob = env_int("SF_PAIR", -1);
+    if (knob == 1 || (knob < 0 && pl.bn == 256 && p.N >= 4096 && p.M >= 16384)) pl.pair = true;
+  }
   return pl;
 }
 
@@ -337,6 +348,58 @@ static int32_t dispatch_tc(int fmt, bool bmn, bool promote, int bn, const CUtens
                  : launch_tc<2, false, 0>(bn, ma, mb, a, grid, s, device);
 }
 
+// CTA-pair launch: clusters of 2 along x, one cluster per SM pair, persistent
+// over the pair tiles.  The number of co-resident clusters comes from the
+// occupancy calculator (SMs that cannot host a whole pair stay idle).
+template <class Cfg>
+static int32_t launch_tc2_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const GemmTcArgs& a,
+                              int64_t tiles, cudaStream_t s, int device) {
+  static int max_clusters[64] = {0};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (device >= 64) return fail(SF_ERR_UNSUPPORTED, "device index %d", device);
+  if (max_clusters[device] == 0) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(gemm_tc2_kernel<Cfg>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    cfg.gridDim = dim3(2, 1, 1);
+    int n = 0;
+    SF_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<Cfg>, &cfg));
+    if (n < 1) return fail(SF_ERR_UNSUPPORTED, "no co-resident CTA pair for this kernel");
+    max_clusters[device] = n;
+  }
+  const int64_t clusters = std::min<int64_t>(tiles, max_clusters[device]);
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  SF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<Cfg>, ma, mb, t_map_c, a));
+  return SF_OK;
+}
+
+template <int FMT>
+static int32_t launch_tc2(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                          const GemmTcArgs& a, int64_t tiles, cudaStream_t s, int device) {
+  switch (bn) {
+    case 128: return launch_tc2_cfg<Tc2Cfg<128, tc2_stages<128>(), FMT>>(ma, mb, a, tiles, s, device);
+    case 192: return launch_tc2_cfg<Tc2Cfg<192, tc2_stages<192>(), FMT>>(ma, mb, a, tiles, s, device);
+    case 256: return launch_tc2_cfg<Tc2Cfg<256, tc2_stages<256>(), FMT>>(ma, mb, a, tiles, s, device);
+    default: return fail(SF_ERR_UNSUPPORTED, "pair tile width %d", bn);
+  }
+}
+
+static int32_t dispatch_tc2(int fmt, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                            const GemmTcArgs& a, int64_t tiles, cudaStream_t s, int device) {
+  if (fmt == kBF16) return launch_tc2<1>(bn, ma, mb, a, tiles, s, device);
+  if (fmt == kF16) return launch_tc2<0>(bn, ma, mb, a, tiles, s, device);
+  return fail(SF_ERR_UNSUPPORTED, "pair kernel needs 16-bit operands");
+}
+
 static int grid_for(int64_t n, int sm_count) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), sm_count * 8LL)));
 }
@@ -437,7 +500,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   } else {
     MapSpec sb{tb_ptr, es, tma_dtype(fmt), static_cast<uint64_t>(kk), static_cast<uint64_t>(tN),
                static_cast<uint64_t>(p.nb0), static_cast<uint64_t>(p.nb1), tb_ld, tb_s0, tb_s1,
-               static_cast<uint32_t>(bk), static_cast<uint32_t>(pl.bn)};
+               static_cast<uint32_t>(bk), static_cast<uint32_t>(pl.pair ? pl.bn / 2 : pl.bn)};
     st = encode_map(&mbm, sb);
   }
   if (st != SF_OK) return st;
@@ -448,7 +511,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   a.K = static_cast<int>(kk);
   a.nb0 = static_cast<int>(p.nb0);
   a.nb1 = static_cast<int>(p.nb1);
-  a.m_tiles = static_cast<int>(ceil_div(tM, 128));
+  a.m_tiles = static_cast<int>(ceil_div(tM, pl.pair ? 256 : 128));
   a.n_tiles = static_cast<int>(ceil_div(tN, pl.bn));
   a.k_blocks = static_cast<int>(ceil_div(kk, bk));
   const int64_t total = int64_t(a.m_tiles) * a.n_tiles * p.nb0 * p.nb1;
@@ -472,6 +535,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   a.ldw = 0;
   a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
+  a.epi_sleep_ns = env_int("SF_EPI_SLEEP", 0);  // tuning knob
   a.tma_store = 0;
   memset(&t_map_c, 0, sizeof(t_map_c));
   if (!swap && pl.splits == 1 && a.vec_ok && env_int("SF_TMA_STORE", 1)) {
@@ -507,6 +571,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
     SF_CUDA_TRY(cudaMemsetAsync(p.ws, 0, static_cast<size_t>(p.M) * p.N * 4u, p.stream));
   }
   const int64_t units = total * pl.splits;
+  if (pl.pair) return dispatch_tc2(fmt, pl.bn, ma, mbm, a, total, p.stream, device);
   const int grid = static_cast<int>(std::min<int64_t>(units, dev.sm_count));
   st = dispatch_tc(fmt, pl.b_mn, pl.promote, pl.bn, ma, mbm, a, grid, p.stream, device);
   if (st != SF_OK) return st;

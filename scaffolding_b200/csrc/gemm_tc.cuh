@@ -71,6 +71,7 @@ struct GemmTcArgs {
   int64_t ldw;
   EpilogueArgs epi;
   int* err;             // device error word
+  int epi_sleep_ns;     // poll back-off of the epilogue's accumulator waits (0 = spin)
 };
 
 template <int BN_, int STAGES_, int FMT_, bool B_MN_, int PROMOTE_KB_ = 0>
@@ -521,7 +522,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       tile_coords(tile, p, mb, nb, b0, b1);
       const int i = mb * BM + row;
       if constexpr (PKB == 0) {
-        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) break;
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, p.epi_sleep_ns)) break;
         tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                static_cast<uint32_t>(acc * Cfg::ACC_COLS);
@@ -555,7 +556,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kc = kb0; kc < kb1; kc += PKB) {
-          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) {
+          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, p.epi_sleep_ns)) {
             ok = false;
             break;
           }

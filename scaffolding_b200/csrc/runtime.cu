@@ -132,7 +132,7 @@ int32_t sf_get_fp32_mode(int32_t* mode) {
   return SF_OK;
 }
 int32_t sf_set_kernel_override(int32_t kernel) {
-  if (kernel < SF_KERNEL_AUTO || kernel > SF_KERNEL_SIMT)
+  if (kernel < SF_KERNEL_AUTO || kernel > SF_KERNEL_TCGEN05_1CTA)
     return fail(SF_ERR_INVALID_ARGUMENT, "unknown kernel override %d", kernel);
   g_kernel_override = kernel;
   return SF_OK;

@@ -282,3 +282,55 @@ def test_gemv_small_m(gpu, ops, M, dt):
     E.gemm(M, N, K, gx.ptr, K, 0, gw.ptr, K, 1, out.ptr, N, code, code, epi=epi)
     ref = O.gelu_tanh(O.linear(x, w, b)) + res
     assert_close_16bit(to_host32(ops, out), ref, f"gemv M={M} {dt}")
+
+
+# M >= 1024, K >= 256, N > 64: the CTA-pair (cta_group::2) kernel.  Ragged M
+# (not a multiple of the 256-row pair tile), ragged N and K, and both
+# pair tile widths.
+PAIR_SHAPES = [(1024, 256, 256), (1100, 1000, 300), (2048, 1920, 1920), (1536, 384, 512),
+               (1280, 200, 264), (1030, 5760, 640)]
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_pair_kernel_nt(gpu, ops, dt, M, N, K, monkeypatch):
+    rng = np.random.default_rng(M + 5 * N + 11 * K)
+    ga, a = to_device(ops, _rand(rng, M, K), dt)
+    gb, b = to_device(ops, _rand(rng, N, K), dt)
+    monkeypatch.setenv("SF_PAIR", "1")  # every eligible GEMM on the pair kernel
+    pair = to_host32(ops, ops.dev_matmul_nt(ga, gb))
+    monkeypatch.delenv("SF_PAIR")
+    kernel_override(3)  # SF_KERNEL_TCGEN05_1CTA
+    try:
+        single = to_host32(ops, ops.dev_matmul_nt(ga, gb))
+    finally:
+        kernel_override(0)
+    ref = O.matmul_nt(a, b)
+    assert_close_16bit(pair, ref, f"pair {dt} {M}x{N}x{K}")
+    assert_close_16bit(single, ref, f"1-CTA {dt} {M}x{N}x{K}")
+    assert device_error(0) == 0
+
+
+def test_pair_kernel_fused_epilogue_and_batch(gpu, ops, monkeypatch):
+    """Bias + GELU + scaled residual on the pair kernel, and a batched pair GEMM."""
+    from scaffolding_b200 import engine as E
+    monkeypatch.setenv("SF_PAIR", "1")
+    rng = np.random.default_rng(123)
+    M, N, K = 1300, 768, 384
+    gx, x = to_device(ops, _rand(rng, M, K), "bf16")
+    gw, w = to_device(ops, _rand(rng, N, K, scale=0.05), "bf16")
+    gb, bias = to_device(ops, _rand(rng, N, scale=0.1), "bf16")
+    gr, res = to_device(ops, _rand(rng, M, N), "bf16")
+    out = ops._alloc((M, N), np_dtype("bf16"), 0)
+    epi = E.make_epilogue(alpha=0.5, bias_ptr=gb.ptr, bias_dt=2, act=2, residual_ptr=gr.ptr,
+                          residual_dt=2, ldr=N, beta=1.0)
+    E.gemm(M, N, K, gx.ptr, K, 0, gw.ptr, K, 1, out.ptr, N, 2, 2, epi=epi)
+    ref = O.gelu_tanh(0.5 * (x @ w.T) + bias) + res
+    assert_close_16bit(to_host32(ops, out), ref, "pair epilogue")
+
+    B = 3
+    ga, a = to_device(ops, _rand(rng, B, 1024, 256), "bf16")
+    gbb, bb = to_device(ops, _rand(rng, B, 320, 256), "bf16")
+    c = to_host32(ops, ops.dev_batched_matmul_nt(ga, gbb))
+    assert_close_16bit(c, O.batched_matmul_nt(a, bb), "pair batched")
+    assert device_error(0) == 0
