@@ -129,6 +129,7 @@ struct Plan {
   int splits = 1;
   bool promote = false; // fp32-accurate: chunked TMEM accumulation promoted to registers
   bool pair = false;    // 2-CTA cluster (cta_group::2) kernel, 256-row pair tiles
+  int a_box_rows = 128; // pair kernel: rows per A box (fewer for skinny M)
   int64_t kk = 0;       // reduction length seen by the TC kernel (3K for 3xTF32)
   int64_t ld_split = 0; // leading dimension of the split panels
   size_t ws_bytes = 0;
@@ -147,6 +148,26 @@ static int pick_bn(int64_t n) {
   const int64_t w256 = ceil_div(n, 256) * 256 - n;
   const int64_t w192 = ceil_div(n, 192) * 192 - n;
   return w192 < w256 ? 192 : 256;
+}
+
+// Skinny pair GEMMs (M <= 256: one 256-row pair tile holds every activation
+// row, so each weight byte is read once): the pair tile width whose tile
+// count best fills the SM pairs, counting column padding as waste.
+static int pick_bn_pair_skinny(int64_t n, int clusters) {
+  static const int kCand[] = {64, 96, 128, 160, 192, 256};
+  int best = 256;
+  double best_eff = -1.0;
+  for (int bn : kCand) {
+    const int64_t tiles = ceil_div(n, bn);
+    const int64_t rounds = ceil_div(tiles, clusters);
+    const double eff = static_cast<double>(tiles) / static_cast<double>(rounds * clusters) *
+                       static_cast<double>(n) / static_cast<double>(tiles * bn);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
 }
 
 // Reduction length from which narrow 16-bit GEMMs promote their accumulators.
@@ -205,10 +226,28 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     if (p.K >= kPromoteMinK && pl.bn <= 128) pl.promote = true;
     return pl;
   }
-  if (batch == 1 && p.M <= 4 && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
+  // M <= 4 always; up to SF_GEMV_MAX_M (<= 8) on the balanced kernel (K % 256 == 0).
+  const int gemv_max_m = (p.K % 256 == 0 && env_int("SF_GEMV_SEG", 1))
+                             ? std::min(8, env_int("SF_GEMV_MAX_M", 4))
+                             : 4;
+  if (batch == 1 && p.M <= gemv_max_m && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
       ovr != SF_KERNEL_TCGEN05 && ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_GEMV", 1)) {
     // Decode-style shapes: a pure weight stream, served by the GEMV kernel.
     pl.kind = kPlanGemv;
+    return pl;
+  }
+  // Skinny M on B200 (graph-replayed, K = 4096): M <= 32 is fastest on the
+  // swap-AB kernel (weights fill the 128-row MMA side), M = 33..256 on CTA
+  // pairs holding every activation row in one pair tile.
+  const int pair_min_m = env_int("SF_SKINNY_PAIR_MIN_M", 33);
+  if (batch == 1 && p.M <= 256 && p.M >= pair_min_m && p.N >= 1024 && p.K >= 64 &&
+      ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_SKINNY_PAIR", 1)) {
+    // Skinny M on CTA pairs: activations = A (one pair tile), weights = B
+    // split into ~one tile per SM pair.
+    pl.kind = kPlanTc;
+    pl.pair = true;
+    pl.bn = pick_bn_pair_skinny(p.N, std::max(1, sm_count / 2));
+    pl.a_box_rows = static_cast<int>(std::min<int64_t>(128, (p.M + 7) / 8 * 8));
     return pl;
   }
   if (batch == 1 && p.M <= 256 && p.N >= 256) {
@@ -386,7 +425,10 @@ template <int FMT>
 static int32_t launch_tc2(int bn, const CUtensorMap& ma, const CUtensorMap& mb,
                           const GemmTcArgs& a, int64_t tiles, cudaStream_t s, int device) {
   switch (bn) {
+    case 64: return launch_tc2_cfg<Tc2Cfg<64, tc2_stages<64>(), FMT>>(ma, mb, a, tiles, s, device);
+    case 96: return launch_tc2_cfg<Tc2Cfg<96, tc2_stages<96>(), FMT>>(ma, mb, a, tiles, s, device);
     case 128: return launch_tc2_cfg<Tc2Cfg<128, tc2_stages<128>(), FMT>>(ma, mb, a, tiles, s, device);
+    case 160: return launch_tc2_cfg<Tc2Cfg<160, tc2_stages<160>(), FMT>>(ma, mb, a, tiles, s, device);
     case 192: return launch_tc2_cfg<Tc2Cfg<192, tc2_stages<192>(), FMT>>(ma, mb, a, tiles, s, device);
     case 256: return launch_tc2_cfg<Tc2Cfg<256, tc2_stages<256>(), FMT>>(ma, mb, a, tiles, s, device);
     default: return fail(SF_ERR_UNSUPPORTED, "pair tile width %d", bn);
@@ -489,7 +531,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   CUtensorMap ma, mbm;
   MapSpec sa{ta_ptr, es, tma_dtype(fmt), static_cast<uint64_t>(kk), static_cast<uint64_t>(tM),
              static_cast<uint64_t>(p.nb0), static_cast<uint64_t>(p.nb1), ta_ld, ta_s0, ta_s1,
-             static_cast<uint32_t>(bk), 128u};
+             static_cast<uint32_t>(bk), static_cast<uint32_t>(pl.pair ? pl.a_box_rows : 128)};
   int32_t st = encode_map(&ma, sa);
   if (st != SF_OK) return st;
   if (pl.b_mn) {
@@ -536,6 +578,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
   a.epi_sleep_ns = env_int("SF_EPI_SLEEP", 0);  // tuning knob
+  a.a_box_rows = pl.pair ? pl.a_box_rows : 128;
   a.tma_store = 0;
   memset(&t_map_c, 0, sizeof(t_map_c));
   if (!swap && pl.splits == 1 && a.vec_ok && env_int("SF_TMA_STORE", 1)) {
@@ -607,14 +650,54 @@ static void launch_gemv_m(const Problem& p, const EpilogueArgs& e, cudaStream_t 
     launch_gemv_mr<MM, 2>(p, e, s);
 }
 
+// Balanced GEMV: one CTA per SM, contiguous row ranges (shared-memory row sums
+// of ceil(N/G) x M floats; the grid grows past one CTA per SM only when
+// that would exceed 48 KB).
+template <int MM, int R, int U>
+static int32_t launch_gemv_seg(const Problem& p, const EpilogueArgs& e, int sm_count) {
+  int64_t G = sm_count;
+  const int64_t max_rows = (48 * 1024) / (MM * 4);
+  if (ceil_div(p.N, G) > max_rows) G = ceil_div(p.N, max_rows);
+  G = std::min<int64_t>(G, p.N);
+  const size_t smem = static_cast<size_t>(ceil_div(p.N, G)) * MM * 4;
+  const uint16_t* x = static_cast<const uint16_t*>(p.A);
+  const uint16_t* w = static_cast<const uint16_t*>(p.B);
+  const int grid = static_cast<int>(G);
+  if (p.in_dt == kBF16)
+    gemv_seg_kernel<MM, R, U, true><<<grid, kSegWarps * 32, smem, p.stream>>>(
+        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
+  else
+    gemv_seg_kernel<MM, R, U, false><<<grid, kSegWarps * 32, smem, p.stream>>>(
+        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}
+
+static bool gemv_seg_ok(const Problem& p) {
+  return p.K % 256 == 0 && aligned16(p.A) && aligned16(p.B) && env_int("SF_GEMV_SEG", 1);
+}
+
 static int32_t run_gemv(const Problem& p, const DeviceInfo& dev) {
   const EpilogueArgs e = to_epi(p.epi, p.out_dt);
+  if (gemv_seg_ok(p)) {
+    switch (p.M) {
+      case 1: return launch_gemv_seg<1, 4, 4>(p, e, dev.sm_count);
+      case 2: return launch_gemv_seg<2, 4, 4>(p, e, dev.sm_count);
+      case 3: return launch_gemv_seg<3, 4, 2>(p, e, dev.sm_count);
+      case 4: return launch_gemv_seg<4, 4, 2>(p, e, dev.sm_count);
+      case 5: return launch_gemv_seg<5, 2, 2>(p, e, dev.sm_count);
+      case 6: return launch_gemv_seg<6, 2, 2>(p, e, dev.sm_count);
+      case 7: return launch_gemv_seg<7, 2, 2>(p, e, dev.sm_count);
+      case 8: return launch_gemv_seg<8, 2, 2>(p, e, dev.sm_count);
+      default: return fail(SF_ERR_UNSUPPORTED, "GEMV path needs M <= 8");
+    }
+  }
   switch (p.M) {
     case 1: launch_gemv_m<1>(p, e, p.stream, dev.sm_count); break;
     case 2: launch_gemv_m<2>(p, e, p.stream, dev.sm_count); break;
     case 3: launch_gemv_m<3>(p, e, p.stream, dev.sm_count); break;
     case 4: launch_gemv_m<4>(p, e, p.stream, dev.sm_count); break;
-    default: return fail(SF_ERR_UNSUPPORTED, "GEMV path needs M <= 4");
+    default: return fail(SF_ERR_UNSUPPORTED, "row-per-warp GEMV path needs M <= 4");
   }
   SF_CUDA_TRY(cudaGetLastError());
   return SF_OK;

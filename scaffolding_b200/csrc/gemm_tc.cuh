@@ -72,6 +72,25 @@ struct GemmTcArgs {
   EpilogueArgs epi;
   int* err;             // device error word
   int epi_sleep_ns;     // poll back-off of the epilogue's accumulator waits (0 = spin)
+  int a_box_rows;       // pair kernel: rows per A box (128, or fewer for skinny M)
+};
+
+// Work units of one CTA as (tile, k-block range [kb0, kb1)): unit
+// u = blockIdx.x + i * gridDim.x over total_tiles * k_splits (k_splits > 1:
+// split-K slices of a tile).
+struct WorkIter {
+  int u, units;
+  __device__ __forceinline__ explicit WorkIter(const GemmTcArgs& p)
+      : u(blockIdx.x), units(p.total_tiles * p.k_splits) {}
+  __device__ __forceinline__ bool next(const GemmTcArgs& p, int& tile, int& kb0, int& kb1) {
+    if (u >= units) return false;
+    tile = u / p.k_splits;
+    const int split = u - tile * p.k_splits;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+    u += gridDim.x;
+    return true;
+  }
 };
 
 template <int BN_, int STAGES_, int FMT_, bool B_MN_, int PROMOTE_KB_ = 0>
@@ -389,8 +408,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   const uint32_t tmem_base = tmem_slot;
   volatile int* abortp = &abort_flag;
 
-  const int units = p.total_tiles * p.k_splits;
-
   if (warp == 0) {
     // ───────────── TMA producer ─────────────
     if (lane == 0) {
@@ -398,12 +415,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int tile = u / p.k_splits, split = u - (u / p.k_splits) * p.k_splits;
+      WorkIter it(p);
+      int tile, kb0, kb1;
+      while (ok && it.next(p, tile, kb0, kb1)) {
         int mb, nb, b0, b1;
         tile_coords(tile, p, mb, nb, b0, b1);
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
             ok = false;
@@ -453,10 +469,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int split = u - (u / p.k_splits) * p.k_splits;
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+      WorkIter it(p);
+      int tile, kb0, kb1;
+      while (ok && it.next(p, tile, kb0, kb1)) {
         const int chunk = PKB > 0 ? PKB : max(kb1 - kb0, 1);
         for (int kc = kb0; kc < kb1 && ok; kc += chunk) {
           const int kce = min(kb1, kc + chunk);
@@ -516,19 +531,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const int tile = u / p.k_splits;
+    WorkIter it(p);
+    int tile, kb0, kb1;
+    while (ok && it.next(p, tile, kb0, kb1)) {
       int mb, nb, b0, b1;
       tile_coords(tile, p, mb, nb, b0, b1);
       const int i = mb * BM + row;
+      // Warp-uniform: does any row of this warp's 32-row quadrant exist?
+      const bool rows_live = mb * BM + quad * 32 < p.M;
       if constexpr (PKB == 0) {
-        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, p.epi_sleep_ns)) break;
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs,
+                       p.epi_sleep_ns))
+          break;
         tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                static_cast<uint32_t>(acc * Cfg::ACC_COLS);
 #pragma unroll 1
-        // Warp-uniform: does any row of this warp's 32-row quadrant exist?
-        const bool rows_live = mb * BM + quad * 32 < p.M;
         for (int c = half * CH; c < BN; c += 2 * CH) {
           float v[CH];
           tmem_load_chunk<CH>(tbase + c, v);
@@ -552,11 +570,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         float racc[OWN];
 #pragma unroll
         for (int t = 0; t < OWN; ++t) racc[t] = 0.0f;
-        const int split = u - tile * p.k_splits;
-        const int kb0 = split * p.kb_per_split;
-        const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
         for (int kc = kb0; kc < kb1; kc += PKB) {
-          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, p.epi_sleep_ns)) {
+          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp,
+                         kWaitLimitNs, p.epi_sleep_ns)) {
             ok = false;
             break;
           }
@@ -578,8 +594,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           }
         }
         if (!ok) break;
-#pragma unroll
-        const bool rows_live = mb * BM + quad * 32 < p.M;
         for (int q = 0; q < OWN / CH; ++q) {
           const int j0 = nb * BN + half * CH + q * 2 * CH;
           if (j0 < p.N && rows_live) {

@@ -57,15 +57,18 @@ struct Tc2Cfg {
   static constexpr int THREADS = 64 + EPI_WARPS * 32;
   static constexpr int CH = 32;
   static_assert(FMT == 0 || FMT == 1, "16-bit operands");
-  static_assert(BN % 64 == 0 && BN >= 128 && BN <= 256, "pair tile width");
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair tile width");
   static_assert(BN_HALF % 8 == 0, "B half is whole 8-row swizzle atoms");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-// Operand-ring depth per pair tile width (per-CTA stage = 16 KB + BN/2 rows).
+// Operand-ring depth per pair tile width: as many stages of 16 KB + BN/2 rows
+// as fit next to the 32 KB of epilogue staging (at most 12).
 template <int BN>
 constexpr int tc2_stages() {
-  return BN >= 256 ? 6 : BN >= 192 ? 6 : 8;
+  constexpr int stage = 128 * 128 + (BN / 2) * 128;
+  constexpr int n = (227 * 1024 - 8 * 4096 - 1024 - 512) / stage;
+  return n > 12 ? 12 : n;
 }
 
 template <class Cfg>
@@ -137,6 +140,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         tile_coords(u, p, mb, nb, b0, b1);
         const int arow = mb * Cfg::PAIR_M + static_cast<int>(rank) * BM;
         const int brow = nb * BN + static_cast<int>(rank) * Cfg::BN_HALF;
+        // A boxes of a_box_rows rows; a CTA whose 128 rows lie wholly past M
+        // loads no A (its accumulator rows are never stored, so the stale
+        // shared memory it multiplies is harmless).
+        const bool load_a = arow < p.M;
+        const uint32_t a_bytes = static_cast<uint32_t>(p.a_box_rows) * 128u;
+        const int base = mb * Cfg::PAIR_M;
+        const uint32_t tx_bytes = (base < p.M ? a_bytes : 0u) + (base + BM < p.M ? a_bytes : 0u) +
+                                  2u * static_cast<uint32_t>(Cfg::B_BYTES);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
             ok = false;
@@ -144,9 +155,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           }
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
           const uint32_t fb = full0 + static_cast<uint32_t>(stage * 8);
-          tma_load_4d_pair(sa, &tmA, fb, kb * BK, arow, b0, b1);
+          if (load_a) tma_load_4d_pair(sa, &tmA, fb, kb * BK, arow, b0, b1);
           tma_load_4d_pair(sb, &tmB, fb, kb * BK, brow, b0, b1);
           ++issued;
           if (++stage == STAGES) {

@@ -113,4 +113,116 @@ static __global__ void __launch_bounds__(kGemvWarps * 32)
     }
 }
 
+// ───────────────────────── balanced (segmented) GEMV ─────────────────────────
+//
+// One CTA of kSegWarps warps per SM.  CTA c owns the contiguous weight rows
+// [c*N/G, (c+1)*N/G) (G = grid size), so every SM streams the same number
+// of bytes to within one row.  Inside the CTA the work is cut into units of
+// (group of R rows) x (512-byte column step); warp w takes the contiguous
+// unit range [w*U/W, (w+1)*U/W), so warps are balanced to one unit instead of
+// one row.  A warp folds each finished row group into per-row fp32 sums in
+// shared memory (warp butterfly + one shared atomic per row and activation
+// row); after a CTA barrier the fused epilogue writes the CTA's outputs.
+// Requires K % 256 == 0 and 16-byte aligned rows of x and W.
+constexpr int kSegWarps = 16;
+
+template <int MM, int R, int U, bool BF16>
+static __global__ void __launch_bounds__(kSegWarps * 32, 1)
+    gemv_seg_kernel(const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ W,
+                    int64_t ldw, void* __restrict__ y, int out_dtype, int64_t ldy, int N, int K,
+                    EpilogueArgs e) {
+  extern __shared__ float sacc[];  // [rows of this CTA][MM]
+  const int G = gridDim.x;
+  const int r0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * N / G);
+  const int r1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * N / G);
+  const int rows = r1 - r0;
+  for (int t = threadIdx.x; t < rows * MM; t += blockDim.x) sacc[t] = 0.0f;
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int spr = K >> 8;                       // 512-byte steps per row
+  const int groups = (rows + R - 1) / R;
+  const int total = groups * spr;
+  const int u0 = static_cast<int>(static_cast<int64_t>(warp) * total / kSegWarps);
+  const int u1 = static_cast<int>(static_cast<int64_t>(warp + 1) * total / kSegWarps);
+
+  float acc[R][MM];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < MM; ++m) acc[r][m] = 0.0f;
+
+  auto flush = [&](int g) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int m = 0; m < MM; ++m) {
+        float v = acc[r][m];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r][m] = 0.0f;
+        const int row = g * R + r;
+        if (lane == 0 && row < rows) atomicAdd(&sacc[row * MM + m], v);
+      }
+  };
+
+  int cur_g = u0 < u1 ? u0 / spr : 0;
+  for (int u = u0; u < u1; u += U) {
+    uint4 wv[U][R];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int uu = u + j;
+      const int g = uu / spr;
+      const int col = (uu - g * spr) * 32 + lane;  // 16-byte chunk index within the row
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int row = r0 + g * R + r;
+        wv[j][r] = (uu < u1 && row < r1)
+                       ? __ldcs(reinterpret_cast<const uint4*>(W + static_cast<int64_t>(row) * ldw) + col)
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int uu = u + j;
+      if (uu >= u1) break;  // warp-uniform
+      const int g = uu / spr;
+      if (g != cur_g) {     // warp-uniform
+        flush(cur_g);
+        cur_g = g;
+      }
+      const int col = (uu - g * spr) * 32 + lane;
+      float xf[MM][8];
+#pragma unroll
+      for (int m = 0; m < MM; ++m)
+        unpack8(__ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(m) * ldx) + col), BF16,
+                xf[m]);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float wf[8];
+        unpack8(wv[j][r], BF16, wf);
+#pragma unroll
+        for (int m = 0; m < MM; ++m)
+#pragma unroll
+          for (int t = 0; t < 8; ++t) acc[r][m] = fmaf(wf[t], xf[m][t], acc[r][m]);
+      }
+    }
+  }
+  if (u0 < u1) flush(cur_g);
+  __syncthreads();
+
+  // Epilogue: consecutive threads take consecutive output columns n.
+  for (int t = threadIdx.x; t < rows * MM; t += blockDim.x) {
+    const int m = t / rows;
+    const int rr = t - m * rows;
+    const int n = r0 + rr;
+    const float bias_v = e.bias ? load_as_f32(e.bias, n, e.bias_dtype) : 0.0f;
+    const float res_v =
+        e.residual ? load_as_f32(e.residual, static_cast<int64_t>(m) * e.ldr + n, e.residual_dtype) : 0.0f;
+    store_from_f32(y, static_cast<int64_t>(m) * ldy + n, out_dtype,
+                   epilogue_value(sacc[rr * MM + m], e, bias_v, res_v));
+  }
+}
+
 }  // namespace sf

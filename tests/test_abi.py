@@ -67,10 +67,18 @@ def test_workspace_sizes():
     assert ws(4096, 4096, 4096, 0, 1, 2) == 0
     # fp32 accurate (3xTF32): K-concatenated hi/lo panels for A and B
     assert ws(512, 4096, 1024, 0, 1, 0) == (512 + 4096) * 3 * 1024 * 4
-    # skinny bf16 with too few tiles: split-K fp32 accumulator
+    # skinny bf16, M <= 32: swap-AB; too few weight tiles -> split-K fp32 accumulator
     assert ws(8, 4096, 4096, 0, 1, 2) == 8 * 4096 * 4
-    # skinny with enough tiles: no split
+    # M = 33..256 on CTA pairs (one pair tile holds all M rows): no workspace
+    assert ws(64, 4096, 4096, 0, 1, 2) == 0
     assert ws(226, 11008, 4096, 0, 1, 2) == 0
+    # the same shapes on the swap-AB path
+    os.environ["SF_SKINNY_PAIR"] = "0"
+    try:
+        assert ws(64, 4096, 4096, 0, 1, 2) == 64 * 4096 * 4
+        assert ws(226, 11008, 4096, 0, 1, 2) == 0
+    finally:
+        del os.environ["SF_SKINNY_PAIR"]
 
 
 def test_fp32_mode_roundtrip():

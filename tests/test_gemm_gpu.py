@@ -60,10 +60,16 @@ def test_matmul_nn_16bit(gpu, ops, dt, M, N, K):
     assert_close_16bit(to_host32(ops, out), O.matmul(a, b), f"nn {dt} {M}x{N}x{K}")
 
 
+@pytest.mark.parametrize("path", ["pair", "swap"])
 @pytest.mark.parametrize("M", [1, 8, 64, 226])
 @pytest.mark.parametrize("N", [4096, 11008])
-def test_skinny_linear_bias_gelu(gpu, ops, M, N):
-    """Benchmark config 3: bf16 x[M,4096] W[N,4096] b[N], bias + GELU-tanh."""
+def test_skinny_linear_bias_gelu(gpu, ops, M, N, path, monkeypatch):
+    """Benchmark config 3: bf16 x[M,4096] W[N,4096] b[N], bias + GELU-tanh, on
+    the skinny CTA-pair path (default) and on the swap-AB path."""
+    if path == "swap":
+        monkeypatch.setenv("SF_SKINNY_PAIR", "0")
+    else:
+        monkeypatch.setenv("SF_SKINNY_PAIR_MIN_M", "5")  # M = 1 stays on the GEMV
     x, W, b = O.skinny_inputs(M, N, seed=M + N)
     bf = np_dtype("bf16")
     gx, gw, gb = (ops.gputensor_from_numpy(t.astype(bf)) for t in (x, W, b))
@@ -263,14 +269,17 @@ def test_graph_capture_replays_gemm(gpu, ops):
     assert_close_16bit(r1, r2, "direct vs graph")
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("K", [1024, 776])
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
-def test_gemv_small_m(gpu, ops, M, dt):
-    """M <= 4 runs on the warp-shuffle GEMV kernel: ragged N, bias + GELU and
-    a residual, against the oracle."""
+def test_gemv_small_m(gpu, ops, M, K, dt, monkeypatch):
+    """Small M runs on the GEMV kernels (balanced one for K % 256 == 0, up to
+    M = 8 here; row-per-warp one otherwise): ragged N, bias + GELU and a
+    residual, against the oracle."""
     from scaffolding_b200 import engine as E
-    rng = np.random.default_rng(90 + M)
-    N, K = 1003, 1024
+    monkeypatch.setenv("SF_GEMV_MAX_M", "8")
+    rng = np.random.default_rng(90 + M + K)
+    N = 1003
     gx, x = to_device(ops, _rand(rng, M, K), dt)
     gw, w = to_device(ops, _rand(rng, N, K, scale=0.03), dt)
     gb, b = to_device(ops, _rand(rng, N, scale=0.1), dt)
@@ -333,4 +342,40 @@ def test_pair_kernel_fused_epilogue_and_batch(gpu, ops, monkeypatch):
     gbb, bb = to_device(ops, _rand(rng, B, 320, 256), "bf16")
     c = to_host32(ops, ops.dev_batched_matmul_nt(ga, gbb))
     assert_close_16bit(c, O.batched_matmul_nt(a, bb), "pair batched")
+    assert device_error(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(5, 1024, 64), (17, 3000, 200), (128, 4100, 520), (129, 2048, 256),
+                                   (256, 1536, 1024), (200, 11008, 4096)])
+def test_skinny_pair_ragged(gpu, ops, M, N, K, monkeypatch):
+    """Skinny CTA-pair path: A boxes of round_up(M, 8) rows, the odd CTA idle
+    when M <= 128, ragged N tiles and K, fp16 and bf16."""
+    monkeypatch.setenv("SF_SKINNY_PAIR_MIN_M", "1")
+    for dt in ("bf16", "f16"):
+        rng = np.random.default_rng(M * 31 + N + K)
+        ga, a = to_device(ops, _rand(rng, M, K), dt)
+        gb, b = to_device(ops, _rand(rng, N, K, scale=0.05), dt)
+        out = to_host32(ops, ops.dev_matmul_nt(ga, gb))
+        assert_close_16bit(out, O.matmul_nt(a, b), f"skinny pair {dt} {M}x{N}x{K}")
+    assert device_error(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(8, 4096, 4096), (33, 1000, 777), (200, 3000, 1000), (5, 300, 4160),
+                                   (64, 11008, 4096)])
+def test_swap_ab_path(gpu, ops, M, N, K, monkeypatch):
+    """Swap-AB skinny GEMM (split-K where the weight tiles are too few), with
+    a bias + GELU + residual epilogue."""
+    from scaffolding_b200 import engine as E
+    monkeypatch.setenv("SF_SKINNY_PAIR", "0")
+    rng = np.random.default_rng(M * 3 + N + K)
+    gx, x = to_device(ops, _rand(rng, M, K), "bf16")
+    gw, w = to_device(ops, _rand(rng, N, K, scale=0.03), "bf16")
+    gb, b = to_device(ops, _rand(rng, N, scale=0.1), "bf16")
+    gr, res = to_device(ops, _rand(rng, M, N), "bf16")
+    out = ops._alloc((M, N), np_dtype("bf16"), 0)
+    epi = E.make_epilogue(bias_ptr=gb.ptr, bias_dt=2, act=2, residual_ptr=gr.ptr, residual_dt=2,
+                          ldr=N)
+    E.gemm(M, N, K, gx.ptr, K, 0, gw.ptr, K, 1, out.ptr, N, 2, 2, epi=epi)
+    ref = O.gelu_tanh(O.linear(x, w, b)) + res
+    assert_close_16bit(to_host32(ops, out), ref, f"swap-AB {M}x{N}x{K}")
     assert device_error(0) == 0
