@@ -565,10 +565,15 @@ def run_gpu_arm(args, dist):
         else:
             fl = {"q": 2.0 * p.m * HIDDEN * HIDDEN, "kv": 4.0 * p.m * HIDDEN * HIDDEN,
                   "out": 2.0 * p.m * HIDDEN * HIDDEN, "up": 8.0 * p.m * HIDDEN * HIDDEN,
-                  "down": 8.0 * p.m * HIDDEN * HIDDEN}.get(top, 0.0)
+                  "down": 8.0 * p.m * HIDDEN * HIDDEN,
+                  # fused attention: QK^T and P.V, 2 * 2 * rows * keys * head_dim per head
+                  "attn": 4.0 * p.samples_per_rank * 30 * rows_q * TOKENS * (HIDDEN // 30)}.get(top, 0.0)
             roof["achieved"] = fl / (ms_top / 1e3) / 1e12
             roof["frac"] = roof["achieved"] / peak
             roof["launch_ms_mean"] = ms_top
+            if top == "attn":
+                roof["kernel"] = "sf::attention_fwd_kernel (tcgen05, fused QK^T-softmax-PV)"
+                roof["algorithmic_flops_per_launch"] = fl
         roof["kernel_share"] = totals[top] / sum(totals.values())
         roof["top_kernel"] = top
         del lin_flops

@@ -171,6 +171,22 @@ int32_t sf_softmax_rows(const void* x, int32_t x_dtype, int64_t ldx,
                         void* y, int32_t y_dtype, int64_t ldy,
                         int64_t rows, int64_t cols, float scale, void* stream);
 
+/* Fused attention forward, head_dim 64, 16-bit Q/K/V/O (fp32 softmax):
+ *   O[b, :, h] = softmax(scale * Q[b, :, h] K[b, :, h]^T) V[b, :, h]
+ * Head h of batch b, row r of Q lives at q + b*q_bstride + r*ldq + h*64
+ * (elements; likewise K, V, O), so the Q/K/V column blocks of a fused
+ * [tokens, 3*C] projection are read in place.  Replaces the batched
+ * matmul -> muls -> softmax -> batched matmul chain of
+ * scaled_dot_product_attention (nn/functional.py:310-321, built from
+ * _cuda_ops.pyx:1152-1190, :990-998, :1016-1034, :1122-1149) and the DiT
+ * attention einsum (diffusion/models.py:529-536).  Pointers and strides
+ * 16-byte aligned; kv_len >= 1. */
+int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                         int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
+                         const void* k, int64_t ldk, int64_t k_bstride, const void* v,
+                         int64_t ldv, int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
+                         float scale, int32_t dtype, void* stream);
+
 /* y[i] = act(alpha * x[i]).  Replaces cuda_silu_f32 / cuda_gelu_f32 /
  * cuda_muls_f32 (_cuda_ops_decl.h:69, :74, :63; _cuda_kernels.cu:384, :428,
  * :237-277) for the standalone dev_silu / dev_gelu / dev_muls calls. */

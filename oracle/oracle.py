@@ -216,6 +216,71 @@ def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
     return (out, absprod) if return_absprod else out
 
 
+def _bf16_neighbours(p: np.ndarray, p_dtype: str):
+    """The two representable ``p_dtype`` values around ``p`` (p >= 0)."""
+    if p_dtype == "bf16":
+        bits = np.asarray(p, np.float32).view(np.uint32) & np.uint32(0xFFFF0000)
+        lo = bits.view(np.float32)
+        hi = (bits + np.uint32(0x10000)).view(np.float32)
+        return lo, hi
+    if p_dtype == "f16":
+        lo = np.asarray(p, np.float32).astype(np.float16)
+        lo = np.where(lo.astype(np.float32) > p, np.nextafter(lo, np.float16(0)), lo)
+        hi = np.nextafter(lo, np.float16(np.inf))
+        return lo.astype(np.float32), hi.astype(np.float32)
+    return p, p
+
+
+def flash_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
+                    block: int = 128, p_dtype: str = "bf16", flip_tol: float = 2.0 ** -12,
+                    return_allowance: bool = False):
+    """Attention ``softmax(scale * q k^T) v`` for one head, restated in the
+    online (blockwise) form the fused device kernel computes, so that the
+    P.V operand is rounded where the device rounds it.
+
+    The result equals ``sdpa`` (``nn/functional.py:323-357``) up to that
+    rounding.  Keys are taken in blocks of ``block``; with the running row
+    maximum ``m`` kept in the log2 domain (``c = scale * log2 e``):
+    ``m' = max(m, c * max_j s_ij)``, ``alpha = 2^(m - m')``,
+    ``p_ij = 2^(c s_ij - m')`` (fp32), ``l = alpha l + sum_j p_ij``,
+    ``o = alpha o + round(p) v_block``; finally ``o / l``.  ``p_dtype`` is the
+    storage type of the P operand (the device's 16-bit MMA input).
+
+    With ``return_allowance`` it also returns, per output element, the
+    change that rounding p the other way could cause for every p lying
+    within ``flip_tol`` (relative) of a rounding midpoint: scores computed
+    in a different summation order shift such p across the midpoint, so no
+    restatement can fix which neighbour the device picks.
+    """
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    n = q.shape[0]
+    c = np.float32(scale * 1.4426950408889634)
+    m = np.full(n, -np.inf, np.float32)
+    l = np.zeros(n, np.float32)
+    o = np.zeros((n, v.shape[1]), np.float32)
+    a = np.zeros((n, v.shape[1]), np.float64)
+    for j0 in range(0, k.shape[0], block):
+        s = (q @ k[j0:j0 + block].T).astype(np.float32)
+        m_new = np.maximum(m, s.max(axis=1) * c)
+        alpha = np.exp2(m - m_new).astype(np.float32)
+        p = np.exp2(s * c - m_new[:, None]).astype(np.float32)
+        l = l * alpha + p.sum(axis=1, dtype=np.float32)
+        o = o * alpha[:, None] + round_to(p, p_dtype) @ v[j0:j0 + block]
+        if return_allowance:
+            lo, hi = _bf16_neighbours(p, p_dtype)
+            mid = 0.5 * (lo.astype(np.float64) + hi)
+            near = np.abs(p - mid) <= flip_tol * np.maximum(p, 1e-30)
+            flip = np.where(near, hi.astype(np.float64) - lo, 0.0)
+            a = a * alpha[:, None] + flip @ np.abs(v[j0:j0 + block].astype(np.float64))
+        m = m_new
+    out = (o / l[:, None]).astype(np.float32)
+    if return_allowance:
+        return out, a / l[:, None]
+    return out
+
+
 def dit_layer(x: np.ndarray, w: dict, batch: int, heads: int, head_dim: int,
               chunk: int = 2048, dtype: str = "bf16") -> np.ndarray:
     """One DiT layer as the B200 engine runs it (no adaLN / LayerNorm).
@@ -329,7 +394,7 @@ def abs_product(a: np.ndarray, b_t: np.ndarray) -> np.ndarray:
 
 def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
                           tau: float = 1e-2, absprod: np.ndarray | None = None,
-                          kappa: float = 1e-2):
+                          kappa: float = 1e-2, allowance: np.ndarray | None = None):
     """Per-element relative check for bf16/fp16 outputs (bar: 1e-2).
 
     An element passes when ``|out - ref| <= rtol * max(|ref|, tau * rms(ref row),
@@ -342,7 +407,9 @@ def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
     absolute sum, the accumulation precision of the tensor cores' fp32
     accumulators (measured ~2^-15 of the absolute sum on cancelling sums).  Returns ``(ok, stats)`` with the worst pure
     relative error, the worst error against the floored denominator, and the
-    number of elements that needed the floor.
+    number of elements that needed the floor.  ``allowance`` (optional) is an
+    absolute per-element slack added to the bar: the rounding decisions the
+    oracle cannot reproduce (``flash_attention``'s flip allowance).
     """
     o = np.asarray(out, dtype=np.float64)
     r = np.asarray(ref, dtype=np.float64)
@@ -358,6 +425,9 @@ def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
         den = np.maximum(den, kappa * np.asarray(absprod, np.float64).reshape(rr.shape))
     den = np.where(den > 0, den, 1.0)
     err = np.abs(oo - rr)
+    if allowance is not None:
+        # an allowance of A widens the bar rtol*den by A: scale it into err
+        err = np.maximum(err - np.asarray(allowance, np.float64).reshape(rr.shape), 0.0)
     floored = err / den
     finite = np.isfinite(oo).all()
     pure = err / np.where(absr > 0, absr, np.inf)

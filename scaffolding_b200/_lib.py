@@ -77,6 +77,8 @@ SIGNATURES: dict[str, list] = {
     "sf_get_fp32_mode": [_P(_i32)],
     "sf_set_kernel_override": [_i32],
     "sf_softmax_rows": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, C.c_float, _vp],
+    "sf_attention_fwd": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp,
+                         _i64, _i64, _vp, _i64, _i64, C.c_float, _i32, _vp],
     "sf_unary": [_vp, _i32, _vp, _i32, _i64, C.c_float, _i32, _vp],
     "sf_device_count": [_P(_i32)],
     "sf_set_device": [_i32],

@@ -1,0 +1,362 @@
+// Fused attention forward for sm_100a (flash-style, tcgen05):
+//
+//   O[b, h] = softmax(scale * Q[b, h] K[b, h]^T) V[b, h],   head_dim = 64,
+//
+// with the scores S and probabilities P kept on chip.  Replaces the unfused
+// chain of the reference's scaled_dot_product_attention
+// (nn/functional.py:310-321: dev_batched_matmul_nt -> dev_muls -> dev_softmax
+// -> dev_batched_matmul) and of the DiT attention einsum
+// (diffusion/models.py:529-536), whose fp32 score matrix makes the unfused
+// path HBM-bound.
+//
+// One CTA per (128-query block, head, batch); 192 threads:
+//   warp 0      TMA producer: Q once, then K and V blocks of 128 keys into a
+//               KV_STAGES-deep ring (K-major 128B-swizzled tiles; V's tile is
+//               the MN-major B operand of P.V).
+//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T (M 128, N 128, K 64)
+//               into one of two TMEM score buffers, then O_j = P_j V_j
+//               (M 128, N 64, K 128) into one of two TMEM output buffers.
+//               S_{j+1} is issued before P_j V_j, so the softmax of block
+//               j+1 overlaps the P.V of block j.
+//   warps 2-5   softmax, one thread per query row (TMEM lane): two passes
+//               over the row's 128 scores (row max, then exp2 / sum / bf16
+//               P into a swizzled shared-memory A tile), online rescaling
+//               in the log2 domain, and the running output accumulated in
+//               fp32 registers from each O_j (o = o * alpha + O_j).
+// Keys past kv_len (the ragged last block; TMA zero-fills them) are masked
+// to -inf; query rows past q_len are computed and not stored.
+//
+// Every wait is bounded (global timer): an expired wait records an error
+// code in the device error word, the CTA drains its copies and MMAs and
+// exits, so a broken pipeline returns a status instead of hanging.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace sf {
+
+struct AttnArgs {
+  int q_len, kv_len, heads, batch;
+  float scale_log2;      // softmax scale * log2(e)
+  void* o;               // output, 16-bit
+  int out_dtype;         // kBF16 / kF16
+  int64_t ldo, o_bstride;  // elements
+  int* err;
+};
+
+constexpr int kAttnBlock = 128;   // queries per CTA and keys per block
+constexpr int kAttnD = 64;        // head dim
+constexpr int kAttnKvStages = 4;
+constexpr int kAttnThreads = 192;
+
+struct AttnSmem {
+  static constexpr int TILE = kAttnBlock * 128;          // 128 rows x 128 B = 16 KB
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = TILE;                    // stage s: K at +2s*TILE, V at +(2s+1)*TILE
+  static constexpr int P_OFF = KV_OFF + kAttnKvStages * 2 * TILE;  // 2 buffers x 2 atoms
+  static constexpr int BYTES = P_OFF + 2 * 2 * TILE + 1024;
+};
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_16bit(float a, float b, bool bf16) {
+  if (bf16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t kv_full[kAttnKvStages];
+  __shared__ __align__(8) uint64_t kv_empty[kAttnKvStages];
+  __shared__ __align__(8) uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int nblk = (p.kv_len + kAttnBlock - 1) / kAttnBlock;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < kAttnKvStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  volatile int* abortp = &abort_flag;
+  // TMEM columns: S buffers [0,128) and [128,256); O buffers [256,320) and [320,384).
+
+  if (warp == 0) {
+    // ───────────── TMA producer ─────────────
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0, stage = 0;
+      uint32_t phase = 0;
+      mbar_arrive_expect_tx(&q_full, AttnSmem::TILE);
+      tma_load_4d(smem + AttnSmem::Q_OFF, &tmQ, &q_full, 0, qb * kAttnBlock, h, b);
+      for (int j = 0; j < nblk; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+          ok = false;
+          break;
+        }
+        uint8_t* kt = smem + AttnSmem::KV_OFF + stage * 2 * AttnSmem::TILE;
+        mbar_arrive_expect_tx(&kv_full[stage], 2 * AttnSmem::TILE);
+        tma_load_4d(kt, &tmK, &kv_full[stage], 0, j * kAttnBlock, h, b);
+        tma_load_4d(kt + AttnSmem::TILE, &tmV, &kv_full[stage], 0, j * kAttnBlock, h, b);
+        ++issued;
+        if (++stage == kAttnKvStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // Wait (bounded) for every copy this thread issued before the CTA may
+      // retire: on the normal path they have all been consumed already.
+      if (!mbar_wait_quiet(&q_full, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      if (!ok) {
+        const int n = issued < kAttnKvStages ? issued : kAttnKvStages;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = kAttnKvStages - 1;
+            ph ^= 1u;
+          }
+          if (!mbar_wait_quiet(&kv_full[s], ph, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ───────────── MMA issuer ─────────────
+    if (lane == 0) {
+      const uint32_t fmt = BF16 ? 1u : 0u;
+      const uint32_t idesc_s = make_idesc(fmt, 128, 128, 0u, 0u);  // K-major A and B
+      const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);   // P K-major, V MN-major
+      const uint32_t q_addr = smem_u32(smem + AttnSmem::Q_OFF);
+      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
+      bool issued_any = false;
+      int stage = 0;
+      uint32_t phase = 0;
+      int pv_stage = 0;
+      auto issue_pv = [&](int jj) -> bool {
+        const int buf = jj & 1;
+        const uint32_t par = (static_cast<uint32_t>(jj) >> 1) & 1u;
+        if (!mbar_wait(&p_full[buf], par, p.err, kDevTimeoutMma, abortp)) return false;
+        if (!mbar_wait(&o_free[buf], par ^ 1u, p.err, kDevTimeoutMma, abortp)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(smem + AttnSmem::P_OFF + buf * 2 * AttnSmem::TILE);
+        const uint32_t v_addr = smem_u32(smem + AttnSmem::KV_OFF + pv_stage * 2 * AttnSmem::TILE +
+                                         AttnSmem::TILE);
+        const uint32_t d_tmem = tmem_base + 256u + static_cast<uint32_t>(buf * 64);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t ad =
+              make_sw128_desc(p_addr + (ks >> 2) * AttnSmem::TILE + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, 8192, 1024);
+          umma_f16(d_tmem, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[buf]);
+        umma_commit(&kv_empty[pv_stage]);  // K and V of this block are consumed
+        if (++pv_stage == kAttnKvStages) pv_stage = 0;
+        return true;
+      };
+      for (int j = 0; j < nblk && ok; ++j) {
+        const int buf = j & 1;
+        const uint32_t par = (static_cast<uint32_t>(j) >> 1) & 1u;
+        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp) ||
+            !mbar_wait(&s_free[buf], par ^ 1u, p.err, kDevTimeoutMma, abortp)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + AttnSmem::KV_OFF + stage * 2 * AttnSmem::TILE);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * 128);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
+          const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
+          umma_f16(d_tmem, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        issued_any = true;
+        umma_commit(&s_full[buf]);
+        if (++stage == kAttnKvStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
+      if (!ok && issued_any) {
+        umma_commit(&drain_bar);
+        if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      }
+    }
+  } else {
+    // ───────────── softmax (warps 2..5): one thread per query row ─────────────
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    float o_acc[kAttnD];
+#pragma unroll
+    for (int t = 0; t < kAttnD; ++t) o_acc[t] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+    const float c = p.scale_log2;
+    bool ok = true;
+    auto consume_o = [&](int jj, float alpha) -> bool {
+      const int buf = jj & 1;
+      const uint32_t par = (static_cast<uint32_t>(jj) >> 1) & 1u;
+      if (!mbar_wait(&o_full[buf], par, p.err, kDevTimeoutEpilogue, abortp)) return false;
+      tc_fence_after();
+      uint32_t r[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(tmem_base + lane_base + 256u + static_cast<uint32_t>(buf * 64 + half * 32), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          o_acc[half * 32 + t] = fmaf(o_acc[half * 32 + t], alpha, __uint_as_float(r[t]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[buf]);
+      return true;
+    };
+    for (int j = 0; j < nblk; ++j) {
+      const int buf = j & 1;
+      const uint32_t par = (static_cast<uint32_t>(j) >> 1) & 1u;
+      if (!mbar_wait(&s_full[buf], par, p.err, kDevTimeoutEpilogue, abortp)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_addr = tmem_base + lane_base + static_cast<uint32_t>(buf * 128);
+      const int valid = min(kAttnBlock, p.kv_len - j * kAttnBlock);
+      // pass 1: row maximum of the (masked) scores
+      float mx = -INFINITY;
+      uint32_t r[32];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        tmem_ld32(s_addr + ch * 32, r);
+        tmem_ld_wait();
+        if (valid == kAttnBlock) {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) mx = fmaxf(mx, __uint_as_float(r[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (ch * 32 + t < valid) mx = fmaxf(mx, __uint_as_float(r[t]));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx * c);
+      const float alpha = ex2_approx(m_run - m_new);  // 0 on the first block
+      // pass 2: P = exp2(c*s - m_new) as 16-bit into the swizzled A tile
+      uint8_t* pbase = smem + AttnSmem::P_OFF + buf * 2 * AttnSmem::TILE;
+      float sum = 0.0f;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        tmem_ld32(s_addr + ch * 32, r);
+        tmem_ld_wait();
+        float pv[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const float e = ex2_approx(fmaf(__uint_as_float(r[t]), c, -m_new));
+          pv[t] = (valid == kAttnBlock || ch * 32 + t < valid) ? e : 0.0f;
+          sum += pv[t];
+        }
+        // keys [ch*32, ch*32+32): atom ch/2, 16-byte chunks (ch%2)*4 .. +3
+        uint8_t* rowp = pbase + (ch >> 1) * AttnSmem::TILE + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (ch & 1) * 4 + q;
+          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(pack_16bit(pv[8 * q], pv[8 * q + 1], BF16),
+                         pack_16bit(pv[8 * q + 2], pv[8 * q + 3], BF16),
+                         pack_16bit(pv[8 * q + 4], pv[8 * q + 5], BF16),
+                         pack_16bit(pv[8 * q + 6], pv[8 * q + 7], BF16));
+        }
+      }
+      l_run = fmaf(l_run, alpha, sum);
+      m_run = m_new;
+      tc_fence_before();
+      fence_proxy_async_smem();  // P writes -> tensor-core (async proxy) reads
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[buf]);
+        mbar_arrive(&p_full[buf]);
+      }
+      if (j >= 1 && !consume_o(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && nblk > 0) ok = consume_o(nblk - 1, alpha_prev);
+    const int qrow = qb * kAttnBlock + row;
+    if (ok && qrow < p.q_len) {
+      const float inv = 1.0f / l_run;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
+                     (static_cast<int64_t>(b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
+                      static_cast<int64_t>(h) * kAttnD) * 2;
+#pragma unroll
+      for (int q = 0; q < kAttnD / 8; ++q)
+        reinterpret_cast<uint4*>(dst)[q] =
+            make_uint4(pack_16bit(o_acc[8 * q] * inv, o_acc[8 * q + 1] * inv, BF16),
+                       pack_16bit(o_acc[8 * q + 2] * inv, o_acc[8 * q + 3] * inv, BF16),
+                       pack_16bit(o_acc[8 * q + 4] * inv, o_acc[8 * q + 5] * inv, BF16),
+                       pack_16bit(o_acc[8 * q + 6] * inv, o_acc[8 * q + 7] * inv, BF16));
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace sf

@@ -28,6 +28,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "gemv.cuh"
+#include "attention.cuh"
 #include "rowwise.cuh"
 
 namespace sf {
@@ -955,3 +956,78 @@ int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float m
 }
 
 }  // extern "C"
+
+// ───────────────────────────── fused attention ─────────────────────────────
+
+extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                                    int32_t head_dim, const void* q, int64_t ldq,
+                                    int64_t q_bstride, const void* k, int64_t ldk,
+                                    int64_t k_bstride, const void* v, int64_t ldv,
+                                    int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
+                                    float scale, int32_t dtype, void* stream) {
+  if (batch < 0 || heads < 0 || q_len < 0 || kv_len < 0)
+    return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
+  if (batch == 0 || heads == 0 || q_len == 0) return SF_OK;
+  if (kv_len == 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention over zero keys");
+  if (head_dim != kAttnD) return fail(SF_ERR_UNSUPPORTED, "fused attention needs head_dim 64 (got %d)", head_dim);
+  if (dtype != kBF16 && dtype != kF16) return fail(SF_ERR_INVALID_ARGUMENT, "fused attention dtype %d", dtype);
+  if (!q || !k || !v || !o) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
+  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
+    if (!aligned16(ptr)) return fail(SF_ERR_INVALID_ARGUMENT, "attention operands must be 16-byte aligned");
+  for (int64_t st : {ldq, ldk, ldv, ldo, q_bstride, k_bstride, v_bstride, o_bstride})
+    if (!bytes16(st, 2) || st < 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention strides must be 16-byte multiples");
+  const int64_t row_min = static_cast<int64_t>(heads) * head_dim;
+  if (ldq < row_min || ldk < row_min || ldv < row_min || ldo < row_min)
+    return fail(SF_ERR_INVALID_ARGUMENT, "leading dimension < heads * head_dim");
+  if (heads > 65535 || batch > 65535) return fail(SF_ERR_UNSUPPORTED, "attention grid");
+  DeviceInfo* dev = nullptr;
+  int device = 0;
+  int32_t st = current_device_info(&dev, &device);
+  if (st != SF_OK) return st;
+  if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
+  const CUtensorMapDataType dt = tma_dtype(dtype);
+  CUtensorMap mq, mk, mv;
+  MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldq, head_dim, q_bstride,
+             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+  MapSpec sk{k, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldk, head_dim, k_bstride,
+             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+  MapSpec sv{v, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldv, head_dim, v_bstride,
+             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+  if ((st = encode_map(&mq, sq)) != SF_OK) return st;
+  if ((st = encode_map(&mk, sk)) != SF_OK) return st;
+  if ((st = encode_map(&mv, sv)) != SF_OK) return st;
+  AttnArgs a;
+  a.q_len = q_len;
+  a.kv_len = kv_len;
+  a.heads = heads;
+  a.batch = batch;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.o = o;
+  a.out_dtype = dtype;
+  a.ldo = ldo;
+  a.o_bstride = o_bstride;
+  a.err = dev->err_word;
+  const dim3 grid(static_cast<unsigned>(ceil_div(q_len, kAttnBlock)), static_cast<unsigned>(heads),
+                  static_cast<unsigned>(batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  static bool attr_set[2][64] = {{false}};
+  const int bi = dtype == kBF16 ? 1 : 0;
+  if (device < 64 && !attr_set[bi][device]) {
+    if (bi)
+      SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::BYTES));
+    else
+      SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::BYTES));
+    attr_set[bi][device] = true;
+  }
+  if (bi)
+    attention_fwd_kernel<true><<<grid, kAttnThreads, AttnSmem::BYTES, s>>>(mq, mk, mv, a);
+  else
+    attention_fwd_kernel<false><<<grid, kAttnThreads, AttnSmem::BYTES, s>>>(mq, mk, mv, a);
+  SF_CUDA_TRY(cudaGetLastError());
+  return SF_OK;
+}

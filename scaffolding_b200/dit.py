@@ -18,6 +18,7 @@ block is exactly four tcgen05 GEMM launches.
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 
@@ -144,6 +145,8 @@ class DitStack:
     Per layer (all on one stream):
       q  = x Wq^T, kv = x Wkv^T          (Wq, Wkv = row blocks of to_qkv)
       [kv all-gather inside the K/V group when the sample is split]
+      attention, either fused (``fused=True``, the default for head_dim 64:
+      one sf_attention_fwd launch, S and P never leave the SM) or unfused,
       per query chunk of <= ``chunk`` rows, for every (sample, head):
         S = (Q K^T) / sqrt(d)  fp32   -- one batched GEMM, scale in the epilogue
         P = softmax(S)         bf16   -- row softmax in fp32
@@ -157,7 +160,7 @@ class DitStack:
 
     def __init__(self, plan: ShardPlan, hidden: int, heads: int, layers: int, device: int,
                  chunk: int = 2048, weights: list | None = None, seed: int = 1,
-                 kv_comm=None, world_comm=None):
+                 kv_comm=None, world_comm=None, fused: bool | None = None):
         import ctypes as C
 
         from ._lib import check, lib
@@ -165,6 +168,9 @@ class DitStack:
         self.D = hidden // heads
         self.dev = device
         self.chunk = chunk
+        if fused is None:
+            fused = self.D == 64 and os.environ.get("SF_ATTN_FUSED", "1") != "0"
+        self.fused = bool(fused)
         self.kv_comm, self.world_comm = kv_comm, world_comm
         bf = E.bfloat16
         m, Cw = plan.m, hidden
@@ -196,8 +202,10 @@ class DitStack:
                         else self.kv_local)
         q_rows = plan.tokens if plan.whole_samples else m
         crow = min(chunk, q_rows)
-        self.S = ops._alloc((spr, heads, crow, keys), np.float32, device)
-        self.P = ops._alloc((spr, heads, crow, keys), bf, device)
+        self.S = self.P = None
+        if not self.fused:
+            self.S = ops._alloc((spr, heads, crow, keys), np.float32, device)
+            self.P = ops._alloc((spr, heads, crow, keys), bf, device)
         self.attn = ops._alloc((m, Cw), bf, device)
         self.h = ops._alloc((m, Cw), bf, device)
         self.f = ops._alloc((m, 4 * Cw), bf, device)
@@ -214,15 +222,24 @@ class DitStack:
             timer.stop(name)
 
     def _attention(self, stream, timer):
-        import ctypes as C
-
-        from ._lib import check, lib
         p, Cw, H, D = self.plan, self.C, self.H, self.D
         keys = p.tokens
         spr = p.samples_per_rank
         q_rows = p.tokens if p.whole_samples else p.m
         scale = 1.0 / math.sqrt(D)
         bf = DT_BF16
+        if self.fused:
+            # Q rows of each local sample; K and V in place in the [keys, 2C]
+            # rows of kv_full (K at column 0, V at column C, head h at h*64).
+            if timer is not None:
+                timer.start("attn")
+            E.attention(spr, H, q_rows, keys, self.q.ptr, Cw, q_rows * Cw, self.kv_full.ptr,
+                        2 * Cw, keys * 2 * Cw, self.kv_full.ptr + Cw * 2, 2 * Cw, keys * 2 * Cw,
+                        self.attn.ptr, Cw, q_rows * Cw, scale, dtype=bf, head_dim=D,
+                        stream=stream, device=self.dev)
+            if timer is not None:
+                timer.stop("attn")
+            return
         for c0 in range(0, q_rows, self.chunk):
             rows = min(self.chunk, q_rows - c0)
             s_batch = rows * keys
@@ -318,6 +335,8 @@ class DitStack:
 
     def launches_per_forward(self) -> int:
         p = self.plan
+        if self.fused:
+            return self.L * 6
         q_rows = p.tokens if p.whole_samples else p.m
         chunks = (q_rows + self.chunk - 1) // self.chunk
         return self.L * (5 + 3 * chunks)

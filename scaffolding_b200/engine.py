@@ -265,6 +265,20 @@ def softmax_rows(x, x_dt, ldx, y, y_dt, ldy, rows, cols, scale=1.0, stream=None,
           "sf_softmax_rows")
 
 
+def attention(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride, v, ldv,
+              v_bstride, o, ldo, o_bstride, scale, dtype=DT_BF16, head_dim=64, stream=None,
+              device=None):
+    """Fused attention forward (sf_attention_fwd): pointers are device
+    addresses, strides in elements; head h of Q at column h * head_dim."""
+    dev = current_device() if device is None else device
+    s = get_stream(dev) if stream is None else stream
+    check(lib.sf_attention_fwd(batch, heads, q_len, kv_len, head_dim, C.c_void_p(q), ldq,
+                               q_bstride, C.c_void_p(k), ldk, k_bstride, C.c_void_p(v), ldv,
+                               v_bstride, C.c_void_p(o), ldo, o_bstride, float(scale), dtype,
+                               C.c_void_p(s) if s else None),
+          "sf_attention_fwd")
+
+
 def unary(x, x_dt, y, y_dt, n, alpha=1.0, act=ACT_NONE, stream=None, device=None):
     dev = current_device() if device is None else device
     if stream is None:

@@ -73,3 +73,93 @@ def test_dev_muls_silu_gelu(gpu, ops, golden):
     np.testing.assert_allclose(ops.gputensor_to_numpy(ops.dev_gelu(gz)), golden["act_gelu"],
                                rtol=2e-6, atol=1e-6)
     np.testing.assert_array_equal(ops.gputensor_to_numpy(ops.dev_muls(gz, 0.125)), z * np.float32(0.125))
+
+
+# Fused attention rounds the unnormalised block probabilities 2^(c s - m)
+# to 16 bits as the P.V operand; the oracle restates that (flash_attention).
+# Scores summed in another order can move a p across a 16-bit rounding
+# midpoint; flash_attention's allowance adds, per output, the change such a
+# flip could cause for every p within 2^-12 of a midpoint.
+def _check_attn(out, ref, absprod, allowance, what):
+    ok, st = O.elementwise_rel_check(out, ref, rtol=1e-2, tau=1e-2, absprod=absprod,
+                                     kappa=1e-2, allowance=allowance)
+    assert ok, f"{what}: {st}"
+
+
+def _fused(ops, batch, heads, q_len, kv_len, q, k, v, ldq, ldk, ldv, q_bs, k_bs, v_bs, scale,
+           dt="bf16"):
+    """Run sf_attention_fwd on device copies; returns O as fp32 [batch*q_len, heads*64]."""
+    from scaffolding_b200 import engine as E
+    o = ops._alloc((batch * q_len, heads * 64), np_dtype(dt), 0)
+    E.attention(batch, heads, q_len, kv_len, q.ptr, ldq, q_bs, k.ptr, ldk, k_bs, v.ptr, ldv, v_bs,
+                o.ptr, heads * 64, q_len * heads * 64, scale, dtype=E.dtype_code(np_dtype(dt)))
+    return to_host32(ops, o)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("batch,tokens,heads", [(2, 300, 3), (1, 128, 1), (1, 2048, 2), (2, 1000, 4)])
+def test_fused_attention_dit_layout(gpu, ops, dt, batch, tokens, heads):
+    """Fused attention reading Q, K, V in place from a fused [B*N, 3C] QKV
+    activation (the DiT layout), ragged last query and key blocks; against
+    the oracle's exact-softmax attention with the |P||V| error floor."""
+    from tests.gpu_util import device_error
+    rng = np.random.default_rng(tokens + heads)
+    C = heads * 64
+    qkv32 = rng.standard_normal((batch * tokens, 3 * C), dtype=np.float32)
+    g, qkv = to_device(ops, qkv32, dt)
+    base = g.ptr
+    out = _fused(ops, batch, heads, tokens, tokens,
+                 type("P", (), {"ptr": base})(), type("P", (), {"ptr": base + C * 2})(),
+                 type("P", (), {"ptr": base + 2 * C * 2})(), 3 * C, 3 * C, 3 * C,
+                 tokens * 3 * C, tokens * 3 * C, tokens * 3 * C, 0.125, dt)
+    for b in range(batch):
+        X = qkv[b * tokens:(b + 1) * tokens]
+        for h in range(heads):
+            q, k, v = (X[:, s * C + h * 64:s * C + (h + 1) * 64] for s in range(3))
+            ref, allow = O.flash_attention(q, k, v, 0.125, p_dtype=dt, return_allowance=True)
+            p = O.softmax_rows((q @ k.T * np.float32(0.125)).astype(np.float32))
+            _check_attn(out[b * tokens:(b + 1) * tokens, h * 64:(h + 1) * 64], ref,
+                        O.abs_product(p, v.T), allow, f"fused {dt} B={batch} N={tokens} b{b} h{h}")
+    assert device_error(0) == 0
+
+
+def test_fused_attention_separate_qkv_lengths(gpu, ops):
+    """Separate Q / K / V buffers, q_len != kv_len (ragged both), large
+    logits (online-softmax rescaling), against per-head oracle SDPA."""
+    from tests.gpu_util import device_error
+    rng = np.random.default_rng(5)
+    B, H, Lq, Lk = 2, 2, 200, 517
+    q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
+    k32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32) * np.float32(3)
+    v32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32)
+    gq, q = to_device(ops, q32, "bf16")
+    gk, k = to_device(ops, k32, "bf16")
+    gv, v = to_device(ops, v32, "bf16")
+    out = _fused(ops, B, H, Lq, Lk, gq, gk, gv, H * 64, H * 64, H * 64, Lq * H * 64, Lk * H * 64,
+                 Lk * H * 64, 0.125)
+    for b in range(B):
+        for h in range(H):
+            sl = slice(h * 64, (h + 1) * 64)
+            s = q[b][:, sl] @ k[b][:, sl].T * np.float32(0.125)
+            p = O.softmax_rows(s.astype(np.float32))
+            ref, allow = O.flash_attention(q[b][:, sl], k[b][:, sl], v[b][:, sl], 0.125,
+                                           return_allowance=True)
+            ap = O.abs_product(p, v[b][:, sl].T)
+            _check_attn(out[b * Lq:(b + 1) * Lq, sl], ref, ap, allow, f"b{b} h{h}")
+    assert device_error(0) == 0
+
+
+def test_fused_attention_rejects_bad_arguments(gpu, ops):
+    from scaffolding_b200._lib import SF_ERR_INVALID_ARGUMENT, SF_ERR_UNSUPPORTED, lib
+    import ctypes as C
+    buf = ops._alloc((256, 3 * 64), np_dtype("bf16"), 0)
+    p = C.c_void_p(buf.ptr)
+    # head_dim other than 64
+    assert lib.sf_attention_fwd(1, 1, 8, 8, 32, p, 192, 0, p, 192, 0, p, 192, 0, p, 192, 0,
+                                1.0, 2, None) == SF_ERR_UNSUPPORTED
+    # misaligned stride (ld * 2 bytes not a multiple of 16)
+    assert lib.sf_attention_fwd(1, 1, 8, 8, 64, p, 65, 0, p, 192, 0, p, 192, 0, p, 192, 0,
+                                1.0, 2, None) == SF_ERR_INVALID_ARGUMENT
+    # zero keys
+    assert lib.sf_attention_fwd(1, 1, 8, 0, 64, p, 192, 0, p, 192, 0, p, 192, 0, p, 192, 0,
+                                1.0, 2, None) == SF_ERR_INVALID_ARGUMENT

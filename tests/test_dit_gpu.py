@@ -72,8 +72,8 @@ def test_stack_small_matches_oracle(gpu, ops):
     ws = _weights(L, Cw, 40)
     x = O.round_bf16(np.random.default_rng(41).standard_normal((B * N, Cw), dtype=np.float32))
     plan = dit.ShardPlan(B, N, 1, 0)
-    st = dit.DitStack(plan, Cw, H, L, 0, chunk=256, weights=ws)
-    chunked = dit.DitStack(plan, Cw, H, L, 0, chunk=64, weights=ws)
+    st = dit.DitStack(plan, Cw, H, L, 0, chunk=256, weights=ws, fused=False)
+    chunked = dit.DitStack(plan, Cw, H, L, 0, chunk=64, weights=ws, fused=False)
     gx = _upload_x(ops, x)
     cur_ptr, cur = gx.ptr, x
     for li in range(L):
@@ -109,22 +109,26 @@ def test_stack_small_matches_oracle(gpu, ops):
     np.testing.assert_array_equal(_host(ops, st.y[(L - 1) % 2]), cur)
 
 
-def test_sliced_ranks_equal_whole_sample(gpu, ops):
+@pytest.mark.parametrize("fused", [False, True])
+def test_sliced_ranks_equal_whole_sample(gpu, ops, fused):
     """Four emulated ranks holding half a sample each (K/V exchanged between
     the two ranks of a sample) reproduce the one-rank result bit for bit:
     every row goes through the same kernels over the same keys (shards of
-    300 rows take the same GEMM path as the whole 1200-row batch)."""
+    300 rows take the same GEMM path as the whole 1200-row batch; the fused
+    attention computes each query row from its own scores only)."""
     from scaffolding_b200 import dit
     from scaffolding_b200 import engine as E
     B, N, Cw, H, chunk = 2, 600, 256, 4, 160
     ws = _weights(1, Cw, 50)
     x = O.round_bf16(np.random.default_rng(51).standard_normal((B * N, Cw), dtype=np.float32))
     gx = _upload_x(ops, x)
-    whole = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, 1, 0, chunk=chunk, weights=ws)
+    whole = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, 1, 0, chunk=chunk, weights=ws,
+                         fused=fused)
     whole.forward(gx.ptr)
     ref = _host(ops, whole.y[0])
     world = 4
-    ranks = [dit.DitStack(dit.ShardPlan(B, N, world, r), Cw, H, 1, 0, chunk=chunk, weights=ws)
+    ranks = [dit.DitStack(dit.ShardPlan(B, N, world, r), Cw, H, 1, 0, chunk=chunk, weights=ws,
+                          fused=fused)
              for r in range(world)]
     outs = []
     for r, st in enumerate(ranks):
@@ -142,15 +146,18 @@ def test_sliced_ranks_equal_whole_sample(gpu, ops):
     np.testing.assert_array_equal(np.concatenate(outs), ref)
 
 
-def test_full_size_attention_sampled_rows(gpu, ops):
-    """Config 5 attention at full size (2 x 17776 tokens, 30 heads, 9 query
-    chunks of <= 2048): the oracle recomputes sampled query rows (including
-    the ragged last chunk) from the device's own bf16 Q/K/V."""
+@pytest.mark.parametrize("fused", [False, True])
+def test_full_size_attention_sampled_rows(gpu, ops, fused):
+    """Config 5 attention at full size (2 x 17776 tokens, 30 heads; unfused in
+    9 query chunks of <= 2048, or fused): the oracle recomputes sampled query
+    rows (including the ragged last chunk / block) from the device's own
+    bf16 Q/K/V -- for the fused kernel in its blockwise form with the
+    rounding-flip allowance."""
     from scaffolding_b200 import dit
     B, N, Cw, H = 2, 17776, 1920, 30
     D = Cw // H
     plan = dit.ShardPlan(B, N, 1, 0)
-    st = dit.DitStack(plan, Cw, H, 1, 0, chunk=2048, seed=3)
+    st = dit.DitStack(plan, Cw, H, 1, 0, chunk=2048, seed=3, fused=fused)
     xt = ops._alloc((B * N, Cw), np_dtype("bf16"), 0)
     from scaffolding_b200._lib import lib
     assert lib.sf_fill_normal(C.c_void_p(xt.ptr), 2, B * N * Cw, 5, 0.0, 1.0, None) == 0
@@ -165,9 +172,64 @@ def test_full_size_attention_sampled_rows(gpu, ops):
         b = r // N
         keys = kv[b * N:(b + 1) * N]
         ref = np.empty(Cw, np.float32)
+        allow = np.zeros(Cw)
+        absprod = np.zeros(Cw)
         for h in range(H):
-            s = (q[r, h * D:(h + 1) * D] @ keys[:, h * D:(h + 1) * D].T) * np.float32(0.125)
-            p = O.round_bf16(O.softmax_rows(s[None]))[0]
-            ref[h * D:(h + 1) * D] = p @ keys[:, Cw + h * D:Cw + (h + 1) * D]
-        assert_close_16bit(attn[r][None], ref[None], f"attention row {r}")
+            qh, kh, vh = (q[r, h * D:(h + 1) * D][None], keys[:, h * D:(h + 1) * D],
+                          keys[:, Cw + h * D:Cw + (h + 1) * D])
+            s = (qh @ kh.T) * np.float32(0.125)
+            if fused:
+                o, a = O.flash_attention(qh, kh, vh, 0.125, return_allowance=True)
+                ref[h * D:(h + 1) * D], allow[h * D:(h + 1) * D] = o[0], a[0]
+                absprod[h * D:(h + 1) * D] = O.abs_product(O.softmax_rows(s), vh.T)[0]
+            else:
+                p = O.round_bf16(O.softmax_rows(s))[0]
+                ref[h * D:(h + 1) * D] = p @ vh
+        if fused:
+            ok, stt = O.elementwise_rel_check(attn[r][None], ref[None], absprod=absprod[None],
+                                              allowance=allow[None])
+            assert ok, f"fused attention row {r}: {stt}"
+        else:
+            assert_close_16bit(attn[r][None], ref[None], f"attention row {r}")
     assert np.isfinite(attn).all()
+
+
+def test_stack_small_fused_matches_oracle(gpu, ops):
+    """The fused-attention stack: the attention output of each layer against
+    the blockwise oracle on the device's own Q/K/V (with the rounding-flip
+    allowance), the linears stage-wise, and forward() bit for bit equal to
+    the stage-by-stage run."""
+    from scaffolding_b200 import dit
+    B, N, Cw, H, L = 2, 200, 256, 4, 2
+    D = Cw // H
+    ws = _weights(L, Cw, 60)
+    x = O.round_bf16(np.random.default_rng(61).standard_normal((B * N, Cw), dtype=np.float32))
+    st = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, L, 0, weights=ws, fused=True)
+    assert st.S is None and st.launches_per_forward() == 6 * L
+    gx = _upload_x(ops, x)
+    cur_ptr, cur = gx.ptr, x
+    for li in range(L):
+        w = ws[li]
+        st.qkv(li, cur_ptr)
+        q, kv = _host(ops, st.q), _host(ops, st.kv_local)
+        st._attention(None, None)
+        attn = _host(ops, st.attn)
+        for b in range(B):
+            for h in range(H):
+                rs = slice(b * N, (b + 1) * N)
+                qh, kh = q[rs, h * D:(h + 1) * D], kv[rs, h * D:(h + 1) * D]
+                vh = kv[rs, Cw + h * D:Cw + (h + 1) * D]
+                ref, allow = O.flash_attention(qh, kh, vh, 1.0 / np.sqrt(D), return_allowance=True)
+                p = O.softmax_rows((qh @ kh.T * np.float32(1.0 / np.sqrt(D))).astype(np.float32))
+                ok, stt = O.elementwise_rel_check(attn[rs, h * D:(h + 1) * D], ref,
+                                                  absprod=O.abs_product(p, vh.T), allowance=allow)
+                assert ok, f"L{li} b{b} h{h}: {stt}"
+        out = st.y[li % 2]
+        st.post(li, cur_ptr, out.ptr)
+        h_, y = _host(ops, st.h), _host(ops, out)
+        rh, ah = _lin(attn, w["out_w"], w["out_b"])
+        assert_close_16bit(h_, rh + cur, f"L{li} out-proj", ah + np.abs(cur))
+        cur_ptr, cur = out.ptr, y
+    gy = st.forward(gx.ptr)
+    np.testing.assert_array_equal(_host(ops, st.y[(L - 1) % 2]), cur)
+    assert gy == st.y[(L - 1) % 2].ptr

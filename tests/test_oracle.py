@@ -137,3 +137,33 @@ def test_seeded_inputs_deterministic():
     np.testing.assert_array_equal(a1, a2)
     np.testing.assert_array_equal(b1, b2)
     np.testing.assert_array_equal(O.round_bf16(a1), a1)
+
+
+def test_flash_attention_matches_sdpa():
+    """The blockwise (online-softmax) restatement equals the reference SDPA
+    when P is not rounded, for ragged key counts and large logits."""
+    rng = np.random.default_rng(9)
+    for n_q, n_k in [(5, 7), (130, 300), (64, 128)]:
+        q = rng.standard_normal((n_q, 64), dtype=np.float32) * np.float32(3)
+        k = rng.standard_normal((n_k, 64), dtype=np.float32) * np.float32(3)
+        v = rng.standard_normal((n_k, 64), dtype=np.float32)
+        ref = O.sdpa(q[None], k[None], v[None], scale=0.125)[0]
+        np.testing.assert_allclose(O.flash_attention(q, k, v, 0.125, p_dtype="f32"), ref,
+                                   rtol=2e-5, atol=2e-6)
+
+
+def test_flash_allowance_covers_flips_only():
+    """The flip allowance is zero when no p lies near a rounding midpoint
+    and otherwise bounded by the 16-bit spacing of the p that may flip."""
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((40, 64), dtype=np.float32)
+    k = rng.standard_normal((200, 64), dtype=np.float32)
+    v = rng.standard_normal((200, 64), dtype=np.float32)
+    _, a0 = O.flash_attention(q, k, v, 0.125, return_allowance=True, flip_tol=0.0)
+    assert np.count_nonzero(a0) <= a0.size // 100  # only exact midpoints
+    ref, a = O.flash_attention(q, k, v, 0.125, return_allowance=True)
+    p = O.softmax_rows((q @ k.T * np.float32(0.125)).astype(np.float32))
+    assert (a <= 2.0 ** -7 * O.abs_product(p, v.T) + 1e-12).all()
+    # a change larger than the allowance still fails the check
+    bad = ref + np.float32(0.05)
+    assert not O.elementwise_rel_check(bad, ref, allowance=a)[0]
