@@ -959,6 +959,21 @@ int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float m
 
 // ───────────────────────────── fused attention ─────────────────────────────
 
+template <bool BF16, int SB>
+static int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                                const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
+                                int device) {
+  static bool attr_set[64] = {false};
+  if (device < 64 && !attr_set[device]) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<BF16, SB>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     AttnCfg<SB>::BYTES));
+    attr_set[device] = true;
+  }
+  attention_fwd_kernel<BF16, SB><<<grid, kAttnThreads, AttnCfg<SB>::BYTES, s>>>(mq, mk, mv, a);
+  return SF_OK;
+}
+
 extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                                     int32_t head_dim, const void* q, int64_t ldq,
                                     int64_t q_bstride, const void* k, int64_t ldk,
@@ -1013,21 +1028,14 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
   const dim3 grid(static_cast<unsigned>(ceil_div(q_len, kAttnBlock)), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  static bool attr_set[2][64] = {{false}};
-  const int bi = dtype == kBF16 ? 1 : 0;
-  if (device < 64 && !attr_set[bi][device]) {
-    if (bi)
-      SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::BYTES));
-    else
-      SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::BYTES));
-    attr_set[bi][device] = true;
-  }
-  if (bi)
-    attention_fwd_kernel<true><<<grid, kAttnThreads, AttnSmem::BYTES, s>>>(mq, mk, mv, a);
+  const int sb = env_int("SF_ATTN_SB", 1) == 2 ? 2 : 1;  // tuning knob: score/P buffering
+  if (dtype == kBF16)
+    st = sb == 1 ? launch_attention<true, 1>(grid, mq, mk, mv, a, s, device)
+                 : launch_attention<true, 2>(grid, mq, mk, mv, a, s, device);
   else
-    attention_fwd_kernel<false><<<grid, kAttnThreads, AttnSmem::BYTES, s>>>(mq, mk, mv, a);
+    st = sb == 1 ? launch_attention<false, 1>(grid, mq, mk, mv, a, s, device)
+                 : launch_attention<false, 2>(grid, mq, mk, mv, a, s, device);
+  if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
   return SF_OK;
 }
