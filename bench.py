@@ -1,17 +1,24 @@
 """Benchmark of the B200 matmul engine (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit_block|square|skinny]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit_stack|dit_block|square|skinny]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
     python bench.py --impl reference ...   # the reference's CPU path (NumPy oracle port)
 
-Default workload (``dit_block``, benchmark config 4): the four linears of a
-DiT block (QKV 1920->5760, out 1920->1920 + bias + residual, FFN-up
-1920->7680 + bias + GELU-tanh, FFN-down 7680->1920 + bias + residual) on
-2 x 17776 = 35552 tokens, bf16 with fp32 accumulation, tokens (M) sharded
-over N GPUs with weights replicated and the block output all-gathered over
-NCCL (strong scaling: the total work is fixed).  A step is one block
-forward over the whole token batch.  ``value`` = algorithmic TFLOP/s of the
-whole job (3.1455 TFLOP per step / max-over-ranks step time).
+Default workload (``dit_stack``, benchmark config 5): the full 30-layer DiT
+forward on 2 x 17776 = 35552 tokens, hidden 1920, 30 heads x 64, bf16 with
+fp32 accumulation.  Per layer: QKV projection, attention (the fused tcgen05
+kernel: QK^T, online softmax and P.V on chip), out projection + bias +
+residual, FFN-up + bias + GELU-tanh, FFN-down + bias + residual.  Tokens are
+sharded over N GPUs (whole samples per rank while N <= 2; beyond that each
+sample's ranks all-gather its K/V over NCCL every layer), weights
+replicated, the final output all-gathered (strong scaling: the total work
+is fixed).  ``value`` = tokens/s of the whole job (35552 tokens per forward /
+max-over-ranks forward time); the line also carries the algorithmic
+TFLOP/s (linears + attention products) and its fraction of the bf16 peak.
+
+``--workload dit_block`` (config 4) times the four DiT block linears alone
+(value in TFLOP/s), ``square`` an N^3 GEMM (config 2), ``skinny`` a
+skinny-M linear replayed from a CUDA graph (config 3, HBM GB/s).
 
 Timing: W warm-up steps, then exactly K steps, each bracketed by CUDA events
 on the launching stream; a 512 MiB buffer (> the 126 MB L2) is written
@@ -308,10 +315,12 @@ def _unit(workload):
 
 def _config(args, world):
     if args.workload == "dit_stack":
-        return {"workload": f"dit_stack (config 5): {args.layers} layers, 30 heads x 64, query chunks of {args.chunk}",
+        fused = os.environ.get("SF_ATTN_FUSED", "1") != "0"
+        attn = "fused attention" if fused else f"unfused attention, query chunks of {args.chunk}"
+        return {"workload": f"dit_stack (config 5): {args.layers} layers, 30 heads x 64, {attn}",
                 "tokens": M_TOTAL, "hidden": HIDDEN, "global_batch": BATCH, "seq_len": TOKENS,
                 "layers": args.layers, "parallelism": f"token-shard{world}",
-                "l2": "inputs and per-chunk scores (>= 4 GB) larger than L2; 512 MiB write between steps"}
+                "l2": "per-layer activations (>= 1.5 GB) larger than L2; 512 MiB write between steps"}
     if args.workload == "dit_block":
         return {"workload": "dit_block_linears (config 4)", "tokens": M_TOTAL, "hidden": HIDDEN,
                 "global_batch": BATCH, "seq_len": TOKENS, "parallelism": f"m-shard{world}",
@@ -581,7 +590,8 @@ def run_gpu_arm(args, dist):
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get(args.workload)
+            t = json.load(open(tpath)).get(args.workload)
+            traffic = t.get("bytes_per_launch") if isinstance(t, dict) else t
         except Exception:
             traffic = None
 
@@ -707,7 +717,7 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="dit_block", choices=["dit_stack", "dit_block", "square", "skinny"])
+    ap.add_argument("--workload", default="dit_stack", choices=["dit_stack", "dit_block", "square", "skinny"])
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--skinny-n", type=int, default=11008)
     ap.add_argument("--chunk", type=int, default=2048, help="attention query chunk (dit_stack)")
