@@ -233,7 +233,7 @@ def _bf16_neighbours(p: np.ndarray, p_dtype: str):
 
 def flash_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
                     block: int = 128, p_dtype: str = "bf16", flip_tol: float = 2.0 ** -12,
-                    return_allowance: bool = False):
+                    return_allowance: bool = False, integer_base: bool = False):
     """Attention ``softmax(scale * q k^T) v`` for one head, restated in the
     online (blockwise) form the fused device kernel computes, so that the
     P.V operand is rounded where the device rounds it.
@@ -245,6 +245,13 @@ def flash_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
     ``p_ij = 2^(c s_ij - m')`` (fp32), ``l = alpha l + sum_j p_ij``,
     ``o = alpha o + round(p) v_block``; finally ``o / l``.  ``p_dtype`` is the
     storage type of the P operand (the device's 16-bit MMA input).
+
+    ``integer_base`` rounds each row's base up to an integer
+    (``m' = max(m, ceil(c * max_j s_ij))``).  With integer bases the rounding
+    of ``2^(c s - m)`` does not depend on which base is used (a change of base
+    scales every p by an exact power of two), so this also stands for the
+    device kernel that raises its integer base only when a block exceeds it
+    by more than 8.
 
     With ``return_allowance`` it also returns, per output element, the
     change that rounding p the other way could cause for every p lying
@@ -263,7 +270,10 @@ def flash_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
     a = np.zeros((n, v.shape[1]), np.float64)
     for j0 in range(0, k.shape[0], block):
         s = (q @ k[j0:j0 + block].T).astype(np.float32)
-        m_new = np.maximum(m, s.max(axis=1) * c)
+        cand = s.max(axis=1) * c
+        if integer_base:
+            cand = np.ceil(cand)
+        m_new = np.maximum(m, cand)
         alpha = np.exp2(m - m_new).astype(np.float32)
         p = np.exp2(s * c - m_new[:, None]).astype(np.float32)
         l = l * alpha + p.sum(axis=1, dtype=np.float32)

@@ -959,19 +959,80 @@ int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float m
 
 // ───────────────────────────── fused attention ─────────────────────────────
 
-template <bool BF16, int SB>
+// Fused-attention configurations (see AttnCfg): variant 1 = 128-key blocks,
+// single-buffered scores, two CTAs per SM; 2 = 128-key blocks,
+// double-buffered, one CTA per SM; 3 = 96-key blocks, double-buffered
+// scores, two CTAs per SM.
+using AttnCfgV1 = AttnCfg<128, 1, 1, 2, 2>;
+using AttnCfgV2 = AttnCfg<128, 2, 2, 2, 4>;
+using AttnCfgV3 = AttnCfg<96, 2, 1, 1, 2>;
+// attention_fwd2_kernel (O in TMEM, lazily rescaled integer bases): variant 4 =
+// 64-key blocks, three CTAs per SM; 5 = 128-key blocks, two CTAs per SM.
+using Attn2CfgV4 = Attn2Cfg<64, 2>;
+using Attn2CfgV5 = Attn2Cfg<128, 2>;
+
+template <bool BF16, class Cfg>
+static int32_t launch_attention2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                                 const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
+                                 int device) {
+  static bool attr_set[64] = {false};
+  if (device < 64 && !attr_set[device]) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Cfg>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
+    attr_set[device] = true;
+  }
+  attention_fwd2_kernel<BF16, Cfg><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
+  return SF_OK;
+}
+
+template <bool BF16, class Cfg, int EMU>
 static int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
                                 const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
                                 int device) {
   static bool attr_set[64] = {false};
   if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<BF16, SB>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     AttnCfg<SB>::BYTES));
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<BF16, Cfg, EMU>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
     attr_set[device] = true;
   }
-  attention_fwd_kernel<BF16, SB><<<grid, kAttnThreads, AttnCfg<SB>::BYTES, s>>>(mq, mk, mv, a);
+  attention_fwd_kernel<BF16, Cfg, EMU><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
   return SF_OK;
+}
+
+template <bool BF16, class Cfg>
+static int32_t launch_attention_emu(int emu, const dim3& grid, const CUtensorMap& mq,
+                                    const CUtensorMap& mk, const CUtensorMap& mv,
+                                    const AttnArgs& a, cudaStream_t s, int device) {
+  switch (emu) {
+    case 0: return launch_attention<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
+    case 1: return launch_attention<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
+    case 3: return launch_attention<BF16, Cfg, 3>(grid, mq, mk, mv, a, s, device);
+    default: return launch_attention<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
+  }
+}
+
+template <bool BF16>
+static int32_t launch_attention_variant(int variant, int emu, const dim3& grid,
+                                        const CUtensorMap& mq, const CUtensorMap& mk,
+                                        const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
+                                        int device) {
+  switch (variant) {
+    case 4: return launch_attention2<BF16, Attn2CfgV4>(grid, mq, mk, mv, a, s, device);
+    case 5: return launch_attention2<BF16, Attn2CfgV5>(grid, mq, mk, mv, a, s, device);
+    case 2: return launch_attention<BF16, AttnCfgV2, 0>(grid, mq, mk, mv, a, s, device);
+    case 3: return launch_attention_emu<BF16, AttnCfgV3>(emu, grid, mq, mk, mv, a, s, device);
+    default: return launch_attention_emu<BF16, AttnCfgV1>(emu, grid, mq, mk, mv, a, s, device);
+  }
+}
+
+static int attn_key_block(int variant) {
+  switch (variant) {
+    case 2: return AttnCfgV2::KB;
+    case 3: return AttnCfgV3::KB;
+    case 4: return Attn2CfgV4::KB;
+    case 5: return Attn2CfgV5::KB;
+    default: return AttnCfgV1::KB;
+  }
 }
 
 extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
@@ -1001,16 +1062,18 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
   if (st != SF_OK) return st;
   if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
   const CUtensorMapDataType dt = tma_dtype(dtype);
+  const int variant = env_int("SF_ATTN_VARIANT", 4);  // tuning knob: see AttnCfgV1..V3, Attn2CfgV4..V5
+  const uint32_t kb = static_cast<uint32_t>(attn_key_block(variant));
   CUtensorMap mq, mk, mv;
   MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
              static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldq, head_dim, q_bstride,
              static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
   MapSpec sk{k, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
              static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldk, head_dim, k_bstride,
-             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+             static_cast<uint32_t>(head_dim), kb};
   MapSpec sv{v, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
              static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldv, head_dim, v_bstride,
-             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+             static_cast<uint32_t>(head_dim), kb};
   if ((st = encode_map(&mq, sq)) != SF_OK) return st;
   if ((st = encode_map(&mk, sk)) != SF_OK) return st;
   if ((st = encode_map(&mv, sv)) != SF_OK) return st;
@@ -1025,16 +1088,15 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
   a.ldo = ldo;
   a.o_bstride = o_bstride;
   a.err = dev->err_word;
+  a.sleep_ns = env_int("SF_ATTN_SLEEP", 0);  // tuning knob
   const dim3 grid(static_cast<unsigned>(ceil_div(q_len, kAttnBlock)), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int sb = env_int("SF_ATTN_SB", 1) == 2 ? 2 : 1;  // tuning knob: score/P buffering
-  if (dtype == kBF16)
-    st = sb == 1 ? launch_attention<true, 1>(grid, mq, mk, mv, a, s, device)
-                 : launch_attention<true, 2>(grid, mq, mk, mv, a, s, device);
-  else
-    st = sb == 1 ? launch_attention<false, 1>(grid, mq, mk, mv, a, s, device)
-                 : launch_attention<false, 2>(grid, mq, mk, mv, a, s, device);
+  // Share of the exp2 pairs computed on the FMA pipe, in quarters (tuning knob).
+  const int emu = env_int("SF_ATTN_EMU", 2);
+  st = dtype == kBF16
+           ? launch_attention_variant<true>(variant, emu, grid, mq, mk, mv, a, s, device)
+           : launch_attention_variant<false>(variant, emu, grid, mq, mk, mv, a, s, device);
   if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
   return SF_OK;

@@ -4,7 +4,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.gpu_util import assert_close_16bit, assert_close_fp32, np_dtype, to_device, to_host32
+from tests.gpu_util import (assert_close_16bit, assert_close_fp32, attn_oracle_opts, np_dtype,
+                            to_device, to_host32)
 
 pytestmark = pytest.mark.gpu
 
@@ -116,7 +117,8 @@ def test_fused_attention_dit_layout(gpu, ops, dt, batch, tokens, heads):
         X = qkv[b * tokens:(b + 1) * tokens]
         for h in range(heads):
             q, k, v = (X[:, s * C + h * 64:s * C + (h + 1) * 64] for s in range(3))
-            ref, allow = O.flash_attention(q, k, v, 0.125, p_dtype=dt, return_allowance=True)
+            ref, allow = O.flash_attention(q, k, v, 0.125, p_dtype=dt, return_allowance=True,
+                                           **attn_oracle_opts())
             p = O.softmax_rows((q @ k.T * np.float32(0.125)).astype(np.float32))
             _check_attn(out[b * tokens:(b + 1) * tokens, h * 64:(h + 1) * 64], ref,
                         O.abs_product(p, v.T), allow, f"fused {dt} B={batch} N={tokens} b{b} h{h}")
@@ -143,7 +145,7 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
             s = q[b][:, sl] @ k[b][:, sl].T * np.float32(0.125)
             p = O.softmax_rows(s.astype(np.float32))
             ref, allow = O.flash_attention(q[b][:, sl], k[b][:, sl], v[b][:, sl], 0.125,
-                                           return_allowance=True)
+                                           return_allowance=True, **attn_oracle_opts())
             ap = O.abs_product(p, v[b][:, sl].T)
             _check_attn(out[b * Lq:(b + 1) * Lq, sl], ref, ap, allow, f"b{b} h{h}")
     assert device_error(0) == 0

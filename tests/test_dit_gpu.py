@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests.gpu_util import assert_close_16bit, np_dtype, to_host32
+from tests.gpu_util import attn_oracle_opts, assert_close_16bit, np_dtype, to_host32
 
 pytestmark = pytest.mark.gpu
 
@@ -179,7 +179,8 @@ def test_full_size_attention_sampled_rows(gpu, ops, fused):
                           keys[:, Cw + h * D:Cw + (h + 1) * D])
             s = (qh @ kh.T) * np.float32(0.125)
             if fused:
-                o, a = O.flash_attention(qh, kh, vh, 0.125, return_allowance=True)
+                o, a = O.flash_attention(qh, kh, vh, 0.125, return_allowance=True,
+                                         **attn_oracle_opts())
                 ref[h * D:(h + 1) * D], allow[h * D:(h + 1) * D] = o[0], a[0]
                 absprod[h * D:(h + 1) * D] = O.abs_product(O.softmax_rows(s), vh.T)[0]
             else:
@@ -219,7 +220,8 @@ def test_stack_small_fused_matches_oracle(gpu, ops):
                 rs = slice(b * N, (b + 1) * N)
                 qh, kh = q[rs, h * D:(h + 1) * D], kv[rs, h * D:(h + 1) * D]
                 vh = kv[rs, Cw + h * D:Cw + (h + 1) * D]
-                ref, allow = O.flash_attention(qh, kh, vh, 1.0 / np.sqrt(D), return_allowance=True)
+                ref, allow = O.flash_attention(qh, kh, vh, 1.0 / np.sqrt(D), return_allowance=True,
+                                               **attn_oracle_opts())
                 p = O.softmax_rows((qh @ kh.T * np.float32(1.0 / np.sqrt(D))).astype(np.float32))
                 ok, stt = O.elementwise_rel_check(attn[rs, h * D:(h + 1) * D], ref,
                                                   absprod=O.abs_product(p, vh.T), allowance=allow)
