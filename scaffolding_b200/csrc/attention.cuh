@@ -524,7 +524,8 @@ struct Attn2Cfg {
   static_assert((1 + 2 * KV_STAGES + 5) * 8 + 8 <= 256, "barrier area");
 };
 
-template <bool BF16, class Cfg>
+// EMU of every four exp2 pairs of a full block go through exp2_poly2.
+template <bool BF16, class Cfg, int EMU>
 __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
     attention_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ,
                           const __grid_constant__ CUtensorMap tmK,
@@ -754,8 +755,12 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
           for (int t = 0; t < 32; t += 2) {
             float x0, x1;
             fma2(x0, x1, pv[t], pv[t + 1], c, c, nm, nm);
-            pv[t] = ex2_approx(x0);
-            pv[t + 1] = ex2_approx(x1);
+            if (((t >> 1) & 3) < EMU) {
+              exp2_poly2(pv[t], pv[t + 1], x0, x1);
+            } else {
+              pv[t] = ex2_approx(x0);
+              pv[t + 1] = ex2_approx(x1);
+            }
             add2(sp[(t >> 1) & 2], sp[((t >> 1) & 2) + 1], pv[t], pv[t + 1]);
           }
         } else {

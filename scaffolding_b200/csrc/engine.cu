@@ -971,18 +971,29 @@ using AttnCfgV3 = AttnCfg<96, 2, 1, 1, 2>;
 using Attn2CfgV4 = Attn2Cfg<64, 2>;
 using Attn2CfgV5 = Attn2Cfg<128, 2>;
 
-template <bool BF16, class Cfg>
+template <bool BF16, class Cfg, int EMU>
 static int32_t launch_attention2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
                                  const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
                                  int device) {
   static bool attr_set[64] = {false};
   if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Cfg>,
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Cfg, EMU>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
     attr_set[device] = true;
   }
-  attention_fwd2_kernel<BF16, Cfg><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
+  attention_fwd2_kernel<BF16, Cfg, EMU><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
   return SF_OK;
+}
+
+template <bool BF16, class Cfg>
+static int32_t launch_attention2_emu(int emu, const dim3& grid, const CUtensorMap& mq,
+                                     const CUtensorMap& mk, const CUtensorMap& mv,
+                                     const AttnArgs& a, cudaStream_t s, int device) {
+  switch (emu) {
+    case 1: return launch_attention2<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
+    case 2: return launch_attention2<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
+    default: return launch_attention2<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
+  }
 }
 
 template <bool BF16, class Cfg, int EMU>
@@ -1017,8 +1028,8 @@ static int32_t launch_attention_variant(int variant, int emu, const dim3& grid,
                                         const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
                                         int device) {
   switch (variant) {
-    case 4: return launch_attention2<BF16, Attn2CfgV4>(grid, mq, mk, mv, a, s, device);
-    case 5: return launch_attention2<BF16, Attn2CfgV5>(grid, mq, mk, mv, a, s, device);
+    case 4: return launch_attention2_emu<BF16, Attn2CfgV4>(emu, grid, mq, mk, mv, a, s, device);
+    case 5: return launch_attention2_emu<BF16, Attn2CfgV5>(emu, grid, mq, mk, mv, a, s, device);
     case 2: return launch_attention<BF16, AttnCfgV2, 0>(grid, mq, mk, mv, a, s, device);
     case 3: return launch_attention_emu<BF16, AttnCfgV3>(emu, grid, mq, mk, mv, a, s, device);
     default: return launch_attention_emu<BF16, AttnCfgV1>(emu, grid, mq, mk, mv, a, s, device);
@@ -1093,7 +1104,7 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
                   static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Share of the exp2 pairs computed on the FMA pipe, in quarters (tuning knob).
-  const int emu = env_int("SF_ATTN_EMU", 2);
+  const int emu = env_int("SF_ATTN_EMU", 0);
   st = dtype == kBF16
            ? launch_attention_variant<true>(variant, emu, grid, mq, mk, mv, a, s, device)
            : launch_attention_variant<false>(variant, emu, grid, mq, mk, mv, a, s, device);
