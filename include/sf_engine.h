@@ -187,6 +187,27 @@ int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv
                          int64_t ldv, int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
                          float scale, int32_t dtype, void* stream);
 
+/* sf_attention_fwd over part of the keys, for overlapping a key exchange
+ * with attention (the token-sharded DiT stack: attention over a rank's own
+ * keys while the other ranks' keys are gathered, then over the gathered
+ * ones).  Keys [skip_lo, skip_hi) are left out (skip_lo = skip_hi = kv_len:
+ * none).  part_mode 1 writes this pass's unnormalised fp32 output to part_o
+ * ([batch][q_len][heads][64]) and each row's (integer exponent base, sum) to
+ * part_ml ([batch][q_len][heads][2]) instead of o; part_mode 2 merges such
+ * a partial result with this pass and writes the normalised o; part_mode 0
+ * is sf_attention_fwd with the skip.  The split result equals the one-pass
+ * result up to fp32 summation order (the merge scales by exact powers of
+ * two).  Same DiT attention the entry above replaces
+ * (diffusion/models.py:529-536; nn/parallel.py:45-290 is the reference's
+ * multi-GPU wrapper, which gathers on the host instead). */
+int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                                 int32_t head_dim, const void* q, int64_t ldq,
+                                 int64_t q_bstride, const void* k, int64_t ldk,
+                                 int64_t k_bstride, const void* v, int64_t ldv,
+                                 int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
+                                 float scale, int32_t dtype, int32_t skip_lo, int32_t skip_hi,
+                                 float* part_o, float* part_ml, int32_t part_mode, void* stream);
+
 /* y[i] = act(alpha * x[i]).  Replaces cuda_silu_f32 / cuda_gelu_f32 /
  * cuda_muls_f32 (_cuda_ops_decl.h:69, :74, :63; _cuda_kernels.cu:384, :428,
  * :237-277) for the standalone dev_silu / dev_gelu / dev_muls calls. */
@@ -244,6 +265,12 @@ int32_t sf_memset(void* dst, int32_t value, size_t bytes, void* stream);
 
 /* Streams and events (_cuda_ops.pyx:608-673). */
 int32_t sf_stream_create(int32_t device, int32_t non_blocking, void** stream);
+/* A stream whose kernels the scheduler prefers (high_priority != 0) or the
+ * default priority: a collective issued on it gets SMs while a long kernel on
+ * another stream is still filling the GPU (no counterpart in the reference,
+ * whose streams are all default priority, _cuda_ops.pyx:608-640). */
+int32_t sf_stream_create_priority(int32_t device, int32_t non_blocking, int32_t high_priority,
+                                  void** stream);
 int32_t sf_stream_destroy(void* stream);
 int32_t sf_stream_synchronize(void* stream);
 int32_t sf_stream_wait_event(void* stream, void* event);

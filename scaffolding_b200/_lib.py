@@ -79,6 +79,9 @@ SIGNATURES: dict[str, list] = {
     "sf_softmax_rows": [_vp, _i32, _i64, _vp, _i32, _i64, _i64, _i64, C.c_float, _vp],
     "sf_attention_fwd": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp,
                          _i64, _i64, _vp, _i64, _i64, C.c_float, _i32, _vp],
+    "sf_attention_fwd_partial": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64,
+                                 _vp, _i64, _i64, _vp, _i64, _i64, C.c_float, _i32, _i32, _i32,
+                                 _vp, _vp, _i32, _vp],
     "sf_unary": [_vp, _i32, _vp, _i32, _i64, C.c_float, _i32, _vp],
     "sf_device_count": [_P(_i32)],
     "sf_set_device": [_i32],
@@ -97,6 +100,7 @@ SIGNATURES: dict[str, list] = {
     "sf_memcpy_peer": [_vp, _i32, _vp, _i32, _sz, _vp],
     "sf_memset": [_vp, _i32, _sz, _vp],
     "sf_stream_create": [_i32, _i32, _P(_vp)],
+    "sf_stream_create_priority": [_i32, _i32, _i32, _P(_vp)],
     "sf_stream_destroy": [_vp],
     "sf_stream_synchronize": [_vp],
     "sf_stream_wait_event": [_vp, _vp],

@@ -47,6 +47,18 @@ struct AttnArgs {
   int64_t ldo, o_bstride;  // elements
   int* err;
   int sleep_ns;          // poll back-off of the softmax warps' waits (0 = spin)
+  // attention_fwd2_kernel only: keys [skip_lo, skip_hi) are left out (none
+  // when skip_lo == skip_hi == kv_len), and part_mode selects the output:
+  //   0  normalised 16-bit O;
+  //   1  write the partial result: unnormalised fp32 O to part_o and the
+  //      row's (integer base m, sum l) to part_ml;
+  //   2  merge with the partial result in part_o / part_ml, then write the
+  //      normalised 16-bit O.
+  // part_o is [batch][q_len][heads][64] fp32, part_ml [batch][q_len][heads][2].
+  int skip_lo, skip_hi;
+  int part_mode;
+  float* part_o;
+  float* part_ml;
 };
 
 constexpr int kAttnBlock = 128;   // queries per CTA and keys per block
@@ -550,7 +562,13 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int nblk = (p.kv_len + KB - 1) / KB;
+  // Key blocks over [0, skip_lo) then [skip_hi, kv_len).
+  const int nb0 = (p.skip_lo + KB - 1) / KB;
+  const int nblk = nb0 + (p.kv_len - p.skip_hi + KB - 1) / KB;
+  auto block_start = [&](int j) { return j < nb0 ? j * KB : p.skip_hi + (j - nb0) * KB; };
+  auto block_valid = [&](int j) {
+    return j < nb0 ? min(KB, p.skip_lo - j * KB) : min(KB, p.kv_len - block_start(j));
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -596,8 +614,8 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         }
         uint8_t* kt = smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE;
         mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::KV_TILE);
-        tma_load_4d(kt, &tmK, &kv_full[stage], 0, j * KB, h, b);
-        tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, j * KB, h, b);
+        tma_load_4d(kt, &tmK, &kv_full[stage], 0, block_start(j), h, b);
+        tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, block_start(j), h, b);
         ++issued;
         if (++stage == ST) {
           stage = 0;
@@ -696,7 +714,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         break;
       }
       tc_fence_after();
-      const int valid = min(KB, p.kv_len - j * KB);
+      const int valid = block_valid(j);
       const bool full = valid == KB;
       float mxc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -797,6 +815,22 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
     const int qrow = qb * kAttnBlock + row;
     if (ok) {
       tc_fence_after();
+      const bool live = qrow < p.q_len;
+      const int64_t prow = (static_cast<int64_t>(b) * p.q_len + qrow) * p.heads + h;
+      // Merge with a partial result over other keys: both bases are integers,
+      // so the rescale factors are exact powers of two.
+      float a_own = 1.0f, a_part = 0.0f;
+      if (p.part_mode == 2 && live) {
+        const float m_p = p.part_ml[2 * prow], l_p = p.part_ml[2 * prow + 1];
+        const float m = fmaxf(m_run, m_p);
+        a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
+        a_part = ex2_approx(m_p - m);
+        l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
+      }
+      if (p.part_mode == 1 && live) {
+        p.part_ml[2 * prow] = m_run;
+        p.part_ml[2 * prow + 1] = l_run;
+      }
       const float inv = 1.0f / l_run;
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
                      (static_cast<int64_t>(b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
@@ -805,15 +839,36 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       for (int half = 0; half < 2; ++half) {
         tmem_ld32(o_addr + half * 32, r);
         tmem_ld_wait();
-        if (qrow < p.q_len) {
+        if (!live) continue;
+        if (p.part_mode == 1) {
+          float4* po = reinterpret_cast<float4*>(p.part_o + prow * kAttnD + half * 32);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            reinterpret_cast<uint4*>(dst)[half * 4 + q] = make_uint4(
-                pack_16bit(__uint_as_float(r[8 * q]) * inv, __uint_as_float(r[8 * q + 1]) * inv, BF16),
-                pack_16bit(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv, BF16),
-                pack_16bit(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv, BF16),
-                pack_16bit(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv, BF16));
+          for (int q = 0; q < 8; ++q)
+            po[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          continue;
         }
+        float ov[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) ov[t] = nblk > 0 ? __uint_as_float(r[t]) : 0.0f;
+        if (p.part_mode == 2) {
+          const float4* po = reinterpret_cast<const float4*>(p.part_o + prow * kAttnD + half * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = po[q];
+            ov[4 * q] = ov[4 * q] * a_own + v.x * a_part;
+            ov[4 * q + 1] = ov[4 * q + 1] * a_own + v.y * a_part;
+            ov[4 * q + 2] = ov[4 * q + 2] * a_own + v.z * a_part;
+            ov[4 * q + 3] = ov[4 * q + 3] * a_own + v.w * a_part;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(dst)[half * 4 + q] =
+              make_uint4(pack_16bit(ov[8 * q] * inv, ov[8 * q + 1] * inv, BF16),
+                         pack_16bit(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv, BF16),
+                         pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
+                         pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
       }
     }
   }

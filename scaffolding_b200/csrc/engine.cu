@@ -1046,12 +1046,53 @@ static int attn_key_block(int variant) {
   }
 }
 
+static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                              int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
+                              const void* k, int64_t ldk, int64_t k_bstride, const void* v,
+                              int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
+                              int64_t o_bstride, float scale, int32_t dtype, int32_t skip_lo,
+                              int32_t skip_hi, float* part_o, float* part_ml, int32_t part_mode,
+                              void* stream);
+
 extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                                     int32_t head_dim, const void* q, int64_t ldq,
                                     int64_t q_bstride, const void* k, int64_t ldk,
                                     int64_t k_bstride, const void* v, int64_t ldv,
                                     int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
                                     float scale, int32_t dtype, void* stream) {
+  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
+                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, kv_len,
+                        kv_len, nullptr, nullptr, 0, stream);
+}
+
+extern "C" int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len,
+                                            int32_t kv_len, int32_t head_dim, const void* q,
+                                            int64_t ldq, int64_t q_bstride, const void* k,
+                                            int64_t ldk, int64_t k_bstride, const void* v,
+                                            int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
+                                            int64_t o_bstride, float scale, int32_t dtype,
+                                            int32_t skip_lo, int32_t skip_hi, float* part_o,
+                                            float* part_ml, int32_t part_mode, void* stream) {
+  if (part_mode < 0 || part_mode > 2)
+    return fail(SF_ERR_INVALID_ARGUMENT, "partial mode %d", part_mode);
+  if (skip_lo < 0 || skip_hi < skip_lo || skip_hi > kv_len)
+    return fail(SF_ERR_INVALID_ARGUMENT, "skipped keys [%d, %d) outside [0, %d]", skip_lo, skip_hi, kv_len);
+  if (part_mode != 0 && (!part_o || !part_ml || !aligned16(part_o) || (reinterpret_cast<uintptr_t>(part_ml) & 7u)))
+    return fail(SF_ERR_INVALID_ARGUMENT, "partial buffers missing or misaligned");
+  if (part_mode != 2 && skip_hi - skip_lo == kv_len && kv_len > 0)
+    return fail(SF_ERR_INVALID_ARGUMENT, "every key skipped");
+  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
+                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, skip_lo,
+                        skip_hi, part_o, part_ml, part_mode, stream);
+}
+
+static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                              int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
+                              const void* k, int64_t ldk, int64_t k_bstride, const void* v,
+                              int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
+                              int64_t o_bstride, float scale, int32_t dtype, int32_t skip_lo,
+                              int32_t skip_hi, float* part_o, float* part_ml, int32_t part_mode,
+                              void* stream) {
   if (batch < 0 || heads < 0 || q_len < 0 || kv_len < 0)
     return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
   if (batch == 0 || heads == 0 || q_len == 0) return SF_OK;
@@ -1074,6 +1115,8 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
   if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
   const CUtensorMapDataType dt = tma_dtype(dtype);
   const int variant = env_int("SF_ATTN_VARIANT", 4);  // tuning knob: see AttnCfgV1..V3, Attn2CfgV4..V5
+  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && variant != 4 && variant != 5)
+    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variant 4 or 5)");
   const uint32_t kb = static_cast<uint32_t>(attn_key_block(variant));
   CUtensorMap mq, mk, mv;
   MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
@@ -1100,6 +1143,11 @@ extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len,
   a.o_bstride = o_bstride;
   a.err = dev->err_word;
   a.sleep_ns = env_int("SF_ATTN_SLEEP", 0);  // tuning knob
+  a.skip_lo = skip_lo;
+  a.skip_hi = skip_hi;
+  a.part_mode = part_mode;
+  a.part_o = part_o;
+  a.part_ml = part_ml;
   const dim3 grid(static_cast<unsigned>(ceil_div(q_len, kAttnBlock)), static_cast<unsigned>(heads),
                   static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);

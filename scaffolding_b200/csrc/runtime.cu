@@ -333,6 +333,20 @@ int32_t sf_stream_create(int32_t device, int32_t non_blocking, void** stream) {
   return SF_OK;
 }
 
+int32_t sf_stream_create_priority(int32_t device, int32_t non_blocking, int32_t high_priority,
+                                  void** stream) {
+  if (!stream) return fail(SF_ERR_INVALID_ARGUMENT, "null output");
+  DeviceGuard g(device);
+  int least = 0, greatest = 0;
+  SF_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  cudaStream_t s;
+  SF_CUDA_TRY(cudaStreamCreateWithPriority(
+      &s, non_blocking ? cudaStreamNonBlocking : cudaStreamDefault,
+      high_priority ? greatest : least));
+  *stream = s;
+  return SF_OK;
+}
+
 int32_t sf_stream_destroy(void* stream) {
   if (stream) SF_CUDA_TRY(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
   return SF_OK;

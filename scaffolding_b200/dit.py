@@ -212,6 +212,27 @@ class DitStack:
         self.y = [ops._alloc((m, Cw), bf, device), ops._alloc((m, Cw), bf, device)]
         self.out_full = (ops._alloc((plan.batch * plan.tokens, Cw), bf, device)
                          if plan.world > 1 else None)
+        # Overlap of the K/V all-gather with attention over the rank's own keys
+        # (fused TMEM-accumulator kernel only): attention over kv_local writes a
+        # partial result while the gather runs on a side stream; attention over
+        # the gathered keys (minus the local slice) merges it.
+        self.overlap = (self.fused and plan.kv_exchange
+                        and os.environ.get("SF_KV_OVERLAP", "1") != "0"
+                        and os.environ.get("SF_ATTN_VARIANT", "4") in ("4", "5"))
+        self.part_o = self.part_ml = None
+        self.comm_stream = self.ev_kv = self.ev_gather = None
+        if self.overlap:
+            self.part_o = ops._alloc((m, Cw), np.float32, device)
+            self.part_ml = ops._alloc((m, heads, 2), np.float32, device)
+            if kv_comm is not None:
+                sp, e1, e2 = C.c_void_p(), C.c_void_p(), C.c_void_p()
+                # high priority: the gather's kernel is scheduled onto SMs as
+                # soon as attention blocks retire instead of after them all
+                check(lib.sf_stream_create_priority(device, 1, 1, C.byref(sp)),
+                      "sf_stream_create_priority")
+                check(lib.sf_event_create(0, C.byref(e1)), "sf_event_create")
+                check(lib.sf_event_create(0, C.byref(e2)), "sf_event_create")
+                self.comm_stream, self.ev_kv, self.ev_gather = sp.value, e1.value, e2.value
 
     # ── launches
     def _gemm(self, name, timer, stream, *args, **kw):
@@ -228,6 +249,32 @@ class DitStack:
         q_rows = p.tokens if p.whole_samples else p.m
         scale = 1.0 / math.sqrt(D)
         bf = DT_BF16
+        if self.overlap:
+            import ctypes as C
+
+            from ._lib import check, lib
+            m = p.m
+            if timer is not None:
+                timer.start("attn")
+            # own keys (kv_local) -> partial result
+            E.attention_partial(1, H, m, m, self.q.ptr, Cw, m * Cw, self.kv_local.ptr, 2 * Cw,
+                                m * 2 * Cw, self.kv_local.ptr + Cw * 2, 2 * Cw, m * 2 * Cw,
+                                self.attn.ptr, Cw, m * Cw, scale, m, m, self.part_o.ptr,
+                                self.part_ml.ptr, 1, dtype=bf, head_dim=D, stream=stream,
+                                device=self.dev)
+            if self.comm_stream is not None:
+                s = stream if stream else E.get_stream(self.dev)
+                check(lib.sf_stream_wait_event(C.c_void_p(s), C.c_void_p(self.ev_gather)),
+                      "sf_stream_wait_event")
+            # the group's other keys (the local slice skipped), merged
+            E.attention_partial(1, H, m, keys, self.q.ptr, Cw, m * Cw, self.kv_full.ptr, 2 * Cw,
+                                keys * 2 * Cw, self.kv_full.ptr + Cw * 2, 2 * Cw, keys * 2 * Cw,
+                                self.attn.ptr, Cw, m * Cw, scale, p.token0, p.token0 + m,
+                                self.part_o.ptr, self.part_ml.ptr, 2, dtype=bf, head_dim=D,
+                                stream=stream, device=self.dev)
+            if timer is not None:
+                timer.stop("attn")
+            return
         if self.fused:
             # Q rows of each local sample; K and V in place in the [keys, 2C]
             # rows of kv_full (K at column 0, V at column C, head h at h*64).
@@ -276,6 +323,19 @@ class DitStack:
         from ._lib import check, lib
         p = self.plan
         if not p.kv_exchange:
+            return
+        if self.comm_stream is not None:
+            # gather on the side stream once the K/V projection is done; the
+            # attention over the gathered keys waits for ev_gather
+            s = stream if stream else E.get_stream(self.dev)
+            check(lib.sf_event_record(C.c_void_p(self.ev_kv), C.c_void_p(s)), "sf_event_record")
+            check(lib.sf_stream_wait_event(C.c_void_p(self.comm_stream), C.c_void_p(self.ev_kv)),
+                  "sf_stream_wait_event")
+            check(lib.sf_comm_allgather(C.c_void_p(self.kv_comm), C.c_void_p(self.kv_local.ptr),
+                                        C.c_void_p(self.kv_full.ptr), p.m * 2 * self.C * 2,
+                                        C.c_void_p(self.comm_stream)), "sf_comm_allgather")
+            check(lib.sf_event_record(C.c_void_p(self.ev_gather), C.c_void_p(self.comm_stream)),
+                  "sf_event_record")
             return
         if timer is not None:
             timer.start("kv_allgather")
@@ -336,7 +396,7 @@ class DitStack:
     def launches_per_forward(self) -> int:
         p = self.plan
         if self.fused:
-            return self.L * 6
+            return self.L * (7 if self.overlap else 6)
         q_rows = p.tokens if p.whole_samples else p.m
         chunks = (q_rows + self.chunk - 1) // self.chunk
         return self.L * (5 + 3 * chunks)

@@ -279,6 +279,23 @@ def attention(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride,
           "sf_attention_fwd")
 
 
+def attention_partial(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride, v, ldv,
+                      v_bstride, o, ldo, o_bstride, scale, skip_lo, skip_hi, part_o, part_ml,
+                      part_mode, dtype=DT_BF16, head_dim=64, stream=None, device=None):
+    """sf_attention_fwd_partial: attention over keys [0, kv_len) minus
+    [skip_lo, skip_hi); part_mode 1 writes the partial result to part_o /
+    part_ml, 2 merges it and writes o."""
+    dev = current_device() if device is None else device
+    s = get_stream(dev) if stream is None else stream
+    check(lib.sf_attention_fwd_partial(batch, heads, q_len, kv_len, head_dim, C.c_void_p(q), ldq,
+                                       q_bstride, C.c_void_p(k), ldk, k_bstride, C.c_void_p(v),
+                                       ldv, v_bstride, C.c_void_p(o), ldo, o_bstride, float(scale),
+                                       dtype, skip_lo, skip_hi, C.c_void_p(part_o),
+                                       C.c_void_p(part_ml), part_mode,
+                                       C.c_void_p(s) if s else None),
+          "sf_attention_fwd_partial")
+
+
 def unary(x, x_dt, y, y_dt, n, alpha=1.0, act=ACT_NONE, stream=None, device=None):
     dev = current_device() if device is None else device
     if stream is None:

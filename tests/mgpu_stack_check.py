@@ -69,10 +69,18 @@ def main():
             same = np.array_equal(got, ref)
             ok, stats = O.elementwise_rel_check(got, ref, rtol=1e-2, tau=1e-2)
             differ = int(np.count_nonzero(got != ref))
-            print(f"[mgpu] world={world} batch={B} kv_exchange={plan.kv_exchange} bitwise_equal={same} "
+            print(f"[mgpu] world={world} batch={B} kv_exchange={plan.kv_exchange} overlap={st.overlap} bitwise_equal={same} "
                   f"differing={differ}/{got.size} max_abs_diff={float(np.abs(got - ref).max()):.3e} "
-                  f"bf16_bar_ok={ok}", flush=True)
-            failures += 0 if same else 1
+                  f"bf16_bar_ok={ok} rel_frob={O.rel_frobenius(got, ref):.2e}", flush=True)
+            # With the K/V exchange overlapped, attention is split into the
+            # rank's own keys and the gathered ones (another fp32 summation
+            # order): the bf16 bar instead of bit equality.
+            split = plan.kv_exchange and st.overlap
+            # Two bf16 layers re-round every intermediate, so one-ulp flips in
+            # them carry into cancelling outputs: the aggregate bar here.
+            close = (O.rel_frobenius(got, ref) < 2e-3
+                     and float(np.abs(got - ref).max()) <= 2.0 ** -5 * float(np.abs(ref).max()))
+            failures += 0 if (close if split else same) else 1
         if kv:
             lib.sf_comm_destroy(C.c_void_p(kv))
         td.barrier()

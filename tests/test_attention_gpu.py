@@ -165,3 +165,53 @@ def test_fused_attention_rejects_bad_arguments(gpu, ops):
     # zero keys
     assert lib.sf_attention_fwd(1, 1, 8, 0, 64, p, 192, 0, p, 192, 0, p, 192, 0, p, 192, 0,
                                 1.0, 2, None) == SF_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("lo,hi", [(300, 500), (0, 256), (520, 700)])
+def test_fused_attention_split_keys_merge(gpu, ops, lo, hi):
+    """Two-pass attention as the sharded DiT stack runs it: keys [lo, hi)
+    from their own buffer (partial result written), then every other key
+    (skip [lo, hi)) merged with it.  Equals the one-pass kernel up to fp32
+    summation order, and the oracle with its usual bar."""
+    import ctypes as C
+
+    from scaffolding_b200 import engine as E
+    from tests.gpu_util import device_error
+    if attn_oracle_opts()["integer_base"] is False:
+        pytest.skip("partial attention needs the TMEM-accumulator kernel")
+    rng = np.random.default_rng(lo + hi)
+    B, H, Lq, Lk = 2, 3, 200, 700
+    W = H * 64
+    gq, q = to_device(ops, rng.standard_normal((B, Lq, W), dtype=np.float32), "bf16")
+    gk, k = to_device(ops, rng.standard_normal((B, Lk, W), dtype=np.float32), "bf16")
+    gv, v = to_device(ops, rng.standard_normal((B, Lk, W), dtype=np.float32), "bf16")
+    bf = np_dtype("bf16")
+    one = ops._alloc((B * Lq, W), bf, 0)
+    E.attention(B, H, Lq, Lk, gq.ptr, W, Lq * W, gk.ptr, W, Lk * W, gv.ptr, W, Lk * W,
+                one.ptr, W, Lq * W, 0.125)
+    part_o = ops._alloc((B * Lq * H * 64,), np.float32, 0)
+    part_ml = ops._alloc((B * Lq * H * 2,), np.float32, 0)
+    two = ops._alloc((B * Lq, W), bf, 0)
+    off = lo * W * 2  # the slice [lo, hi) as its own K/V buffer
+    E.attention_partial(B, H, Lq, hi - lo, gq.ptr, W, Lq * W, gk.ptr + off, W, Lk * W,
+                        gv.ptr + off, W, Lk * W, two.ptr, W, Lq * W, 0.125, hi - lo, hi - lo,
+                        part_o.ptr, part_ml.ptr, 1)
+    E.attention_partial(B, H, Lq, Lk, gq.ptr, W, Lq * W, gk.ptr, W, Lk * W, gv.ptr, W, Lk * W,
+                        two.ptr, W, Lq * W, 0.125, lo, hi, part_o.ptr, part_ml.ptr, 2)
+    a, b2 = to_host32(ops, one), to_host32(ops, two)
+    # one 16-bit ulp at most where the two summation orders round differently
+    assert np.abs(a - b2).max() <= 2.0 ** -7 * np.abs(a).max()
+    for b in range(B):
+        for h in range(H):
+            sl = slice(h * 64, (h + 1) * 64)
+            ref, allow = O.flash_attention(q[b][:, sl], k[b][:, sl], v[b][:, sl], 0.125,
+                                           return_allowance=True, **attn_oracle_opts())
+            p = O.softmax_rows((q[b][:, sl] @ k[b][:, sl].T * np.float32(0.125)).astype(np.float32))
+            _check_attn(b2[b * Lq:(b + 1) * Lq, sl], ref, O.abs_product(p, v[b][:, sl].T), allow,
+                        f"split [{lo},{hi}) b{b} h{h}")
+    assert device_error(0) == 0
+    from scaffolding_b200._lib import SF_ERR_INVALID_ARGUMENT, lib
+    assert lib.sf_attention_fwd_partial(B, H, Lq, Lk, 64, C.c_void_p(gq.ptr), W, Lq * W,
+                                        C.c_void_p(gk.ptr), W, Lk * W, C.c_void_p(gv.ptr), W,
+                                        Lk * W, C.c_void_p(two.ptr), W, Lq * W, 0.125, 2, 10, 1,
+                                        None, None, 1, None) == SF_ERR_INVALID_ARGUMENT

@@ -109,15 +109,22 @@ def test_stack_small_matches_oracle(gpu, ops):
     np.testing.assert_array_equal(_host(ops, st.y[(L - 1) % 2]), cur)
 
 
-@pytest.mark.parametrize("fused", [False, True])
-def test_sliced_ranks_equal_whole_sample(gpu, ops, fused):
+@pytest.mark.parametrize("mode", ["unfused", "fused", "fused_split"])
+def test_sliced_ranks_equal_whole_sample(gpu, ops, mode, monkeypatch):
     """Four emulated ranks holding half a sample each (K/V exchanged between
-    the two ranks of a sample) reproduce the one-rank result bit for bit:
-    every row goes through the same kernels over the same keys (shards of
-    300 rows take the same GEMM path as the whole 1200-row batch; the fused
-    attention computes each query row from its own scores only)."""
+    the two ranks of a sample) reproduce the one-rank result: bit for bit
+    when every row goes through the same kernels over the same keys (shards
+    of 300 rows take the same GEMM path as the whole 1200-row batch; the
+    fused attention computes each query row from its own scores only), and
+    within the bf16 bar when the fused attention is split into the rank's
+    own keys and the gathered ones (the overlapped exchange: another fp32
+    summation order)."""
     from scaffolding_b200 import dit
     from scaffolding_b200 import engine as E
+    fused = mode != "unfused"
+    monkeypatch.setenv("SF_KV_OVERLAP", "1" if mode == "fused_split" else "0")
+    if mode == "fused_split" and not attn_oracle_opts()["integer_base"]:
+        pytest.skip("split attention needs the TMEM-accumulator kernel")
     B, N, Cw, H, chunk = 2, 600, 256, 4, 160
     ws = _weights(1, Cw, 50)
     x = O.round_bf16(np.random.default_rng(51).standard_normal((B * N, Cw), dtype=np.float32))
@@ -130,6 +137,7 @@ def test_sliced_ranks_equal_whole_sample(gpu, ops, fused):
     ranks = [dit.DitStack(dit.ShardPlan(B, N, world, r), Cw, H, 1, 0, chunk=chunk, weights=ws,
                           fused=fused)
              for r in range(world)]
+    assert all(st.overlap == (mode == "fused_split") for st in ranks)
     outs = []
     for r, st in enumerate(ranks):
         st.qkv(0, gx.ptr + st.plan.row0 * Cw * 2)
@@ -143,7 +151,13 @@ def test_sliced_ranks_equal_whole_sample(gpu, ops, fused):
         st._attention(None, None)
         st.post(0, gx.ptr + st.plan.row0 * Cw * 2, st.y[0].ptr)
         outs.append(_host(ops, st.y[0]))
-    np.testing.assert_array_equal(np.concatenate(outs), ref)
+    got = np.concatenate(outs)
+    if mode == "fused_split":
+        # one layer: attention differs in fp32 order, then three bf16 linears
+        assert np.abs(got - ref).max() <= 2.0 ** -5 * np.abs(ref).max()
+        assert O.rel_frobenius(got, ref) < 2e-3
+    else:
+        np.testing.assert_array_equal(got, ref)
 
 
 @pytest.mark.parametrize("fused", [False, True])

@@ -15,15 +15,19 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def test_sharded_stack_equals_single_gpu(gpu, ops):
+@pytest.mark.parametrize("overlap", ["0", "1"])
+def test_sharded_stack_equals_single_gpu(gpu, ops, overlap):
+    """overlap=0: bit-identical to one GPU; overlap=1 (K/V all-gather on a
+    side stream behind attention over the rank's own keys): within the bf16
+    bar where the attention is split."""
     n = ops.get_device_count()
     if n < 2:
         pytest.skip("needs at least 2 GPUs")
     world = 4 if n >= 4 else 2
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SF_KV_OVERLAP=overlap)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
-           "--master-port", "29533", os.path.join(HERE, "mgpu_stack_check.py")]
+           "--master-port", str(29533 + int(overlap)), os.path.join(HERE, "mgpu_stack_check.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "[mgpu] OK" in r.stdout
