@@ -514,15 +514,26 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
 //     so the result equals the eager per-block rescale up to fp32 rounding.
 // With 64-key blocks a CTA needs 128 TMEM columns and ~64 KB of shared
 // memory, so three CTAs share an SM (three softmax warps per scheduler).
+//
+// PT (P in tensor memory, 64-key blocks only): the softmax warps store the
+// 16-bit P of block j over the first 32 columns of its own score buffer
+// (two values per 32-bit column) and P.V reads its A operand from TMEM.
+// The MMA warp issues P.V_j before S_{j+1} (tcgen05.mma of one thread run
+// in issue order, so S_{j+1} overwrites P_j only after P.V_j has read it),
+// and the commit that signals S_{j+1} also covers P.V_j: the softmax warps
+// wait on one barrier per block, and O is final in TMEM whenever a score
+// block is ready.  Without the P tile a CTA needs ~49 KB of shared memory,
+// so four CTAs share an SM.
 constexpr float kAttnRescaleLog2 = 8.0f;
 
-template <int KB_, int ST_>
+template <int KB_, int ST_, bool PT_ = false>
 struct Attn2Cfg {
   static constexpr int KB = KB_;
   static constexpr int KV_STAGES = ST_;
+  static constexpr bool PT = PT_;
   static constexpr int TILE = kAttnBlock * 128;          // Q tile / one P atom (64 keys)
   static constexpr int KV_TILE = KB * 128;
-  static constexpr int P_ATOMS = KB / 64;
+  static constexpr int P_ATOMS = PT ? 0 : KB / 64;
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = TILE;
   static constexpr int P_OFF = KV_OFF + KV_STAGES * 2 * KV_TILE;
@@ -530,9 +541,10 @@ struct Attn2Cfg {
   static constexpr int BYTES = BAR_OFF + 256;
   static constexpr uint32_t O_COL = KB;                 // S in [0, KB), O in [KB, KB + 64)
   static constexpr uint32_t TMEM_COLS = KB + 64 <= 128 ? 128 : 256;
-  static constexpr int MIN_BLOCKS = KB == 64 ? 3 : 2;
+  static constexpr int MIN_BLOCKS = PT ? 4 : (KB == 64 ? 3 : 2);
   static constexpr int CHUNKS = KB / 32;
   static_assert(KB == 64 || KB == 128, "key block");
+  static_assert(!PT || KB == 64, "P in TMEM: 64-key blocks");
   static_assert((1 + 2 * KV_STAGES + 5) * 8 + 8 <= 256, "barrier area");
 };
 
@@ -656,19 +668,34 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
                                          Cfg::KV_TILE);
 #pragma unroll
         for (int ks = 0; ks < KB / 16; ++ks) {
-          const uint64_t ad =
-              make_sw128_desc(p_addr + (ks >> 2) * Cfg::TILE + (ks & 3) * 32, 16, 1024);
           const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, 8192, 1024);
-          umma_f16(tmem_base + Cfg::O_COL, ad, bd, idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
+          if constexpr (Cfg::PT) {
+            umma_f16_tmem_a(tmem_base + Cfg::O_COL, tmem_base + ks * 8, bd, idesc_o,
+                            (jj > 0 || ks > 0) ? 1u : 0u);
+          } else {
+            const uint64_t ad =
+                make_sw128_desc(p_addr + (ks >> 2) * Cfg::TILE + (ks & 3) * 32, 16, 1024);
+            umma_f16(tmem_base + Cfg::O_COL, ad, bd, idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
+          }
         }
-        umma_commit(&o_full);
+        if (!Cfg::PT || jj == nblk - 1) umma_commit(&o_full);
         umma_commit(&kv_empty[pv_stage]);
         if (++pv_stage == ST) pv_stage = 0;
         return true;
       };
       for (int j = 0; j < nblk && ok; ++j) {
-        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp) ||
-            !mbar_wait(&s_free, (static_cast<uint32_t>(j) & 1u) ^ 1u, p.err, kDevTimeoutMma, abortp)) {
+        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp)) {
+          ok = false;
+          break;
+        }
+        if constexpr (Cfg::PT) {
+          // P.V_{j-1} first: S_j overwrites the P_{j-1} it reads.
+          if (j >= 1 && !issue_pv(j - 1)) {
+            ok = false;
+            break;
+          }
+        } else if (!mbar_wait(&s_free, (static_cast<uint32_t>(j) & 1u) ^ 1u, p.err, kDevTimeoutMma,
+                              abortp)) {
           ok = false;
           break;
         }
@@ -686,7 +713,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
           stage = 0;
           phase ^= 1u;
         }
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        if (!Cfg::PT && j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
       if (!ok && issued_any) {
@@ -737,8 +764,10 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
       // P.V of the previous block must be done: it reads the P tile this block
       // overwrites, and its sum is in the O rows a rescale touches.
+      // (With P in TMEM the score barrier already covers P.V of the previous block.)
       if (j >= 1) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
+        if (!Cfg::PT &&
+            !__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
                                                kDevTimeoutEpilogue, abortp))) {
           ok = false;
           break;
@@ -789,29 +818,41 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
             sp[t & 3] += pv[t];
           }
         }
-        uint8_t* rowp = pbase + (ch >> 1) * Cfg::TILE + row * 128;
+        if constexpr (Cfg::PT) {
+          // Keys ch*32 + 2c, +2c+1 go to column ch*16 + c (low half first),
+          // over score columns this thread has already read.
+          uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = (ch & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(pack_16bit(pv[8 * q], pv[8 * q + 1], BF16),
-                         pack_16bit(pv[8 * q + 2], pv[8 * q + 3], BF16),
-                         pack_16bit(pv[8 * q + 4], pv[8 * q + 5], BF16),
-                         pack_16bit(pv[8 * q + 6], pv[8 * q + 7], BF16));
+          for (int t = 0; t < 16; ++t) pk[t] = pack_16bit(pv[2 * t], pv[2 * t + 1], BF16);
+          tmem_st16(s_addr + ch * 16, pk);
+        } else {
+          uint8_t* rowp = pbase + (ch >> 1) * Cfg::TILE + row * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = (ch & 1) * 4 + q;
+            *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
+                make_uint4(pack_16bit(pv[8 * q], pv[8 * q + 1], BF16),
+                           pack_16bit(pv[8 * q + 2], pv[8 * q + 3], BF16),
+                           pack_16bit(pv[8 * q + 4], pv[8 * q + 5], BF16),
+                           pack_16bit(pv[8 * q + 6], pv[8 * q + 7], BF16));
+          }
         }
       }
       l_run += (sp[0] + sp[1]) + (sp[2] + sp[3]);
+      if constexpr (Cfg::PT) tmem_st_wait();
       tc_fence_before();
-      fence_proxy_async_smem();
+      if constexpr (!Cfg::PT) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&s_free);
+        if constexpr (!Cfg::PT) mbar_arrive(&s_free);
         mbar_arrive(&p_full);
       }
     }
+    // With P in TMEM only the last P.V signals o_full (phase 0).
     if (ok && nblk > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(nblk - 1) & 1u, p.err,
-                                             kDevTimeoutEpilogue, abortp));
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&o_full, Cfg::PT ? 0u : static_cast<uint32_t>(nblk - 1) & 1u,
+                                p.err, kDevTimeoutEpilogue, abortp));
     const int qrow = qb * kAttnBlock + row;
     if (ok) {
       tc_fence_after();

@@ -967,9 +967,11 @@ using AttnCfgV1 = AttnCfg<128, 1, 1, 2, 2>;
 using AttnCfgV2 = AttnCfg<128, 2, 2, 2, 4>;
 using AttnCfgV3 = AttnCfg<96, 2, 1, 1, 2>;
 // attention_fwd2_kernel (O in TMEM, lazily rescaled integer bases): variant 4 =
-// 64-key blocks, three CTAs per SM; 5 = 128-key blocks, two CTAs per SM.
+// 64-key blocks, three CTAs per SM; 5 = 128-key blocks, two CTAs per SM;
+// 6 = 64-key blocks with P in TMEM, four CTAs per SM.
 using Attn2CfgV4 = Attn2Cfg<64, 2>;
 using Attn2CfgV5 = Attn2Cfg<128, 2>;
+using Attn2CfgV6 = Attn2Cfg<64, 2, true>;
 
 template <bool BF16, class Cfg, int EMU>
 static int32_t launch_attention2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
@@ -1030,6 +1032,7 @@ static int32_t launch_attention_variant(int variant, int emu, const dim3& grid,
   switch (variant) {
     case 4: return launch_attention2_emu<BF16, Attn2CfgV4>(emu, grid, mq, mk, mv, a, s, device);
     case 5: return launch_attention2_emu<BF16, Attn2CfgV5>(emu, grid, mq, mk, mv, a, s, device);
+    case 6: return launch_attention2_emu<BF16, Attn2CfgV6>(emu, grid, mq, mk, mv, a, s, device);
     case 2: return launch_attention<BF16, AttnCfgV2, 0>(grid, mq, mk, mv, a, s, device);
     case 3: return launch_attention_emu<BF16, AttnCfgV3>(emu, grid, mq, mk, mv, a, s, device);
     default: return launch_attention_emu<BF16, AttnCfgV1>(emu, grid, mq, mk, mv, a, s, device);
@@ -1042,6 +1045,7 @@ static int attn_key_block(int variant) {
     case 3: return AttnCfgV3::KB;
     case 4: return Attn2CfgV4::KB;
     case 5: return Attn2CfgV5::KB;
+    case 6: return Attn2CfgV6::KB;
     default: return AttnCfgV1::KB;
   }
 }
@@ -1114,9 +1118,9 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
   if (st != SF_OK) return st;
   if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
   const CUtensorMapDataType dt = tma_dtype(dtype);
-  const int variant = env_int("SF_ATTN_VARIANT", 4);  // tuning knob: see AttnCfgV1..V3, Attn2CfgV4..V5
-  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && variant != 4 && variant != 5)
-    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variant 4 or 5)");
+  const int variant = env_int("SF_ATTN_VARIANT", 6);  // tuning knob: see AttnCfgV1..V3, Attn2CfgV4..V6
+  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && (variant < 4 || variant > 6))
+    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variant 4, 5 or 6)");
   const uint32_t kb = static_cast<uint32_t>(attn_key_block(variant));
   CUtensorMap mq, mk, mv;
   MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),

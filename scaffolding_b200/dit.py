@@ -218,7 +218,7 @@ class DitStack:
         # the gathered keys (minus the local slice) merges it.
         self.overlap = (self.fused and plan.kv_exchange
                         and os.environ.get("SF_KV_OVERLAP", "1") != "0"
-                        and os.environ.get("SF_ATTN_VARIANT", "4") in ("4", "5"))
+                        and os.environ.get("SF_ATTN_VARIANT", "6") in ("4", "5", "6"))
         self.part_o = self.part_ml = None
         self.comm_stream = self.ev_kv = self.ev_gather = None
         if self.overlap:

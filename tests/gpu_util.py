@@ -57,12 +57,12 @@ def fp32_mode(mode):
     check(lib.sf_set_fp32_mode(mode), "sf_set_fp32_mode")
 
 
-def attn_oracle_opts():
-    """oracle.flash_attention settings that restate the active fused-attention
-    kernel: its key block and whether its row bases are integers (variant 4,
-    the default, and 5: O in TMEM with lazily raised integer bases; 1-3: real
-    bases).  SF_ATTN_VARIANT selects the kernel, as in the engine."""
+def attn_oracle_opts(variant=None):
+    """oracle.flash_attention settings that restate a fused-attention kernel:
+    its key block and whether its row bases are integers (variants 4, 5 and
+    6, the default: O in TMEM with lazily raised integer bases; 1-3: real
+    bases).  SF_ATTN_VARIANT selects the active kernel, as in the engine."""
     import os
-    v = int(os.environ.get("SF_ATTN_VARIANT", "4") or 4)
-    block = {1: 128, 2: 128, 3: 96, 4: 64, 5: 128}.get(v, 64)
+    v = int(variant or os.environ.get("SF_ATTN_VARIANT", "6") or 6)
+    block = {1: 128, 2: 128, 3: 96, 4: 64, 5: 128, 6: 64}.get(v, 64)
     return {"block": block, "integer_base": v >= 4}

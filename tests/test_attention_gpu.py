@@ -151,6 +151,32 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
     assert device_error(0) == 0
 
 
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6])
+def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant):
+    """Each fused-attention configuration (SF_ATTN_VARIANT) on a ragged case
+    with q_len != kv_len and large logits, against the oracle restating that
+    configuration's key block and row bases."""
+    from tests.gpu_util import device_error
+    monkeypatch.setenv("SF_ATTN_VARIANT", str(variant))
+    rng = np.random.default_rng(40 + variant)
+    B, H, Lq, Lk = 1, 2, 300, 641
+    q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
+    k32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32) * np.float32(3)
+    v32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32)
+    gq, q = to_device(ops, q32, "bf16")
+    gk, k = to_device(ops, k32, "bf16")
+    gv, v = to_device(ops, v32, "bf16")
+    out = _fused(ops, B, H, Lq, Lk, gq, gk, gv, H * 64, H * 64, H * 64, Lq * H * 64, Lk * H * 64,
+                 Lk * H * 64, 0.125)
+    for h in range(H):
+        sl = slice(h * 64, (h + 1) * 64)
+        p = O.softmax_rows((q[0][:, sl] @ k[0][:, sl].T * np.float32(0.125)).astype(np.float32))
+        ref, allow = O.flash_attention(q[0][:, sl], k[0][:, sl], v[0][:, sl], 0.125,
+                                       return_allowance=True, **attn_oracle_opts(variant))
+        _check_attn(out[:, sl], ref, O.abs_product(p, v[0][:, sl].T), allow, f"v{variant} h{h}")
+    assert device_error(0) == 0
+
+
 def test_fused_attention_rejects_bad_arguments(gpu, ops):
     from scaffolding_b200._lib import SF_ERR_INVALID_ARGUMENT, SF_ERR_UNSUPPORTED, lib
     import ctypes as C
