@@ -208,6 +208,15 @@ int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len, in
                                  float scale, int32_t dtype, int32_t skip_lo, int32_t skip_hi,
                                  float* part_o, float* part_ml, int32_t part_mode, void* stream);
 
+/* Kernel launches one sf_attention_fwd (part_mode 0) or
+ * sf_attention_fwd_partial call of these sizes makes on the current device:
+ * 1, or 2 when the last wave of query blocks is split into key-range pieces
+ * and merged by a second kernel; 0 for empty sizes.  Lets callers count
+ * their launches (no reference counterpart: the reference's attention chain,
+ * nn/functional.py:310-321, launches a fixed sequence). */
+int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                                  int32_t part_mode, int32_t* count);
+
 /* y[i] = act(alpha * x[i]).  Replaces cuda_silu_f32 / cuda_gelu_f32 /
  * cuda_muls_f32 (_cuda_ops_decl.h:69, :74, :63; _cuda_kernels.cu:384, :428,
  * :237-277) for the standalone dev_silu / dev_gelu / dev_muls calls. */

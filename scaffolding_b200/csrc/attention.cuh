@@ -47,6 +47,9 @@ struct AttnArgs {
   int64_t ldo, o_bstride;  // elements
   int* err;
   int sleep_ns;          // poll back-off of the softmax warps' waits (0 = spin)
+  // attention_fwd2_kernel: suspend-time hints (ns) of the producer / MMA
+  // waits and of the softmax waits (0 = poll without suspending).
+  uint32_t suspend_mma, suspend_smx;
   // attention_fwd2_kernel only: keys [skip_lo, skip_hi) are left out (none
   // when skip_lo == skip_hi == kv_len), and part_mode selects the output:
   //   0  normalised 16-bit O;
@@ -59,6 +62,20 @@ struct AttnArgs {
   int part_mode;
   float* part_o;
   float* part_ml;
+  // Split dispatch (attention_fwd2_kernel; part_mode 0 or 2), so that the
+  // last wave of CTAs is not mostly empty: a 1-D grid whose blocks
+  // [0, split_first) are whole units u (query block u % nqb, head
+  // (u / nqb) % heads, batch u / (nqb * heads)); block split_first + j is
+  // piece j % split_k of unit split_first + j / split_k, a contiguous share
+  // of the key blocks, and writes its unnormalised fp32 O rows and (m, l)
+  // to slot j of ws_o [slot][128][64] / ws_ml [slot][128][2] (zeros and
+  // m = -inf when all its keys are skipped); attention_merge_kernel then
+  // combines the pieces of each split unit (and part_o / part_ml in mode 2).
+  int split_first;  // -1: 3-D grid (query block, head, batch), no pieces
+  int split_k;
+  int nqb;
+  float* ws_o;
+  float* ws_ml;
 };
 
 constexpr int kAttnBlock = 128;   // queries per CTA and keys per block
@@ -524,6 +541,13 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
 // wait on one barrier per block, and O is final in TMEM whenever a score
 // block is ready.  Without the P tile a CTA needs ~49 KB of shared memory,
 // so four CTAs share an SM.
+//
+// PT with 32-key blocks: two score buffers (S_j in buffer j % 2) and O fit
+// the same 128 columns.  S_{j+1} is computed while block j's softmax runs;
+// the MMA warp issues P.V_{j-1} before S_{j+1} (which overwrites P_{j-1}).
+// The softmax of block j reads its 32 scores once, and when its row base
+// rises it waits for P.V_{j-1} (o_full, one phase per P.V) before scaling
+// O; the final wait is on o_last, signalled by the last P.V only.
 constexpr float kAttnRescaleLog2 = 8.0f;
 
 template <int KB_, int ST_, bool PT_ = false>
@@ -531,6 +555,7 @@ struct Attn2Cfg {
   static constexpr int KB = KB_;
   static constexpr int KV_STAGES = ST_;
   static constexpr bool PT = PT_;
+  static constexpr int NS = KB == 32 ? 2 : 1;            // score buffers
   static constexpr int TILE = kAttnBlock * 128;          // Q tile / one P atom (64 keys)
   static constexpr int KV_TILE = KB * 128;
   static constexpr int P_ATOMS = PT ? 0 : KB / 64;
@@ -539,13 +564,14 @@ struct Attn2Cfg {
   static constexpr int P_OFF = KV_OFF + KV_STAGES * 2 * KV_TILE;
   static constexpr int BAR_OFF = P_OFF + P_ATOMS * TILE;
   static constexpr int BYTES = BAR_OFF + 256;
-  static constexpr uint32_t O_COL = KB;                 // S in [0, KB), O in [KB, KB + 64)
-  static constexpr uint32_t TMEM_COLS = KB + 64 <= 128 ? 128 : 256;
+  static constexpr uint32_t O_COL = NS * KB;            // S in [0, NS * KB), O in the next 64
+  static constexpr uint32_t TMEM_COLS = NS * KB + 64 <= 128 ? 128 : 256;
   static constexpr int MIN_BLOCKS = PT ? 4 : (KB == 64 ? 3 : 2);
   static constexpr int CHUNKS = KB / 32;
-  static_assert(KB == 64 || KB == 128, "key block");
-  static_assert(!PT || KB == 64, "P in TMEM: 64-key blocks");
-  static_assert((1 + 2 * KV_STAGES + 5) * 8 + 8 <= 256, "barrier area");
+  static_assert(KB == 32 || KB == 64 || KB == 128, "key block");
+  static_assert(PT ? KB <= 64 : KB >= 64, "P in TMEM: 32- or 64-key blocks; P in smem: 64 or 128");
+  static_assert((1 + 2 * KV_STAGES + 2 * NS + 4) * 8 + 8 <= 192, "barrier area");
+  static constexpr int DESC_OFF = BAR_OFF + 192;        // the CTA's work description (10 ints)
 };
 
 // EMU of every four exp2 pairs of a full block go through exp2_poly2.
@@ -560,26 +586,66 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
   uint64_t& q_full = bars[0];
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ST;
-  uint64_t& s_full = kv_empty[ST];
-  uint64_t& s_free = kv_empty[ST + 1];
-  uint64_t& p_full = kv_empty[ST + 2];
-  uint64_t& o_full = kv_empty[ST + 3];
-  uint64_t& drain_bar = kv_empty[ST + 4];
-  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&kv_empty[ST + 5]);
-  int& abort_flag = *(reinterpret_cast<int*>(&kv_empty[ST + 5]) + 1);
+  constexpr int NS = Cfg::NS;
+  // One score-ready and one P-ready barrier per score buffer, so that each
+  // wait is on a phase that is at most one behind (block j + NS, the next
+  // user of a buffer, cannot start before P.V_j has been issued).
+  uint64_t* s_full = kv_empty + ST;
+  uint64_t* p_full = s_full + NS;
+  uint64_t& s_free = p_full[NS];
+  uint64_t& o_full = p_full[NS + 1];
+  uint64_t& o_last = p_full[NS + 2];
+  uint64_t& drain_bar = p_full[NS + 3];
+  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&p_full[NS + 4]);
+  int& abort_flag = *(reinterpret_cast<int*>(&p_full[NS + 4]) + 1);
   if ((smem_u32(smem) & 1023u) != 0) {
     if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadConfig);
     return;
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  // Key blocks over [0, skip_lo) then [skip_hi, kv_len).
-  const int nb0 = (p.skip_lo + KB - 1) / KB;
-  const int nblk = nb0 + (p.kv_len - p.skip_hi + KB - 1) / KB;
-  auto block_start = [&](int j) { return j < nb0 ? j * KB : p.skip_hi + (j - nb0) * KB; };
+  // Work description, computed by thread 0 into shared memory (read where
+  // used rather than held in registers): query block, head, batch, workspace
+  // slot (-1: none) and the key blocks over [k0, e0) then [s1, k1), where
+  // [k0, k1) is the CTA's key range and [e0, s1) the skipped keys in it.
+  int* desc = reinterpret_cast<int*>(smem + Cfg::DESC_OFF);
+  enum { kQb, kH, kB, kSlot, kK0, kK1, kE0, kS1, kNb0, kNblk };
+  if (threadIdx.x == 0) {
+    int u = static_cast<int>(blockIdx.x), k0 = 0, k1 = p.kv_len, slot = -1;
+    if (p.split_first < 0) {
+      desc[kQb] = blockIdx.x;
+      desc[kH] = blockIdx.y;
+      desc[kB] = blockIdx.z;
+    } else {
+      if (u >= p.split_first) {
+        const int j = u - p.split_first;
+        const int piece = j % p.split_k;
+        const int nkb = (p.kv_len + KB - 1) / KB;
+        u = p.split_first + j / p.split_k;
+        k0 = (piece * nkb / p.split_k) * KB;
+        k1 = min(p.kv_len, ((piece + 1) * nkb / p.split_k) * KB);
+        slot = j;
+      }
+      desc[kQb] = u % p.nqb;
+      desc[kH] = (u / p.nqb) % p.heads;
+      desc[kB] = u / (p.nqb * p.heads);
+    }
+    const int e0 = min(k1, p.skip_lo), s1 = max(k0, p.skip_hi);
+    const int nb0 = e0 > k0 ? (e0 - k0 + KB - 1) / KB : 0;
+    desc[kSlot] = slot;
+    desc[kK0] = k0;
+    desc[kK1] = k1;
+    desc[kE0] = e0;
+    desc[kS1] = s1;
+    desc[kNb0] = nb0;
+    desc[kNblk] = nb0 + (k1 > s1 ? (k1 - s1 + KB - 1) / KB : 0);
+  }
+  auto block_start = [&](int j) {
+    const int nb0 = desc[kNb0];
+    return j < nb0 ? desc[kK0] + j * KB : desc[kS1] + (j - nb0) * KB;
+  };
   auto block_valid = [&](int j) {
-    return j < nb0 ? min(KB, p.skip_lo - j * KB) : min(KB, p.kv_len - block_start(j));
+    return min(KB, (j < desc[kNb0] ? desc[kE0] : desc[kK1]) - block_start(j));
   };
 
   if (threadIdx.x == 0) {
@@ -588,10 +654,13 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(&s_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
     mbar_init(&s_free, 4);
-    mbar_init(&p_full, 4);
     mbar_init(&o_full, 1);
+    mbar_init(&o_last, 1);
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
     fence_mbar_init();
@@ -610,6 +679,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
   volatile int* abortp = &abort_flag;
+  const int nblk = desc[kNblk];
 
   if (warp == 0) {
     // ───────────── TMA producer ─────────────
@@ -617,10 +687,12 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       bool ok = true;
       int issued = 0, stage = 0;
       uint32_t phase = 0;
+      const int h = desc[kH], b = desc[kB];
       mbar_arrive_expect_tx(&q_full, Cfg::TILE);
-      tma_load_4d(smem + Cfg::Q_OFF, &tmQ, &q_full, 0, qb * kAttnBlock, h, b);
+      tma_load_4d(smem + Cfg::Q_OFF, &tmQ, &q_full, 0, desc[kQb] * kAttnBlock, h, b);
       for (int j = 0; j < nblk; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp,
+                       kWaitLimitNs, 0, p.suspend_mma)) {
           ok = false;
           break;
         }
@@ -656,12 +728,13 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);
       const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF);
       const uint32_t p_addr = smem_u32(smem + Cfg::P_OFF);
-      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
+      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp, kWaitLimitNs, 0, p.suspend_mma);
       bool issued_any = false;
       int stage = 0, pv_stage = 0;
       uint32_t phase = 0;
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(&p_full, static_cast<uint32_t>(jj) & 1u, p.err, kDevTimeoutMma, abortp))
+        if (!mbar_wait(&p_full[jj % NS], static_cast<uint32_t>(jj / NS) & 1u, p.err, kDevTimeoutMma,
+                       abortp, kWaitLimitNs, 0, p.suspend_mma))
           return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + pv_stage * 2 * Cfg::KV_TILE +
@@ -670,32 +743,34 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         for (int ks = 0; ks < KB / 16; ++ks) {
           const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, 8192, 1024);
           if constexpr (Cfg::PT) {
-            umma_f16_tmem_a(tmem_base + Cfg::O_COL, tmem_base + ks * 8, bd, idesc_o,
-                            (jj > 0 || ks > 0) ? 1u : 0u);
+            umma_f16_tmem_a(tmem_base + Cfg::O_COL, tmem_base + (jj % NS) * KB + ks * 8, bd,
+                            idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
           } else {
             const uint64_t ad =
                 make_sw128_desc(p_addr + (ks >> 2) * Cfg::TILE + (ks & 3) * 32, 16, 1024);
             umma_f16(tmem_base + Cfg::O_COL, ad, bd, idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
           }
         }
-        if (!Cfg::PT || jj == nblk - 1) umma_commit(&o_full);
+        if (!Cfg::PT || NS == 2) umma_commit(&o_full);
+        if (Cfg::PT && jj == nblk - 1) umma_commit(&o_last);
         umma_commit(&kv_empty[pv_stage]);
         if (++pv_stage == ST) pv_stage = 0;
         return true;
       };
       for (int j = 0; j < nblk && ok; ++j) {
-        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp)) {
+        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp, kWaitLimitNs, 0,
+                       p.suspend_mma)) {
           ok = false;
           break;
         }
         if constexpr (Cfg::PT) {
-          // P.V_{j-1} first: S_j overwrites the P_{j-1} it reads.
-          if (j >= 1 && !issue_pv(j - 1)) {
+          // P.V_{j-NS} first: S_j overwrites the P_{j-NS} it reads.
+          if (j >= NS && !issue_pv(j - NS)) {
             ok = false;
             break;
           }
         } else if (!mbar_wait(&s_free, (static_cast<uint32_t>(j) & 1u) ^ 1u, p.err, kDevTimeoutMma,
-                              abortp)) {
+                              abortp, kWaitLimitNs, 0, p.suspend_mma)) {
           ok = false;
           break;
         }
@@ -705,17 +780,22 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
           const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
-          umma_f16(tmem_base, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+          umma_f16(tmem_base + (j % NS) * KB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
         }
         issued_any = true;
-        umma_commit(&s_full);
+        umma_commit(&s_full[j % NS]);
         if (++stage == ST) {
           stage = 0;
           phase ^= 1u;
         }
         if (!Cfg::PT && j >= 1 && !issue_pv(j - 1)) ok = false;
       }
-      if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
+      if constexpr (Cfg::PT) {
+        for (int jj = nblk > NS ? nblk - NS : 0; jj < nblk && ok; ++jj)
+          if (!issue_pv(jj)) ok = false;
+      } else if (ok && nblk > 0 && !issue_pv(nblk - 1)) {
+        ok = false;
+      }
       if (!ok && issued_any) {
         umma_commit(&drain_bar);
         if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
@@ -732,21 +812,33 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
     const float c = p.scale_log2;
     bool ok = true;
     uint32_t r[32];
+    // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
+    auto rescale_o = [&](float alpha) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(o_addr + half * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
+        tmem_st32(o_addr + half * 32, r);
+      }
+    };
     for (int j = 0; j < nblk; ++j) {
       // Waits end the loop for the whole warp together: the TMEM loads and
       // stores that follow are warp-collective.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full, static_cast<uint32_t>(j) & 1u, p.err,
-                                             kDevTimeoutEpilogue, abortp))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j % NS], static_cast<uint32_t>(j / NS) & 1u,
+                                             p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const uint32_t sb_addr = s_addr + (j % NS) * KB;
       const int valid = block_valid(j);
       const bool full = valid == KB;
       float mxc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        tmem_ld32(s_addr + ch * 32, r);
+        tmem_ld32(sb_addr + ch * 32, r);
         tmem_ld_wait();
         if (full) {
 #pragma unroll
@@ -762,27 +854,21 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       const float cand = ceilf(mx * c);
       const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
       const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-      // P.V of the previous block must be done: it reads the P tile this block
-      // overwrites, and its sum is in the O rows a rescale touches.
-      // (With P in TMEM the score barrier already covers P.V of the previous block.)
-      if (j >= 1) {
-        if (!Cfg::PT &&
-            !__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
-                                               kDevTimeoutEpilogue, abortp))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tmem_ld32(o_addr + half * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-            tmem_st32(o_addr + half * 32, r);
+      const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
+      if constexpr (!Cfg::PT) {
+        // P.V of the previous block must be done: it reads the P tile this
+        // block overwrites, and its sum is in the O rows a rescale touches.
+        if (j >= 1) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
+                                                 kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
+            ok = false;
+            break;
           }
-          tmem_st_wait();
+          tc_fence_after();
+          if (rescale) {
+            rescale_o(alpha);
+            tmem_st_wait();
+          }
         }
       }
       if (need) {
@@ -794,8 +880,10 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       const float nm = -m_run;
 #pragma unroll
       for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        tmem_ld32(s_addr + ch * 32, r);
-        tmem_ld_wait();
+        if (Cfg::CHUNKS > 1) {  // one chunk: the scores are still in r
+          tmem_ld32(sb_addr + ch * 32, r);
+          tmem_ld_wait();
+        }
         float* pv = reinterpret_cast<float*>(r);
         if (full) {
 #pragma unroll
@@ -824,7 +912,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
           uint32_t pk[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) pk[t] = pack_16bit(pv[2 * t], pv[2 * t + 1], BF16);
-          tmem_st16(s_addr + ch * 16, pk);
+          tmem_st16(sb_addr + ch * 16, pk);
         } else {
           uint8_t* rowp = pbase + (ch >> 1) * Cfg::TILE + row * 128;
 #pragma unroll
@@ -839,38 +927,61 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         }
       }
       l_run += (sp[0] + sp[1]) + (sp[2] + sp[3]);
-      if constexpr (Cfg::PT) tmem_st_wait();
+      if constexpr (Cfg::PT) {
+        // O is scaled after P is stored (r is free again) and before P.V_j is
+        // issued.  One score buffer: S_j's barrier already covers P.V_{j-1}.
+        // Two: wait for P.V_{j-1} on o_full (at most one phase behind).
+        if (rescale) {
+          if (NS == 2 &&
+              !__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
+                                                 kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          rescale_o(alpha);
+        }
+        tmem_st_wait();
+      }
       tc_fence_before();
       if constexpr (!Cfg::PT) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         if constexpr (!Cfg::PT) mbar_arrive(&s_free);
-        mbar_arrive(&p_full);
+        mbar_arrive(&p_full[j % NS]);
       }
     }
-    // With P in TMEM only the last P.V signals o_full (phase 0).
+    // With P in TMEM the last P.V alone signals o_last.
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu,
-                      mbar_wait(&o_full, Cfg::PT ? 0u : static_cast<uint32_t>(nblk - 1) & 1u,
-                                p.err, kDevTimeoutEpilogue, abortp));
-    const int qrow = qb * kAttnBlock + row;
+                      Cfg::PT ? mbar_wait(&o_last, 0u, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx)
+                              : mbar_wait(&o_full, static_cast<uint32_t>(nblk - 1) & 1u, p.err,
+                                          kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx));
+    const int qrow = desc[kQb] * kAttnBlock + row;
     if (ok) {
       tc_fence_after();
+      const int h = desc[kH], b = desc[kB], slot = desc[kSlot];
       const bool live = qrow < p.q_len;
       const int64_t prow = (static_cast<int64_t>(b) * p.q_len + qrow) * p.heads + h;
+      // A split piece writes its partial result to its workspace slot.
+      const int mode = slot >= 0 ? 1 : p.part_mode;
+      float* const pml = slot >= 0 ? p.ws_ml + (static_cast<int64_t>(slot) * kAttnBlock + row) * 2
+                                   : p.part_ml + 2 * prow;
+      float* const pob = slot >= 0 ? p.ws_o + (static_cast<int64_t>(slot) * kAttnBlock + row) * kAttnD
+                                   : p.part_o + prow * kAttnD;
       // Merge with a partial result over other keys: both bases are integers,
       // so the rescale factors are exact powers of two.
       float a_own = 1.0f, a_part = 0.0f;
-      if (p.part_mode == 2 && live) {
-        const float m_p = p.part_ml[2 * prow], l_p = p.part_ml[2 * prow + 1];
+      if (mode == 2 && live) {
+        const float m_p = pml[0], l_p = pml[1];
         const float m = fmaxf(m_run, m_p);
         a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
         a_part = ex2_approx(m_p - m);
         l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
       }
-      if (p.part_mode == 1 && live) {
-        p.part_ml[2 * prow] = m_run;
-        p.part_ml[2 * prow + 1] = l_run;
+      if (mode == 1 && live) {
+        pml[0] = m_run;
+        pml[1] = l_run;
       }
       const float inv = 1.0f / l_run;
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
@@ -881,19 +992,20 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         tmem_ld32(o_addr + half * 32, r);
         tmem_ld_wait();
         if (!live) continue;
-        if (p.part_mode == 1) {
-          float4* po = reinterpret_cast<float4*>(p.part_o + prow * kAttnD + half * 32);
+        if (mode == 1) {
+          float4* po = reinterpret_cast<float4*>(pob + half * 32);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            po[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+            po[q] = nblk > 0 ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           continue;
         }
         float ov[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) ov[t] = nblk > 0 ? __uint_as_float(r[t]) : 0.0f;
-        if (p.part_mode == 2) {
-          const float4* po = reinterpret_cast<const float4*>(p.part_o + prow * kAttnD + half * 32);
+        if (mode == 2) {
+          const float4* po = reinterpret_cast<const float4*>(pob + half * 32);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float4 v = po[q];
@@ -921,6 +1033,62 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+}
+
+// Combines the split_k pieces of each split unit, and in part_mode 2 the
+// partial result in part_o / part_ml (one CTA per unit, one thread per query
+// row): with integer bases m_p, m = max m_p,
+// O = sum 2^(m_p - m) O_p / sum 2^(m_p - m) l_p, written as 16-bit O.
+template <bool BF16>
+__global__ void __launch_bounds__(kAttnBlock) attention_merge_kernel(const AttnArgs p) {
+  const int u = p.split_first + static_cast<int>(blockIdx.x);
+  const int qb = u % p.nqb, h = (u / p.nqb) % p.heads, b = u / (p.nqb * p.heads);
+  const int row = threadIdx.x;
+  const int qrow = qb * kAttnBlock + row;
+  if (qrow >= p.q_len) return;
+  const int64_t slot0 = static_cast<int64_t>(blockIdx.x) * p.split_k;
+  const int64_t prow = (static_cast<int64_t>(b) * p.q_len + qrow) * p.heads + h;
+  const int n_in = p.split_k + (p.part_mode == 2 ? 1 : 0);
+  // input i < split_k: workspace slot slot0 + i; i == split_k: the partial result
+  auto ml_of = [&](int i) -> const float* {
+    return i < p.split_k ? p.ws_ml + ((slot0 + i) * kAttnBlock + row) * 2 : p.part_ml + 2 * prow;
+  };
+  auto o_of = [&](int i) -> const float* {
+    return i < p.split_k ? p.ws_o + ((slot0 + i) * kAttnBlock + row) * kAttnD
+                         : p.part_o + prow * kAttnD;
+  };
+  float m = -INFINITY;
+  for (int i = 0; i < n_in; ++i) m = fmaxf(m, ml_of(i)[0]);
+  float l = 0.0f;
+  float acc[kAttnD];
+#pragma unroll
+  for (int t = 0; t < kAttnD; ++t) acc[t] = 0.0f;
+  for (int i = 0; i < n_in; ++i) {
+    const float* ml = ml_of(i);
+    if (ml[0] == -INFINITY) continue;  // every key of this piece skipped
+    const float a = ex2_approx(ml[0] - m);
+    l += ml[1] * a;
+    const float4* po = reinterpret_cast<const float4*>(o_of(i));
+#pragma unroll
+    for (int q = 0; q < kAttnD / 4; ++q) {
+      const float4 v = po[q];
+      acc[4 * q] += v.x * a;
+      acc[4 * q + 1] += v.y * a;
+      acc[4 * q + 2] += v.z * a;
+      acc[4 * q + 3] += v.w * a;
+    }
+  }
+  const float inv = 1.0f / l;
+  uint4* dst = reinterpret_cast<uint4*>(
+      reinterpret_cast<uint8_t*>(p.o) +
+      (static_cast<int64_t>(b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
+       static_cast<int64_t>(h) * kAttnD) * 2);
+#pragma unroll
+  for (int q = 0; q < kAttnD / 8; ++q)
+    dst[q] = make_uint4(pack_16bit(acc[8 * q] * inv, acc[8 * q + 1] * inv, BF16),
+                        pack_16bit(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv, BF16),
+                        pack_16bit(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv, BF16),
+                        pack_16bit(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv, BF16));
 }
 
 }  // namespace sf

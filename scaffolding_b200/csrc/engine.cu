@@ -968,10 +968,12 @@ using AttnCfgV2 = AttnCfg<128, 2, 2, 2, 4>;
 using AttnCfgV3 = AttnCfg<96, 2, 1, 1, 2>;
 // attention_fwd2_kernel (O in TMEM, lazily rescaled integer bases): variant 4 =
 // 64-key blocks, three CTAs per SM; 5 = 128-key blocks, two CTAs per SM;
-// 6 = 64-key blocks with P in TMEM, four CTAs per SM.
+// 6 = 64-key blocks with P in TMEM, four CTAs per SM; 7 = 32-key blocks with
+// P in TMEM and two score buffers, four CTAs per SM.
 using Attn2CfgV4 = Attn2Cfg<64, 2>;
 using Attn2CfgV5 = Attn2Cfg<128, 2>;
 using Attn2CfgV6 = Attn2Cfg<64, 2, true>;
+using Attn2CfgV7 = Attn2Cfg<32, 4, true>;
 
 template <bool BF16, class Cfg, int EMU>
 static int32_t launch_attention2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
@@ -1033,6 +1035,7 @@ static int32_t launch_attention_variant(int variant, int emu, const dim3& grid,
     case 4: return launch_attention2_emu<BF16, Attn2CfgV4>(emu, grid, mq, mk, mv, a, s, device);
     case 5: return launch_attention2_emu<BF16, Attn2CfgV5>(emu, grid, mq, mk, mv, a, s, device);
     case 6: return launch_attention2_emu<BF16, Attn2CfgV6>(emu, grid, mq, mk, mv, a, s, device);
+    case 7: return launch_attention2_emu<BF16, Attn2CfgV7>(emu, grid, mq, mk, mv, a, s, device);
     case 2: return launch_attention<BF16, AttnCfgV2, 0>(grid, mq, mk, mv, a, s, device);
     case 3: return launch_attention_emu<BF16, AttnCfgV3>(emu, grid, mq, mk, mv, a, s, device);
     default: return launch_attention_emu<BF16, AttnCfgV1>(emu, grid, mq, mk, mv, a, s, device);
@@ -1046,9 +1049,61 @@ static int attn_key_block(int variant) {
     case 4: return Attn2CfgV4::KB;
     case 5: return Attn2CfgV5::KB;
     case 6: return Attn2CfgV6::KB;
+    case 7: return Attn2CfgV7::KB;
     default: return AttnCfgV1::KB;
   }
 }
+
+static int attn_ctas_per_sm(int variant) {
+  switch (variant) {
+    case 2: return AttnCfgV2::MIN_BLOCKS;
+    case 3: return AttnCfgV3::MIN_BLOCKS;
+    case 4: return Attn2CfgV4::MIN_BLOCKS;
+    case 5: return Attn2CfgV5::MIN_BLOCKS;
+    case 6: return Attn2CfgV6::MIN_BLOCKS;
+    case 7: return Attn2CfgV7::MIN_BLOCKS;
+    default: return AttnCfgV1::MIN_BLOCKS;
+  }
+}
+
+static int attn_variant() { return env_int("SF_ATTN_VARIANT", 6); }  // tuning knob
+
+// Split dispatch plan (see AttnArgs::split_first).  U units on P resident
+// CTA slots take ceil(U / P) unit times; splitting the R = U mod P units of
+// the last wave into k key-range pieces takes floor(U / P) + ceil(R k / P) / k.
+// k in [2, min(32, key blocks)] minimises that; the split is used when it
+// saves more than 3 %.
+struct AttnSplit {
+  int split_first = -1, split_k = 1, pieces = 0;
+};
+static AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
+  AttnSplit sp;
+  if (env_int("SF_ATTN_SPLIT", 1) == 0 || slots <= 0 || nkb < 2) return sp;  // tuning knob
+  const int64_t full = units / slots, rem = units % slots;
+  if (rem == 0) return sp;
+  double best = 1.0;
+  int best_k = 1;
+  for (int k = 2; k <= std::min(32, nkb); ++k) {
+    const double t = static_cast<double>((rem * k + slots - 1) / slots) / k;
+    if (t < best - 1e-9) {
+      best = t;
+      best_k = k;
+    }
+  }
+  if (best_k == 1 || full + best > 0.97 * static_cast<double>(full + 1)) return sp;
+  sp.split_first = static_cast<int>(units - rem);
+  sp.split_k = best_k;
+  sp.pieces = static_cast<int>(rem) * best_k;
+  return sp;
+}
+
+// Per-device workspace of the split pieces (grown on demand, never shrunk).
+struct AttnWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+static std::mutex g_attn_ws_mu;
+static AttnWorkspace g_attn_ws[64];
 
 static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                               int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
@@ -1057,6 +1112,28 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
                               int64_t o_bstride, float scale, int32_t dtype, int32_t skip_lo,
                               int32_t skip_hi, float* part_o, float* part_ml, int32_t part_mode,
                               void* stream);
+
+// Number of kernel launches of sf_attention_fwd (part_mode 0) or
+// sf_attention_fwd_partial for these sizes on the current device (1, or 2
+// when the last wave is split and merged).
+extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len,
+                                             int32_t kv_len, int32_t part_mode, int32_t* count) {
+  if (!count) return fail(SF_ERR_INVALID_ARGUMENT, "null count");
+  *count = 0;
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0) return SF_OK;
+  DeviceInfo* dev = nullptr;
+  int32_t st = current_device_info(&dev, nullptr);
+  if (st != SF_OK) return st;
+  const int variant = attn_variant();
+  *count = 1;
+  if (variant >= 4 && variant <= 7 && part_mode != 1) {
+    const int64_t units = static_cast<int64_t>(ceil_div(q_len, kAttnBlock)) * heads * batch;
+    const AttnSplit sp = attn_split_plan(units, attn_ctas_per_sm(variant) * dev->sm_count,
+                                         ceil_div(kv_len, attn_key_block(variant)));
+    if (sp.split_first >= 0) *count = 2;
+  }
+  return SF_OK;
+}
 
 extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                                     int32_t head_dim, const void* q, int64_t ldq,
@@ -1118,9 +1195,9 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
   if (st != SF_OK) return st;
   if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
   const CUtensorMapDataType dt = tma_dtype(dtype);
-  const int variant = env_int("SF_ATTN_VARIANT", 6);  // tuning knob: see AttnCfgV1..V3, Attn2CfgV4..V6
-  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && (variant < 4 || variant > 6))
-    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variant 4, 5 or 6)");
+  const int variant = attn_variant();  // see AttnCfgV1..V3, Attn2CfgV4..V7
+  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && (variant < 4 || variant > 7))
+    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variants 4-7)");
   const uint32_t kb = static_cast<uint32_t>(attn_key_block(variant));
   CUtensorMap mq, mk, mv;
   MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
@@ -1147,14 +1224,48 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
   a.o_bstride = o_bstride;
   a.err = dev->err_word;
   a.sleep_ns = env_int("SF_ATTN_SLEEP", 0);  // tuning knob
+  // Suspend-time hints of the TMEM-accumulator kernel's waits (tuning knobs).
+  a.suspend_mma = static_cast<uint32_t>(env_int("SF_ATTN_SUSPEND_MMA", 0));
+  a.suspend_smx = static_cast<uint32_t>(env_int("SF_ATTN_SUSPEND_SMX", 0));
   a.skip_lo = skip_lo;
   a.skip_hi = skip_hi;
   a.part_mode = part_mode;
   a.part_o = part_o;
   a.part_ml = part_ml;
-  const dim3 grid(static_cast<unsigned>(ceil_div(q_len, kAttnBlock)), static_cast<unsigned>(heads),
-                  static_cast<unsigned>(batch));
+  a.split_first = -1;
+  a.split_k = 1;
+  a.nqb = ceil_div(q_len, kAttnBlock);
+  a.ws_o = a.ws_ml = nullptr;
+  dim3 grid(static_cast<unsigned>(a.nqb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  AttnSplit sp;
+  if (variant >= 4 && variant <= 7 && part_mode != 1)
+    sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
+                         attn_ctas_per_sm(variant) * dev->sm_count, ceil_div(kv_len, static_cast<int>(kb)));
+  if (sp.split_first >= 0 && device < 64) {
+    const size_t need = static_cast<size_t>(sp.pieces) * kAttnBlock * (kAttnD + 2) * sizeof(float);
+    std::lock_guard<std::mutex> lk(g_attn_ws_mu);
+    AttnWorkspace& ws = g_attn_ws[device];
+    if (ws.bytes < need) {
+      // No allocation while the stream is being captured: use the 3-D grid then.
+      cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+      SF_CUDA_TRY(cudaStreamIsCapturing(s, &cap));
+      if (cap == cudaStreamCaptureStatusNone) {
+        if (ws.ptr) SF_CUDA_TRY(cudaFree(ws.ptr));
+        ws.ptr = nullptr;
+        ws.bytes = 0;
+        SF_CUDA_TRY(cudaMalloc(&ws.ptr, need));
+        ws.bytes = need;
+      }
+    }
+    if (ws.bytes >= need) {
+      a.split_first = sp.split_first;
+      a.split_k = sp.split_k;
+      a.ws_o = static_cast<float*>(ws.ptr);
+      a.ws_ml = a.ws_o + static_cast<size_t>(sp.pieces) * kAttnBlock * kAttnD;
+      grid = dim3(static_cast<unsigned>(sp.split_first + sp.pieces), 1, 1);
+    }
+  }
   // Share of the exp2 pairs computed on the FMA pipe, in quarters (tuning knob).
   const int emu = env_int("SF_ATTN_EMU", 0);
   st = dtype == kBF16
@@ -1162,5 +1273,13 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
            : launch_attention_variant<false>(variant, emu, grid, mq, mk, mv, a, s, device);
   if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
+  if (a.split_first >= 0) {
+    const unsigned n_split = static_cast<unsigned>(sp.pieces / sp.split_k);
+    if (dtype == kBF16)
+      attention_merge_kernel<true><<<n_split, kAttnBlock, 0, s>>>(a);
+    else
+      attention_merge_kernel<false><<<n_split, kAttnBlock, 0, s>>>(a);
+    SF_CUDA_TRY(cudaGetLastError());
+  }
   return SF_OK;
 }

@@ -70,22 +70,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended until it completes or `hint_ns` has passed, instead of returning
+// at once, so a waiting warp takes no issue slots from the warps at work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with parity `parity` of `bar` to complete.
 // Returns false (after recording `code` in *err and raising *abort) on
 // timeout, or immediately when another role has already raised *abort.
 // `sleep_ns` > 0 backs off between polls (for long waits off the critical
 // path, so that polling warps leave issue slots to the MMA and TMA threads).
+// `suspend_ns` > 0 polls with mbar_try_wait_suspend (the limit and the abort
+// flag are then checked after every poll).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           volatile int* abort_flag,
                                           unsigned long long limit_ns = kWaitLimitNs,
-                                          uint32_t sleep_ns = 0) {
+                                          uint32_t sleep_ns = 0, uint32_t suspend_ns = 0) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (sleep_ns) __nanosleep(sleep_ns);
-    if (mbar_try_wait(addr, parity)) return true;
-    if ((i & 63u) == 0) {
+    if (suspend_ns ? mbar_try_wait_suspend(addr, parity, suspend_ns) : mbar_try_wait(addr, parity))
+      return true;
+    if (suspend_ns || (i & 63u) == 0) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > limit_ns) {
         *abort_flag = 1;

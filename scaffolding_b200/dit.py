@@ -218,7 +218,7 @@ class DitStack:
         # the gathered keys (minus the local slice) merges it.
         self.overlap = (self.fused and plan.kv_exchange
                         and os.environ.get("SF_KV_OVERLAP", "1") != "0"
-                        and os.environ.get("SF_ATTN_VARIANT", "6") in ("4", "5", "6"))
+                        and os.environ.get("SF_ATTN_VARIANT", "6") in ("4", "5", "6", "7"))
         self.part_o = self.part_ml = None
         self.comm_stream = self.ev_kv = self.ev_gather = None
         if self.overlap:
@@ -395,9 +395,15 @@ class DitStack:
 
     def launches_per_forward(self) -> int:
         p = self.plan
-        if self.fused:
-            return self.L * (7 if self.overlap else 6)
         q_rows = p.tokens if p.whole_samples else p.m
+        if self.fused:
+            # five linears, then the attention call(s): a split last wave adds a merge launch
+            if self.overlap:
+                n_attn = 1 + E.attention_launch_count(1, self.H, p.m, p.tokens, 2, device=self.dev)
+            else:
+                n_attn = E.attention_launch_count(p.samples_per_rank, self.H, q_rows, p.tokens, 0,
+                                                  device=self.dev)
+            return self.L * (5 + n_attn)
         chunks = (q_rows + self.chunk - 1) // self.chunk
         return self.L * (5 + 3 * chunks)
 

@@ -279,6 +279,22 @@ def attention(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride,
           "sf_attention_fwd")
 
 
+def attention_launch_count(batch, heads, q_len, kv_len, part_mode=0, device=None):
+    """Kernel launches of one attention / attention_partial call of these
+    sizes (sf_attention_launch_count): 1, or 2 with a split last wave."""
+    prev = current_device()
+    if device is not None and device != prev:
+        set_device(device)
+    try:
+        n = C.c_int32()
+        check(lib.sf_attention_launch_count(batch, heads, q_len, kv_len, part_mode, C.byref(n)),
+              "sf_attention_launch_count")
+        return n.value
+    finally:
+        if device is not None and device != prev:
+            set_device(prev)
+
+
 def attention_partial(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride, v, ldv,
                       v_bstride, o, ldo, o_bstride, scale, skip_lo, skip_hi, part_o, part_ml,
                       part_mode, dtype=DT_BF16, head_dim=64, stream=None, device=None):

@@ -59,10 +59,10 @@ def fp32_mode(mode):
 
 def attn_oracle_opts(variant=None):
     """oracle.flash_attention settings that restate a fused-attention kernel:
-    its key block and whether its row bases are integers (variants 4, 5 and
-    6, the default: O in TMEM with lazily raised integer bases; 1-3: real
+    its key block and whether its row bases are integers (variants 4-7, 6
+    the default: O in TMEM with lazily raised integer bases; 1-3: real
     bases).  SF_ATTN_VARIANT selects the active kernel, as in the engine."""
     import os
     v = int(variant or os.environ.get("SF_ATTN_VARIANT", "6") or 6)
-    block = {1: 128, 2: 128, 3: 96, 4: 64, 5: 128, 6: 64}.get(v, 64)
+    block = {1: 128, 2: 128, 3: 96, 4: 64, 5: 128, 6: 64, 7: 32}.get(v, 64)
     return {"block": block, "integer_base": v >= 4}

@@ -151,13 +151,20 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
     assert device_error(0) == 0
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6])
-def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant):
+@pytest.mark.parametrize("split", ["1", "0"])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6, 7])
+def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant, split):
     """Each fused-attention configuration (SF_ATTN_VARIANT) on a ragged case
     with q_len != kv_len and large logits, against the oracle restating that
-    configuration's key block and row bases."""
+    configuration's key block and row bases; with the split last wave (key
+    pieces merged by a second kernel; variants 4-7 at these sizes) and with
+    the one-CTA-per-query-block grid (SF_ATTN_SPLIT=0)."""
+    from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
     monkeypatch.setenv("SF_ATTN_VARIANT", str(variant))
+    monkeypatch.setenv("SF_ATTN_SPLIT", split)
+    expect = 2 if (variant >= 4 and split == "1") else 1
+    assert E.attention_launch_count(1, 2, 300, 641) == expect
     rng = np.random.default_rng(40 + variant)
     B, H, Lq, Lk = 1, 2, 300, 641
     q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
