@@ -581,7 +581,7 @@ def run_gpu_arm(args, dist):
             roof["frac"] = roof["achieved"] / peak
             roof["launch_ms_mean"] = ms_top
             if top == "attn":
-                roof["kernel"] = "sf::attention_fwd_kernel (tcgen05, fused QK^T-softmax-PV)"
+                roof["kernel"] = "sf::attention_fwd2_kernel (tcgen05, fused QK^T-softmax-PV, P in TMEM)"
                 roof["algorithmic_flops_per_launch"] = fl
         roof["kernel_share"] = totals[top] / sum(totals.values())
         roof["top_kernel"] = top
