@@ -128,6 +128,7 @@ struct Plan {
   int bn = 128;
   bool b_mn = false;
   int splits = 1;
+  bool ws_slices = false; // split-K partials stored per split (no zeroing) and summed by the finaliser
   bool promote = false; // fp32-accurate: chunked TMEM accumulation promoted to registers
   bool pair = false;    // 2-CTA cluster (cta_group::2) kernel, 256-row pair tiles
   int a_box_rows = 128; // pair kernel: rows per A box (fewer for skinny M)
@@ -227,9 +228,11 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     if (p.K >= kPromoteMinK && pl.bn <= 128) pl.promote = true;
     return pl;
   }
-  // M <= 4 always; up to SF_GEMV_MAX_M (<= 8) on the balanced kernel (K % 256 == 0).
+  // The balanced GEMV kernel (K % 256 == 0) for M <= SF_GEMV_MAX_M (default 2;
+  // from M = 3 the swap-AB tensor-core path streams the weights faster on
+  // B200), the plain GEMV kernel for M <= 4 otherwise.
   const int gemv_max_m = (p.K % 256 == 0 && env_int("SF_GEMV_SEG", 1))
-                             ? std::min(8, env_int("SF_GEMV_MAX_M", 4))
+                             ? std::min(8, env_int("SF_GEMV_MAX_M", 2))
                              : 4;
   if (batch == 1 && p.M <= gemv_max_m && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
       ovr != SF_KERNEL_TCGEN05 && ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_GEMV", 1)) {
@@ -237,11 +240,14 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     pl.kind = kPlanGemv;
     return pl;
   }
-  // Skinny M on B200 (graph-replayed, K = 4096): M <= 32 is fastest on the
-  // swap-AB kernel (weights fill the 128-row MMA side), M = 33..256 on CTA
-  // pairs holding every activation row in one pair tile.
-  const int pair_min_m = env_int("SF_SKINNY_PAIR_MIN_M", 33);
-  if (batch == 1 && p.M <= 256 && p.M >= pair_min_m && p.N >= 1024 && p.K >= 64 &&
+  // Skinny M on B200 (graph-replayed, K = 4096): with k-balanced split-K the
+  // swap-AB kernel (weights fill the 128-row MMA side) is fastest up to
+  // M = 128, and at N = 4096 up to M = 256; wide outputs with M = 129..256
+  // run on CTA pairs holding every activation row in one pair tile.
+  const int pair_min_m = env_int("SF_SKINNY_PAIR_MIN_M", 129);
+  const int pair_min_n = env_int("SF_SKINNY_PAIR_MIN_N", 8192);
+  if (batch == 1 && p.M <= 256 && p.M >= pair_min_m && p.N >= std::max(1024, pair_min_n) &&
+      p.K >= 64 &&
       ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_SKINNY_PAIR", 1)) {
     // Skinny M on CTA pairs: activations = A (one pair tile), weights = B
     // split into ~one tile per SM pair.
@@ -257,14 +263,34 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     const int64_t tiles = ceil_div(p.N, 128);
     const int64_t kb = ceil_div(p.K, 64);
     int64_t splits = 1;
-    if (tiles * 2 <= sm_count && kb >= 8) {
+    if (env_int("SF_SWAP_BALANCE", 1) && kb >= 8) {  // tuning knob
+      // The weight stream is shared evenly only when every SM has the same
+      // number of k-blocks: pick the split count s (>= 4 k-blocks per split)
+      // minimising the busiest SM's k-blocks, ceil(tiles*s / SMs) * ceil(kb/s),
+      // plus the partials' write + read (s*M*N*8 bytes over all SMs, in units
+      // of one 16 KB weight k-block per SM).
+      double best = static_cast<double>(ceil_div(tiles, sm_count) * kb);
+      for (int64_t s = 2; s <= kb / 4; ++s) {
+        const int64_t per = ceil_div(kb, s);
+        const int64_t ss = ceil_div(kb, per);
+        const double t = static_cast<double>(ceil_div(tiles * ss, sm_count) * per) +
+                         static_cast<double>(ss * p.M * p.N * 8) / (16384.0 * sm_count);
+        if (t < best - 1e-9) {
+          best = t;
+          splits = ss;
+        }
+      }
+      pl.ws_slices = splits > 1;
+    } else if (tiles * 2 <= sm_count && kb >= 8) {
       splits = std::min<int64_t>(kb / 4, sm_count / tiles);
       splits = std::max<int64_t>(splits, 1);
       const int64_t per = ceil_div(kb, splits);
       splits = ceil_div(kb, per);
     }
     pl.splits = static_cast<int>(splits);
-    if (pl.splits > 1) pl.ws_bytes = static_cast<size_t>(p.M) * static_cast<size_t>(p.N) * 4u;
+    if (pl.splits > 1)
+      pl.ws_bytes = static_cast<size_t>(p.M) * static_cast<size_t>(p.N) * 4u *
+                    static_cast<size_t>(pl.ws_slices ? pl.splits : 1);
     return pl;
   }
   pl.kind = kPlanTc;
@@ -324,8 +350,36 @@ static int32_t launch_tc_cfg(const CUtensorMap& ma, const CUtensorMap& mb, const
                                      Cfg::SMEM_BYTES));
     attr_set[device] = true;
   }
-  gemm_tc_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ma, mb, t_map_c, a);
-  SF_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  SF_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<Cfg>, ma, mb, t_map_c, a));
+  return SF_OK;
+}
+
+// Launch of a kernel that waits for its predecessor with griddepcontrol
+// (programmatic dependent launch when `pdl`).
+template <class... KArgs, class... Args>
+static int32_t launch_maybe_pdl(bool pdl, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                void (*kernel)(KArgs...), Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  SF_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
   return SF_OK;
 }
 
@@ -576,11 +630,17 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
                  : 0;
   a.ws = nullptr;
   a.ldw = 0;
+  a.ws_slice = 0;
   a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
   a.epi_sleep_ns = env_int("SF_EPI_SLEEP", 0);  // tuning knob
   a.a_box_rows = pl.pair ? pl.a_box_rows : 128;
   a.tma_store = 0;
+  // Programmatic dependent launch of the 1-CTA kernel (tuning knobs: SF_PDL=0
+  // off; SF_PDL_PF_TC weight k-blocks prefetched before the wait, skinny only).
+  a.pdl = (!pl.pair && env_int("SF_PDL", 1)) ? 1 : 0;
+  a.pdl_pf = (a.pdl && p.M <= 256) ? std::max(0, env_int("SF_PDL_PF_TC", 8)) : 0;
+  a.pdl_pf_b = swap ? 0 : 1;
   memset(&t_map_c, 0, sizeof(t_map_c));
   if (!swap && pl.splits == 1 && a.vec_ok && env_int("SF_TMA_STORE", 1)) {
     // Epilogue chunks of CH columns x 32 rows, stored by TMA with the swizzle
@@ -612,7 +672,10 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   if (pl.splits > 1) {
     a.ws = static_cast<float*>(p.ws);
     a.ldw = p.N;  // output orientation [M][N]
-    SF_CUDA_TRY(cudaMemsetAsync(p.ws, 0, static_cast<size_t>(p.M) * p.N * 4u, p.stream));
+    if (pl.ws_slices)
+      a.ws_slice = p.M * p.N;
+    else
+      SF_CUDA_TRY(cudaMemsetAsync(p.ws, 0, static_cast<size_t>(p.M) * p.N * 4u, p.stream));
   }
   const int64_t units = total * pl.splits;
   if (pl.pair) return dispatch_tc2(fmt, pl.bn, ma, mbm, a, total, p.stream, device);
@@ -620,10 +683,13 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   st = dispatch_tc(fmt, pl.b_mn, pl.promote, pl.bn, ma, mbm, a, grid, p.stream, device);
   if (st != SF_OK) return st;
   if (pl.splits > 1) {
-    epilogue_finalize_kernel<<<grid_for(p.M * p.N, dev.sm_count), 256, 0, p.stream>>>(
-        static_cast<const float*>(p.ws), p.N, static_cast<int>(p.M), static_cast<int>(p.N), p.C,
-        p.out_dt, p.ldc, to_epi(p.epi, p.out_dt));
-    SF_CUDA_TRY(cudaGetLastError());
+    st = launch_maybe_pdl(a.pdl != 0, dim3(static_cast<unsigned>(grid_for(p.M * p.N, dev.sm_count))),
+                          dim3(256), 0, p.stream, epilogue_finalize_kernel,
+                          static_cast<const float*>(p.ws), static_cast<int64_t>(p.N),
+                          static_cast<int>(p.M), static_cast<int>(p.N), p.C, static_cast<int>(p.out_dt),
+                          static_cast<int64_t>(p.ldc), to_epi(p.epi, p.out_dt),
+                          pl.ws_slices ? pl.splits : 1, static_cast<int64_t>(a.ws_slice));
+    if (st != SF_OK) return st;
   }
   return SF_OK;
 }
@@ -663,15 +729,17 @@ static int32_t launch_gemv_seg(const Problem& p, const EpilogueArgs& e, int sm_c
   const size_t smem = static_cast<size_t>(ceil_div(p.N, G)) * MM * 4;
   const uint16_t* x = static_cast<const uint16_t*>(p.A);
   const uint16_t* w = static_cast<const uint16_t*>(p.B);
-  const int grid = static_cast<int>(G);
+  // Programmatic dependent launch (tuning knobs: SF_PDL=0 turns it off,
+  // SF_PDL_PF sets the weight units each warp prefetches before its wait).
+  const bool pdl = env_int("SF_PDL", 1) != 0;
+  const int pf_units = pdl ? std::max(0, std::min(32, env_int("SF_PDL_PF", 8))) : 0;
+  const int n = static_cast<int>(p.N), k = static_cast<int>(p.K);
+  const dim3 grid(static_cast<unsigned>(G)), block(kSegWarps * 32);
   if (p.in_dt == kBF16)
-    gemv_seg_kernel<MM, R, U, true><<<grid, kSegWarps * 32, smem, p.stream>>>(
-        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
-  else
-    gemv_seg_kernel<MM, R, U, false><<<grid, kSegWarps * 32, smem, p.stream>>>(
-        x, p.lda, w, p.ldb, p.C, p.out_dt, p.ldc, static_cast<int>(p.N), static_cast<int>(p.K), e);
-  SF_CUDA_TRY(cudaGetLastError());
-  return SF_OK;
+    return launch_maybe_pdl(pdl, grid, block, smem, p.stream, gemv_seg_kernel<MM, R, U, true>, x,
+                            p.lda, w, p.ldb, p.C, static_cast<int>(p.out_dt), p.ldc, n, k, e, pf_units);
+  return launch_maybe_pdl(pdl, grid, block, smem, p.stream, gemv_seg_kernel<MM, R, U, false>, x,
+                          p.lda, w, p.ldb, p.C, static_cast<int>(p.out_dt), p.ldc, n, k, e, pf_units);
 }
 
 static bool gemv_seg_ok(const Problem& p) {

@@ -69,10 +69,17 @@ struct GemmTcArgs {
   int tma_store;        // 1: stores go through shared memory + TMA (map tmC)
   float* ws;            // split-K fp32 accumulation buffer (output orientation)
   int64_t ldw;
+  int64_t ws_slice;     // 0: splits red.add into ws; > 0: split s stores into ws + s * ws_slice
   EpilogueArgs epi;
   int* err;             // device error word
   int epi_sleep_ns;     // poll back-off of the epilogue's accumulator waits (0 = spin)
   int a_box_rows;       // pair kernel: rows per A box (128, or fewer for skinny M)
+  // Programmatic dependent launch (host: launch with the attribute when pdl
+  // is set).  Before waiting for the previous grid the producer prefetches
+  // the first pdl_pf k-blocks of its first unit's weight operand (A when
+  // pdl_pf_b == 0, else a K-major B) into L2; operands the previous kernel
+  // may write are read, and outputs written, only after the wait.
+  int pdl, pdl_pf, pdl_pf_b;
 };
 
 // Work units of one CTA as (tile, k-block range [kb0, kb1)): unit
@@ -242,17 +249,22 @@ __device__ __forceinline__ void epilogue_compute(const GemmTcArgs& p, int i, int
 // outputs TMA cannot describe).
 template <int CH>
 __device__ __forceinline__ void epilogue_store(const GemmTcArgs& p, int i, int j0, int b0, int b1,
-                                               const float* acc) {
+                                               const float* acc, int split = 0) {
   const EpilogueArgs& e = p.epi;
   if (i >= p.M) return;
   if (p.k_splits > 1) {
-    // Partial sums: raw accumulator into the fp32 workspace.
+    // Partial sums: raw accumulator into the fp32 workspace, added into one
+    // buffer or stored into this split's own slice (no zeroing needed).
+    float* const ws = p.ws + (p.ws_slice > 0 ? split * p.ws_slice : 0);
 #pragma unroll
     for (int t = 0; t < CH; ++t) {
       const int j = j0 + t;
       if (j < p.N) {
-        float* dst = p.c_trans ? p.ws + (int64_t)j * p.ldw + i : p.ws + (int64_t)i * p.ldw + j;
-        atomicAdd(dst, acc[t]);
+        float* dst = p.c_trans ? ws + (int64_t)j * p.ldw + i : ws + (int64_t)i * p.ldw + j;
+        if (p.ws_slice > 0)
+          *dst = acc[t];
+        else
+          atomicAdd(dst, acc[t]);
       }
     }
     return;
@@ -379,6 +391,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -411,6 +424,20 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   if (warp == 0) {
     // ───────────── TMA producer ─────────────
     if (lane == 0) {
+      if (p.pdl_pf > 0) {
+        WorkIter it0(p);
+        int t0, k0, k1, mb, nb, b0, b1;
+        if (it0.next(p, t0, k0, k1)) {
+          tile_coords(t0, p, mb, nb, b0, b1);
+          for (int kb = k0; kb < min(k1, k0 + p.pdl_pf); ++kb) {
+            if (!p.pdl_pf_b)
+              tma_prefetch_l2_4d(&tmA, kb * BK, mb * BM, b0, b1);
+            else if constexpr (!Cfg::B_MN)
+              tma_prefetch_l2_4d(&tmB, kb * BK, nb * BN, b0, b1);
+          }
+        }
+      }
+      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
@@ -523,6 +550,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     }
   } else {
     // ───────────── epilogue (warps 2..9) ─────────────
+    pdl_wait();  // outputs (and residual inputs) belong to the previous grid until it completes
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = quad * 32 + lane;
@@ -555,7 +583,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             if (tma_out)
               epilogue_store_tma<CH>(p, &tmC, slot, lane, i, mb * BM + quad * 32, j0, b0, b1, v);
             else
-              epilogue_store<CH>(p, i, j0, b0, b1, v);
+              epilogue_store<CH>(p, i, j0, b0, b1, v, kb0 / p.kb_per_split);
           }
         }
         tc_fence_before();
@@ -601,7 +629,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               epilogue_store_tma<CH>(p, &tmC, slot, lane, i, mb * BM + quad * 32, j0, b0, b1,
                                      &racc[q * CH]);
             else
-              epilogue_store<CH>(p, i, j0, b0, b1, &racc[q * CH]);
+              epilogue_store<CH>(p, i, j0, b0, b1, &racc[q * CH], kb0 / p.kb_per_split);
           }
         }
       }

@@ -19,6 +19,7 @@
 #include <cstdint>
 
 #include "epilogue.cuh"
+#include "ptx.cuh"
 
 namespace sf {
 
@@ -124,21 +125,27 @@ static __global__ void __launch_bounds__(kGemvWarps * 32)
 // shared memory (warp butterfly + one shared atomic per row and activation
 // row); after a CTA barrier the fused epilogue writes the CTA's outputs.
 // Requires K % 256 == 0 and 16-byte aligned rows of x and W.
+//
+// Programmatic dependent launch: the kernel lets the next one in the stream
+// start at once, and before it waits for the previous grid (griddepcontrol)
+// it only zeroes its shared memory and prefetches the first `pf_units` units
+// of each warp's weights into L2 -- the weights are not written by any
+// kernel on the path, while x and y are touched only after the wait.  Back to
+// back launches so overlap one kernel's launch, prologue and first weight
+// bytes with the previous kernel's tail.
 constexpr int kSegWarps = 16;
 
 template <int MM, int R, int U, bool BF16>
 static __global__ void __launch_bounds__(kSegWarps * 32, 1)
     gemv_seg_kernel(const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ W,
                     int64_t ldw, void* __restrict__ y, int out_dtype, int64_t ldy, int N, int K,
-                    EpilogueArgs e) {
+                    EpilogueArgs e, int pf_units) {
   extern __shared__ float sacc[];  // [rows of this CTA][MM]
+  pdl_launch_dependents();
   const int G = gridDim.x;
   const int r0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * N / G);
   const int r1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * N / G);
   const int rows = r1 - r0;
-  for (int t = threadIdx.x; t < rows * MM; t += blockDim.x) sacc[t] = 0.0f;
-  __syncthreads();
-
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int spr = K >> 8;                       // 512-byte steps per row
@@ -146,6 +153,17 @@ static __global__ void __launch_bounds__(kSegWarps * 32, 1)
   const int total = groups * spr;
   const int u0 = static_cast<int>(static_cast<int64_t>(warp) * total / kSegWarps);
   const int u1 = static_cast<int>(static_cast<int64_t>(warp + 1) * total / kSegWarps);
+  // L2 prefetch of this warp's first units: lane l takes row l % R of unit l / R.
+  for (int l = lane; l < pf_units * R; l += 32) {
+    const int uu = u0 + l / R;
+    const int g = uu / spr;
+    const int row = r0 + g * R + l % R;
+    if (uu < u1 && row < r1)
+      prefetch_l2_bulk(W + static_cast<int64_t>(row) * ldw + (uu - g * spr) * 256, 512);
+  }
+  for (int t = threadIdx.x; t < rows * MM; t += blockDim.x) sacc[t] = 0.0f;
+  pdl_wait();
+  __syncthreads();
 
   float acc[R][MM];
 #pragma unroll

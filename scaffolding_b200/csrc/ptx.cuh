@@ -126,7 +126,36 @@ __device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, uint32_t parity,
   return true;
 }
 
+// ─────────────────────── programmatic dependent launch ───────────────────────
+
+// Lets the next kernel of the stream (launched with programmatic stream
+// serialisation) start its prologue while this grid is still running.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Waits until the grids this one depends on have completed and their memory
+// is visible (returns at once for a launch without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gptr)),
+               "r"(bytes)
+               : "memory");
+}
+
 // ───────────────────────────── TMA loads ───────────────────────────────────
+
+// L2 prefetch of the box a 4-D tiled TMA load at these coordinates would read.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -230,12 +230,17 @@ static __global__ void unary_act_kernel(const void* __restrict__ x, int x_dtype,
 // out[r, c] = epilogue(ws[r, c]) for the split-K / K == 0 paths (ws == null => 0).
 static __global__ void epilogue_finalize_kernel(const float* __restrict__ ws, int64_t ldw, int rows,
                                          int cols, void* __restrict__ out, int out_dtype,
-                                         int64_t ldc, EpilogueArgs e) {
+                                         int64_t ldc, EpilogueArgs e, int slices = 1,
+                                         int64_t slice = 0) {
+  pdl_launch_dependents();
+  pdl_wait();  // the partials come from the previous grid
   const int64_t total = (int64_t)rows * cols;
   for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
        t += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(t / cols), c = (int)(t - (t / cols) * cols);
-    const float acc = ws ? ws[(int64_t)r * ldw + c] : 0.0f;
+    float acc = 0.0f;  // sum of the split slices, in split order
+    if (ws)
+      for (int s = 0; s < slices; ++s) acc += ws[s * slice + (int64_t)r * ldw + c];
     const float bias_v = e.bias ? load_as_f32(e.bias, c, e.bias_dtype) : 0.0f;
     const float res_v =
         e.residual ? load_as_f32(e.residual, (int64_t)r * e.ldr + c, e.residual_dtype) : 0.0f;

@@ -67,15 +67,19 @@ def test_workspace_sizes():
     assert ws(4096, 4096, 4096, 0, 1, 2) == 0
     # fp32 accurate (3xTF32): K-concatenated hi/lo panels for A and B
     assert ws(512, 4096, 1024, 0, 1, 0) == (512 + 4096) * 3 * 1024 * 4
-    # skinny bf16, M <= 32: swap-AB; too few weight tiles -> split-K fp32 accumulator
-    assert ws(8, 4096, 4096, 0, 1, 2) == 8 * 4096 * 4
-    # M = 33..256 on CTA pairs (one pair tile holds all M rows): no workspace
-    assert ws(64, 4096, 4096, 0, 1, 2) == 0
+    # skinny bf16, M <= 32: swap-AB; the k-blocks are split so that every SM
+    # streams the same share of the weights, one fp32 partial slice per split
+    # (148 SMs: 32 tiles x 13 splits of 5 k-blocks; 86 tiles x 5 splits)
+    assert ws(8, 4096, 4096, 0, 1, 2) == 13 * 8 * 4096 * 4
+    assert ws(8, 11008, 4096, 0, 1, 2) == 5 * 8 * 11008 * 4
+    # M = 33..128 (and up to 256 at N < 8192) on the swap-AB path too
+    assert ws(64, 4096, 4096, 0, 1, 2) == 4 * 64 * 4096 * 4
+    # wide outputs with M = 129..256 on CTA pairs (one pair tile holds all M
+    # rows): no workspace
     assert ws(226, 11008, 4096, 0, 1, 2) == 0
-    # the same shapes on the swap-AB path
+    # the same shape on the swap-AB path: too many partial bytes to split
     os.environ["SF_SKINNY_PAIR"] = "0"
     try:
-        assert ws(64, 4096, 4096, 0, 1, 2) == 64 * 4096 * 4
         assert ws(226, 11008, 4096, 0, 1, 2) == 0
     finally:
         del os.environ["SF_SKINNY_PAIR"]

@@ -65,11 +65,12 @@ def test_matmul_nn_16bit(gpu, ops, dt, M, N, K):
 @pytest.mark.parametrize("N", [4096, 11008])
 def test_skinny_linear_bias_gelu(gpu, ops, M, N, path, monkeypatch):
     """Benchmark config 3: bf16 x[M,4096] W[N,4096] b[N], bias + GELU-tanh, on
-    the skinny CTA-pair path (default) and on the swap-AB path."""
+    the skinny CTA-pair path and on the swap-AB path."""
     if path == "swap":
         monkeypatch.setenv("SF_SKINNY_PAIR", "0")
     else:
         monkeypatch.setenv("SF_SKINNY_PAIR_MIN_M", "5")  # M = 1 stays on the GEMV
+        monkeypatch.setenv("SF_SKINNY_PAIR_MIN_N", "1")
     x, W, b = O.skinny_inputs(M, N, seed=M + N)
     bf = np_dtype("bf16")
     gx, gw, gb = (ops.gputensor_from_numpy(t.astype(bf)) for t in (x, W, b))
@@ -351,6 +352,7 @@ def test_skinny_pair_ragged(gpu, ops, M, N, K, monkeypatch):
     """Skinny CTA-pair path: A boxes of round_up(M, 8) rows, the odd CTA idle
     when M <= 128, ragged N tiles and K, fp16 and bf16."""
     monkeypatch.setenv("SF_SKINNY_PAIR_MIN_M", "1")
+    monkeypatch.setenv("SF_SKINNY_PAIR_MIN_N", "1")
     for dt in ("bf16", "f16"):
         rng = np.random.default_rng(M * 31 + N + K)
         ga, a = to_device(ops, _rand(rng, M, K), dt)
@@ -363,8 +365,9 @@ def test_skinny_pair_ragged(gpu, ops, M, N, K, monkeypatch):
 @pytest.mark.parametrize("M,N,K", [(8, 4096, 4096), (33, 1000, 777), (200, 3000, 1000), (5, 300, 4160),
                                    (64, 11008, 4096)])
 def test_swap_ab_path(gpu, ops, M, N, K, monkeypatch):
-    """Swap-AB skinny GEMM (split-K where the weight tiles are too few), with
-    a bias + GELU + residual epilogue."""
+    """Swap-AB skinny GEMM (k-blocks split so that every SM streams the same
+    share of the weights, partial slices summed by the finaliser), with a
+    bias + GELU + residual epilogue; the split count differs per shape."""
     from scaffolding_b200 import engine as E
     monkeypatch.setenv("SF_SKINNY_PAIR", "0")
     rng = np.random.default_rng(M * 3 + N + K)
