@@ -76,11 +76,16 @@ def main():
             # rank's own keys and the gathered ones (another fp32 summation
             # order): the bf16 bar instead of bit equality.
             split = plan.kv_exchange and st.overlap
+            # The split dispatch of the attention's last wave (key-range pieces,
+            # merged) depends on how many query blocks a call has, so it too
+            # changes the fp32 summation order between the sharded and the
+            # one-GPU run; bit equality is required only with it off.
+            exact = os.environ.get("SF_ATTN_SPLIT") == "0" and not split
             # Two bf16 layers re-round every intermediate, so one-ulp flips in
             # them carry into cancelling outputs: the aggregate bar here.
             close = (O.rel_frobenius(got, ref) < 2e-3
                      and float(np.abs(got - ref).max()) <= 2.0 ** -5 * float(np.abs(ref).max()))
-            failures += 0 if (close if split else same) else 1
+            failures += 0 if (same if exact else close) else 1
         if kv:
             lib.sf_comm_destroy(C.c_void_p(kv))
         td.barrier()
