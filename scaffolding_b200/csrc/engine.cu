@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "common.h"
@@ -1165,13 +1166,15 @@ static AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
   return sp;
 }
 
-// Per-device workspace of the split pieces (grown on demand, never shrunk).
+// Workspace of the split pieces, one per (device, stream) so that calls on
+// different streams never share it (grown on demand, never shrunk; calls on
+// one stream run in order).
 struct AttnWorkspace {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
 static std::mutex g_attn_ws_mu;
-static AttnWorkspace g_attn_ws[64];
+static std::map<std::pair<int, void*>, AttnWorkspace> g_attn_ws;
 
 static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                               int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
@@ -1310,10 +1313,13 @@ static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32
   if (variant >= 4 && variant <= 7 && part_mode != 1)
     sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
                          attn_ctas_per_sm(variant) * dev->sm_count, ceil_div(kv_len, static_cast<int>(kb)));
-  if (sp.split_first >= 0 && device < 64) {
+  // Held until the launches are queued, so that no other thread's call on the
+  // same stream regrows (frees) the workspace in between.
+  std::unique_lock<std::mutex> ws_lock(g_attn_ws_mu, std::defer_lock);
+  if (sp.split_first >= 0) {
     const size_t need = static_cast<size_t>(sp.pieces) * kAttnBlock * (kAttnD + 2) * sizeof(float);
-    std::lock_guard<std::mutex> lk(g_attn_ws_mu);
-    AttnWorkspace& ws = g_attn_ws[device];
+    ws_lock.lock();
+    AttnWorkspace& ws = g_attn_ws[std::make_pair(device, stream)];
     if (ws.bytes < need) {
       // No allocation while the stream is being captured: use the 3-D grid then.
       cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;

@@ -184,6 +184,50 @@ def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant, split):
     assert device_error(0) == 0
 
 
+def test_fused_attention_two_streams(gpu, ops):
+    """Split-dispatch calls on two streams at once (each stream has its own
+    piece workspace) give the same bits as the same calls run one by one."""
+    import ctypes as C
+
+    from scaffolding_b200 import engine as E
+    from scaffolding_b200._lib import lib
+    from tests.gpu_util import device_error
+    B, H, L = 1, 3, 700
+    W = H * 64
+    assert E.attention_launch_count(B, H, L, L) == 2
+    bf = np_dtype("bf16")
+    ins, outs = [], []
+    for seed in (71, 72):
+        rng = np.random.default_rng(seed)
+        g, _ = to_device(ops, rng.standard_normal((L, 3 * W), dtype=np.float32), "bf16")
+        ins.append(g)
+        outs.append([ops._alloc((L, W), bf, 0), ops._alloc((L, W), bf, 0)])
+
+    def call(i, o, stream):
+        base = ins[i].ptr
+        E.attention(B, H, L, L, base, 3 * W, L * 3 * W, base + W * 2, 3 * W, L * 3 * W,
+                    base + 2 * W * 2, 3 * W, L * 3 * W, o.ptr, W, L * W, 0.125, stream=stream)
+
+    for i in (0, 1):  # one by one on the default stream
+        call(i, outs[i][0], None)
+    E.check(lib.sf_device_synchronize(), "sync")
+    streams = []
+    for _ in (0, 1):
+        sp = C.c_void_p()
+        E.check(lib.sf_stream_create(0, 1, C.byref(sp)), "sf_stream_create")
+        streams.append(sp.value)
+    for _ in range(3):  # interleaved on two streams
+        for i in (0, 1):
+            call(i, outs[i][1], streams[i])
+    E.check(lib.sf_device_synchronize(), "sync")
+    for i in (0, 1):
+        a, b = (ops.gputensor_to_numpy(t).view(np.uint16) for t in outs[i])
+        assert np.array_equal(a, b), f"stream {i}"
+    for sp in streams:
+        lib.sf_stream_destroy(C.c_void_p(sp))
+    assert device_error(0) == 0
+
+
 def test_fused_attention_rejects_bad_arguments(gpu, ops):
     from scaffolding_b200._lib import SF_ERR_INVALID_ARGUMENT, SF_ERR_UNSUPPORTED, lib
     import ctypes as C
