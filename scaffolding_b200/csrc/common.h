@@ -32,6 +32,16 @@ struct DeviceInfo {
 // Lazily initialised per-device facts for the CURRENT device.
 int32_t current_device_info(DeviceInfo** out, int* device);
 
+// Error word of the no-alloc entry point on the CURRENT device (a static
+// device array, so that entry point never allocates): read into *value and
+// reset to zero when `clear`.  Reported by sf_device_error_status together
+// with the per-device word above.
+int32_t noalloc_error_word(int* value, bool clear);
+
+// Releases the fused attention's split-piece workspace held for `stream`
+// (called by sf_stream_destroy before the stream goes away).
+void attention_release_stream(void* stream);
+
 // Global knobs.
 int fp32_mode();
 int kernel_override();

@@ -18,6 +18,10 @@
 // streams, or from different host threads without ordering) race on the
 // array and produce wrong results -- order them on one stream.
 //
+// Errors: a bounded wait of these kernels that expires records its code in
+// a static device word of this file (not the runtime's per-device word,
+// which is cudaMalloc'd); sf_device_error_status reports both.
+//
 // Set-up: the first call on each device (with that device current) looks up
 // the array's device address with cudaGetSymbolAddress and sets the kernels'
 // shared-memory attributes.  Make that first call before any stream capture
@@ -149,6 +153,18 @@ int32_t launch(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmT
 }
 
 }  // namespace
+
+int32_t noalloc_error_word(int* value, bool clear) {
+  int v = 0;
+  SF_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(int)));
+  if (clear && v != 0) {
+    const int zero = 0;
+    SF_CUDA_TRY(cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int)));
+  }
+  *value = v;
+  return SF_OK;
+}
+
 }  // namespace sf
 
 using namespace sf;

@@ -348,7 +348,9 @@ int32_t sf_stream_create_priority(int32_t device, int32_t non_blocking, int32_t 
 }
 
 int32_t sf_stream_destroy(void* stream) {
-  if (stream) SF_CUDA_TRY(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
+  if (!stream) return SF_OK;
+  attention_release_stream(stream);
+  SF_CUDA_TRY(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
   return SF_OK;
 }
 
@@ -461,8 +463,12 @@ int32_t sf_device_error_status(int32_t device, int32_t* code, int32_t clear) {
   if (st != SF_OK) return st;
   int v = 0;
   SF_CUDA_TRY(cudaMemcpy(&v, info->err_word, sizeof(int), cudaMemcpyDeviceToHost));
-  *code = v;
   if (clear) SF_CUDA_TRY(cudaMemset(info->err_word, 0, sizeof(int)));
+  // The no-alloc linear records its timeouts in its own static word.
+  int w = 0;
+  st = noalloc_error_word(&w, clear != 0);
+  if (st != SF_OK) return st;
+  *code = v != 0 ? v : w;
   return SF_OK;
 }
 
