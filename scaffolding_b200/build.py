@@ -23,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libsf_engine.so")
 
-SOURCES = ["runtime.cu", "engine.cu", "noalloc.cu", "comm.cpp"]
+SOURCES = ["runtime.cu", "engine.cu", "attention.cu", "norm.cu", "noalloc.cu", "comm.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -42,22 +42,42 @@ def _flags(verbose_ptxas: bool) -> list[str]:
     return f
 
 
+def _local_includes(path: str, seen: set[str]) -> None:
+    """Add `path` and, recursively, the files it #includes with quotes."""
+    path = os.path.normpath(path)
+    if path in seen or not os.path.exists(path):
+        return
+    seen.add(path)
+    with open(path, errors="replace") as fh:
+        for line in fh:
+            line = line.strip()
+            if line.startswith("#include") and '"' in line:
+                name = line.split('"')[1]
+                _local_includes(os.path.join(os.path.dirname(path), name), seen)
+
+
 def _digest(paths: list[str], flags: list[str]) -> str:
     h = hashlib.sha256(" ".join(flags).encode())
     for p in sorted(paths):
+        h.update(p.encode())
         with open(p, "rb") as fh:
             h.update(fh.read())
     return h.hexdigest()
 
 
+def _tu_digest(src: str, flags: list[str]) -> str:
+    deps: set[str] = set()
+    _local_includes(os.path.join(CSRC, src), deps)
+    return _digest(sorted(deps), flags)
+
+
 def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = False) -> str:
-    """Compile the engine if any source changed; return the library path."""
+    """Compile the translation units whose sources (or local headers) changed
+    and relink the engine; return the library path."""
     nvcc = _nvcc()
     flags = _flags(verbose_ptxas)
-    deps = [os.path.join(CSRC, f) for f in os.listdir(CSRC)
-            if f.endswith((".cu", ".cuh", ".h", ".cpp"))]
-    deps.append(os.path.join(ROOT, "include", "sf_engine.h"))
-    digest = _digest(deps, flags)
+    digests = {src: _tu_digest(src, flags) for src in SOURCES}
+    digest = _digest([], flags + [digests[s] for s in SOURCES])
     stamp = LIB + ".sha256"
     if not force and os.path.exists(LIB) and os.path.exists(stamp):
         with open(stamp) as fh:
@@ -67,6 +87,11 @@ def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = False)
 
     def compile_one(src: str) -> tuple[str, str]:
         obj = os.path.join(BUILD, src + ".o")
+        ostamp = obj + ".sha256"
+        if not force and not verbose_ptxas and os.path.exists(obj) and os.path.exists(ostamp):
+            with open(ostamp) as fh:
+                if fh.read().strip() == digests[src]:
+                    return obj, ""
         cmd = [nvcc, *flags, "-c", os.path.join(CSRC, src), "-o", obj]
         if src.endswith(".cpp"):
             cmd = [nvcc, "-std=c++17", "-O3", "-Xcompiler", "-fPIC", *ARCH,
@@ -75,6 +100,8 @@ def build(verbose_ptxas: bool = False, force: bool = False, quiet: bool = False)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+        with open(ostamp, "w") as fh:
+            fh.write(digests[src])
         return obj, r.stderr
 
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:

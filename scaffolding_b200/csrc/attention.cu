@@ -1,0 +1,368 @@
+// Fused-attention entry points of the C ABI (sf_attention_fwd,
+// sf_attention_fwd_partial, sf_attention_launch_count): argument checks,
+// TMA descriptors, kernel choice, the split dispatch of the last wave and
+// its workspace.
+//
+// Kernels (attention_pp.cuh, attention.cuh):
+//   attention_pp_kernel     one CTA per SM with NT 128-query tiles sharing
+//                           each K/V block: NT = 4 with 64-key blocks
+//                           (default), NT = 2 with 128-key blocks
+//                           (SF_ATTN_KERNEL=3);
+//   attention_fwd2_kernel   four CTAs per SM, one 128-query tile each,
+//                           64-key blocks (SF_ATTN_KERNEL=2).
+// Both keep S and P in TMEM and O in a TMEM accumulator, with integer row
+// bases raised lazily, and support the key skips and partial modes of
+// sf_attention_fwd_partial.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "attention.cuh"
+#include "attention_pp.cuh"
+#include "common.h"
+#include "tma_host.h"
+
+namespace sf {
+namespace {
+
+using Attn2CfgV6 = Attn2Cfg<64, 2, true>;
+using AttnPp2 = AttnPpCfg<2, 128, 4>;  // kernel 3: two query tiles, 128-key blocks
+using AttnPp4 = AttnPpCfg<4, 64, 6>;   // kernel 4: four query tiles, 64-key blocks
+using AttnPp5 = AttnPpCfg<2, 64, 4>;   // kernel 5: two query tiles, 64-key blocks, 2 CTAs/SM
+
+// Which kernel runs: 2 (attention_fwd2_kernel), 3 or 4 (attention_pp_kernel
+// with two or four query tiles per CTA).
+int attn_kernel() {
+  const int k = env_int("SF_ATTN_KERNEL", 5);
+  return (k >= 2 && k <= 5) ? k : 5;
+}
+int attn_unit_rows(int kernel) {
+  return kernel == 2 ? kAttnBlock : kernel == 3 ? AttnPp2::ROWS : kernel == 5 ? AttnPp5::ROWS : AttnPp4::ROWS;
+}
+int attn_key_block(int kernel) {
+  return kernel == 2 ? Attn2CfgV6::KB : kernel == 3 ? AttnPp2::KB : kernel == 5 ? AttnPp5::KB : AttnPp4::KB;
+}
+int attn_ctas_per_sm(int kernel) {
+  return kernel == 2 ? Attn2CfgV6::MIN_BLOCKS : kernel == 3 ? AttnPp2::MIN_BLOCKS
+         : kernel == 5 ? AttnPp5::MIN_BLOCKS : AttnPp4::MIN_BLOCKS;
+}
+
+template <bool BF16>
+int32_t launch_fwd2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                    const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+  static bool attr_set[64] = {false};
+  if (device < 64 && !attr_set[device]) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Attn2CfgV6, 0>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2CfgV6::BYTES));
+    attr_set[device] = true;
+  }
+  attention_fwd2_kernel<BF16, Attn2CfgV6, 0><<<grid, kAttnThreads, Attn2CfgV6::BYTES, s>>>(mq, mk, mv, a);
+  return SF_OK;
+}
+
+template <bool BF16, class Cfg, int EMU>
+int32_t launch_pp_emu(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                      const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+  static bool attr_set[64] = {false};
+  if (device < 64 && !attr_set[device]) {
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_pp_kernel<BF16, Cfg, EMU>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
+    attr_set[device] = true;
+  }
+  attention_pp_kernel<BF16, Cfg, EMU><<<grid, Cfg::THREADS, Cfg::BYTES, s>>>(mq, mk, mv, a);
+  return SF_OK;
+}
+
+template <bool BF16, class Cfg>
+int32_t launch_pp(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                  const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+  switch (env_int("SF_ATTN_EMU", 0)) {
+    case 1: return launch_pp_emu<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
+    case 2: return launch_pp_emu<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
+    case 3: return launch_pp_emu<BF16, Cfg, 3>(grid, mq, mk, mv, a, s, device);
+    default: return launch_pp_emu<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
+  }
+}
+
+template <bool BF16>
+int32_t launch_kernel(int kernel, const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                      const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+  if (kernel == 2) return launch_fwd2<BF16>(grid, mq, mk, mv, a, s, device);
+  if (kernel == 3) return launch_pp<BF16, AttnPp2>(grid, mq, mk, mv, a, s, device);
+  if (kernel == 5) return launch_pp<BF16, AttnPp5>(grid, mq, mk, mv, a, s, device);
+  return launch_pp<BF16, AttnPp4>(grid, mq, mk, mv, a, s, device);
+}
+
+template <bool BF16>
+void launch_merge(int rows, unsigned n, const AttnArgs& a, cudaStream_t s) {
+  if (rows == kAttnBlock)
+    attention_merge_kernel<BF16, kAttnBlock><<<n, kAttnBlock, 0, s>>>(a);
+  else if (rows == AttnPp2::ROWS)
+    attention_merge_kernel<BF16, AttnPp2::ROWS><<<n, AttnPp2::ROWS, 0, s>>>(a);
+  else
+    attention_merge_kernel<BF16, AttnPp4::ROWS><<<n, AttnPp4::ROWS, 0, s>>>(a);
+}
+
+// Split dispatch plan (see AttnArgs::split_first).  U units on P resident
+// CTA slots take ceil(U / P) unit times; splitting the R = U mod P units of
+// the last wave into k key-range pieces takes floor(U / P) + ceil(R k / P) / k.
+// k in [2, min(32, key blocks)] minimises that; the split is used when it
+// saves more than 3 %.
+struct AttnSplit {
+  int split_first = -1, split_k = 1, pieces = 0;
+};
+AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
+  AttnSplit sp;
+  if (env_int("SF_ATTN_SPLIT", 1) == 0 || slots <= 0 || nkb < 2) return sp;
+  const int64_t full = units / slots, rem = units % slots;
+  if (rem == 0) return sp;
+  double best = 1.0;
+  int best_k = 1;
+  for (int k = 2; k <= std::min(32, nkb); ++k) {
+    const double t = static_cast<double>((rem * k + slots - 1) / slots) / k;
+    if (t < best - 1e-9) {
+      best = t;
+      best_k = k;
+    }
+  }
+  if (best_k == 1 || full + best > 0.97 * static_cast<double>(full + 1)) return sp;
+  sp.split_first = static_cast<int>(units - rem);
+  sp.split_k = best_k;
+  sp.pieces = static_cast<int>(rem) * best_k;
+  return sp;
+}
+
+// Workspace of the split pieces, one per (device, stream) so that calls on
+// different streams never share it; calls on one stream run in order.  The
+// per-thread default stream (cudaStreamPerThread) is a different stream in
+// every host thread, so its key also carries the thread.  A workspace grows
+// on demand (to twice the size asked for) and is never shrunk.  A buffer
+// that was handed to a launch while its stream was being captured may be
+// referenced by a CUDA graph that outlives any later call, so it is never
+// freed: when it is outgrown, or its stream is destroyed, it moves to a
+// retired list kept until the process exits.  Other buffers are freed then
+// (cudaFree waits for the work already queued on them).  A graph captured on
+// stream S and replayed on another stream still uses S's workspace, so its
+// replays must not overlap with direct calls on S.
+struct AttnWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  bool captured = false;  // handed out during a stream capture
+};
+struct AttnWsKey {
+  int device;
+  void* stream;
+  uint64_t thread;  // nonzero only for cudaStreamPerThread
+  bool operator<(const AttnWsKey& o) const {
+    if (device != o.device) return device < o.device;
+    if (stream != o.stream) return stream < o.stream;
+    return thread < o.thread;
+  }
+};
+std::mutex g_attn_ws_mu;
+std::map<AttnWsKey, AttnWorkspace> g_attn_ws;
+std::vector<void*> g_attn_ws_retired;
+
+uint64_t this_thread_tag() {
+  static thread_local int tag;
+  return static_cast<uint64_t>(reinterpret_cast<uintptr_t>(&tag));
+}
+
+// Drops a workspace buffer: retired if a capture may hold it, else freed.
+// Called with g_attn_ws_mu held.
+void attn_ws_drop(AttnWorkspace& ws) {
+  if (ws.ptr) {
+    if (ws.captured)
+      g_attn_ws_retired.push_back(ws.ptr);
+    else if (cudaFree(ws.ptr) != cudaSuccess)
+      cudaGetLastError();
+  }
+  ws = AttnWorkspace{};
+}
+
+int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                       int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
+                       const void* k, int64_t ldk, int64_t k_bstride, const void* v, int64_t ldv,
+                       int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride, float scale,
+                       int32_t dtype, int32_t skip_lo, int32_t skip_hi, float* part_o,
+                       float* part_ml, int32_t part_mode, void* stream) {
+  if (batch < 0 || heads < 0 || q_len < 0 || kv_len < 0)
+    return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
+  if (batch == 0 || heads == 0 || q_len == 0) return SF_OK;
+  if (kv_len == 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention over zero keys");
+  if (head_dim != kAttnD) return fail(SF_ERR_UNSUPPORTED, "fused attention needs head_dim 64 (got %d)", head_dim);
+  if (dtype != kBF16 && dtype != kF16) return fail(SF_ERR_INVALID_ARGUMENT, "fused attention dtype %d", dtype);
+  if (!(scale > 0.0f)) return fail(SF_ERR_INVALID_ARGUMENT, "attention scale must be positive");
+  if (!q || !k || !v || !o) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
+  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
+    if (!aligned16(ptr)) return fail(SF_ERR_INVALID_ARGUMENT, "attention operands must be 16-byte aligned");
+  for (int64_t st : {ldq, ldk, ldv, ldo, q_bstride, k_bstride, v_bstride, o_bstride})
+    if (!bytes16(st, 2) || st < 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention strides must be 16-byte multiples");
+  const int64_t row_min = static_cast<int64_t>(heads) * head_dim;
+  if (ldq < row_min || ldk < row_min || ldv < row_min || ldo < row_min)
+    return fail(SF_ERR_INVALID_ARGUMENT, "leading dimension < heads * head_dim");
+  if (heads > 65535 || batch > 65535) return fail(SF_ERR_UNSUPPORTED, "attention grid");
+  DeviceInfo* dev = nullptr;
+  int device = 0;
+  int32_t st = current_device_info(&dev, &device);
+  if (st != SF_OK) return st;
+  if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
+  const CUtensorMapDataType dt = tma_dtype(dtype);
+  const int kernel = attn_kernel();
+  const int rows = attn_unit_rows(kernel);
+  const uint32_t kb = static_cast<uint32_t>(attn_key_block(kernel));
+  CUtensorMap mq, mk, mv;
+  MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldq, head_dim, q_bstride,
+             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
+  MapSpec sk{k, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldk, head_dim, k_bstride,
+             static_cast<uint32_t>(head_dim), kb};
+  MapSpec sv{v, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
+             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldv, head_dim, v_bstride,
+             static_cast<uint32_t>(head_dim), kb};
+  if ((st = encode_map(&mq, sq)) != SF_OK) return st;
+  if ((st = encode_map(&mk, sk)) != SF_OK) return st;
+  if ((st = encode_map(&mv, sv)) != SF_OK) return st;
+  AttnArgs a;
+  a.q_len = q_len;
+  a.kv_len = kv_len;
+  a.heads = heads;
+  a.batch = batch;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.o = o;
+  a.out_dtype = dtype;
+  a.ldo = ldo;
+  a.o_bstride = o_bstride;
+  a.err = dev->err_word;
+  a.skip_lo = skip_lo;
+  a.skip_hi = skip_hi;
+  a.part_mode = part_mode;
+  a.part_o = part_o;
+  a.part_ml = part_ml;
+  a.split_first = -1;
+  a.split_k = 1;
+  a.nqb = static_cast<int>(ceil_div(q_len, rows));
+  a.ws_o = a.ws_ml = nullptr;
+  dim3 grid(static_cast<unsigned>(a.nqb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  AttnSplit sp;
+  if (part_mode != 1)
+    sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
+                         attn_ctas_per_sm(kernel) * dev->sm_count,
+                         static_cast<int>(ceil_div(kv_len, static_cast<int>(kb))));
+  // Held until the launches are queued, so that no other thread's call on the
+  // same stream regrows (frees) the workspace in between.
+  std::unique_lock<std::mutex> ws_lock(g_attn_ws_mu, std::defer_lock);
+  if (sp.split_first >= 0) {
+    const size_t need = static_cast<size_t>(sp.pieces) * rows * (kAttnD + 2) * sizeof(float);
+    ws_lock.lock();
+    const AttnWsKey key{device, stream, s == cudaStreamPerThread ? this_thread_tag() : 0};
+    AttnWorkspace& ws = g_attn_ws[key];
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    SF_CUDA_TRY(cudaStreamIsCapturing(s, &cap));
+    // No allocation while the stream is being captured: use the 3-D grid then.
+    if (ws.bytes < need && cap == cudaStreamCaptureStatusNone) {
+      attn_ws_drop(ws);
+      SF_CUDA_TRY(cudaMalloc(&ws.ptr, 2 * need));
+      ws.bytes = 2 * need;
+    }
+    if (ws.bytes >= need) {
+      if (cap != cudaStreamCaptureStatusNone) ws.captured = true;
+      a.split_first = sp.split_first;
+      a.split_k = sp.split_k;
+      a.ws_o = static_cast<float*>(ws.ptr);
+      a.ws_ml = a.ws_o + static_cast<size_t>(sp.pieces) * rows * kAttnD;
+      grid = dim3(static_cast<unsigned>(sp.split_first + sp.pieces), 1, 1);
+    }
+  }
+  st = dtype == kBF16 ? launch_kernel<true>(kernel, grid, mq, mk, mv, a, s, device)
+                      : launch_kernel<false>(kernel, grid, mq, mk, mv, a, s, device);
+  if (st != SF_OK) return st;
+  SF_CUDA_TRY(cudaGetLastError());
+  if (a.split_first >= 0) {
+    const unsigned n_split = static_cast<unsigned>(sp.pieces / sp.split_k);
+    if (dtype == kBF16)
+      launch_merge<true>(rows, n_split, a, s);
+    else
+      launch_merge<false>(rows, n_split, a, s);
+    SF_CUDA_TRY(cudaGetLastError());
+  }
+  return SF_OK;
+}
+
+}  // namespace
+
+void attention_release_stream(void* stream) {
+  std::lock_guard<std::mutex> lk(g_attn_ws_mu);
+  for (auto it = g_attn_ws.begin(); it != g_attn_ws.end();) {
+    if (it->first.stream == stream) {
+      attn_ws_drop(it->second);
+      it = g_attn_ws.erase(it);
+    } else {
+      ++it;
+    }
+  }
+}
+
+}  // namespace sf
+
+using namespace sf;
+
+// Number of kernel launches of sf_attention_fwd (part_mode 0) or
+// sf_attention_fwd_partial for these sizes on the current device (1, or 2
+// when the last wave is split and merged).
+extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len,
+                                             int32_t kv_len, int32_t part_mode, int32_t* count) {
+  if (!count) return fail(SF_ERR_INVALID_ARGUMENT, "null count");
+  *count = 0;
+  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0) return SF_OK;
+  DeviceInfo* dev = nullptr;
+  int32_t st = current_device_info(&dev, nullptr);
+  if (st != SF_OK) return st;
+  const int kernel = attn_kernel();
+  *count = 1;
+  if (part_mode != 1) {
+    const int64_t units = ceil_div(q_len, attn_unit_rows(kernel)) * heads * batch;
+    const AttnSplit sp = attn_split_plan(units, attn_ctas_per_sm(kernel) * dev->sm_count,
+                                         static_cast<int>(ceil_div(kv_len, attn_key_block(kernel))));
+    if (sp.split_first >= 0) *count = 2;
+  }
+  return SF_OK;
+}
+
+extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
+                                    int32_t head_dim, const void* q, int64_t ldq,
+                                    int64_t q_bstride, const void* k, int64_t ldk,
+                                    int64_t k_bstride, const void* v, int64_t ldv,
+                                    int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
+                                    float scale, int32_t dtype, void* stream) {
+  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
+                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, kv_len,
+                        kv_len, nullptr, nullptr, 0, stream);
+}
+
+extern "C" int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len,
+                                            int32_t kv_len, int32_t head_dim, const void* q,
+                                            int64_t ldq, int64_t q_bstride, const void* k,
+                                            int64_t ldk, int64_t k_bstride, const void* v,
+                                            int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
+                                            int64_t o_bstride, float scale, int32_t dtype,
+                                            int32_t skip_lo, int32_t skip_hi, float* part_o,
+                                            float* part_ml, int32_t part_mode, void* stream) {
+  if (part_mode < 0 || part_mode > 2)
+    return fail(SF_ERR_INVALID_ARGUMENT, "partial mode %d", part_mode);
+  if (skip_lo < 0 || skip_hi < skip_lo || skip_hi > kv_len)
+    return fail(SF_ERR_INVALID_ARGUMENT, "skipped keys [%d, %d) outside [0, %d]", skip_lo, skip_hi, kv_len);
+  if (part_mode != 0 && (!part_o || !part_ml || !aligned16(part_o) || (reinterpret_cast<uintptr_t>(part_ml) & 7u)))
+    return fail(SF_ERR_INVALID_ARGUMENT, "partial buffers missing or misaligned");
+  if (part_mode != 2 && skip_hi - skip_lo == kv_len && kv_len > 0)
+    return fail(SF_ERR_INVALID_ARGUMENT, "every key skipped");
+  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
+                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, skip_lo,
+                        skip_hi, part_o, part_ml, part_mode, stream);
+}

@@ -46,10 +46,6 @@ struct AttnArgs {
   int out_dtype;         // kBF16 / kF16
   int64_t ldo, o_bstride;  // elements
   int* err;
-  int sleep_ns;          // poll back-off of the softmax warps' waits (0 = spin)
-  // attention_fwd2_kernel: suspend-time hints (ns) of the producer / MMA
-  // waits and of the softmax waits (0 = poll without suspending).
-  uint32_t suspend_mma, suspend_smx;
   // attention_fwd2_kernel only: keys [skip_lo, skip_hi) are left out (none
   // when skip_lo == skip_hi == kv_len), and part_mode selects the output:
   //   0  normalised 16-bit O;
@@ -81,39 +77,6 @@ struct AttnArgs {
 constexpr int kAttnBlock = 128;   // queries per CTA and keys per block
 constexpr int kAttnD = 64;        // head dim
 constexpr int kAttnThreads = 192;
-
-// Configuration: KB keys per block; NS score buffers (TMEM), NP probability
-// tiles (shared memory), NO output buffers (TMEM), ST K/V ring stages.
-//   AttnCfg<128, 1, 1, 2, 2>  256 TMEM columns, ~113 KB: two CTAs per SM;
-//                             S_{j+1} waits for the softmax of block j.
-//   AttnCfg<96, 2, 1, 1, 2>   256 TMEM columns, ~97 KB: two CTAs per SM and
-//                             double-buffered scores, so S_{j+1} is computed
-//                             while block j's softmax runs (96-key blocks
-//                             keep 2 x 96 score + 64 output columns in 256).
-//   AttnCfg<128, 2, 2, 2, 4>  512 TMEM columns: one CTA per SM.
-template <int KB_, int NS_, int NP_, int NO_, int ST_>
-struct AttnCfg {
-  static constexpr int KB = KB_;
-  static constexpr int NS = NS_, NP = NP_, NO = NO_;
-  static constexpr int KV_STAGES = ST_;
-  static constexpr int TILE = kAttnBlock * 128;          // Q tile / P atom: 128 rows x 128 B
-  static constexpr int KV_TILE = KB * 128;               // K or V tile: KB rows x 128 B
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = TILE;                    // stage s: K at +2s*KV_TILE, V after it
-  static constexpr int P_OFF = KV_OFF + KV_STAGES * 2 * KV_TILE;  // NP tiles x 2 atoms
-  static constexpr int BAR_OFF = P_OFF + NP * 2 * TILE;         // mbarriers and flags
-  static constexpr int BYTES = BAR_OFF + 256;
-  static constexpr uint32_t O_COL = NS * KB;             // NO 64-column O buffers follow S
-  static constexpr uint32_t COLS_USED = NS * KB + NO * 64;
-  static constexpr uint32_t TMEM_COLS = COLS_USED <= 256 ? 256 : 512;
-  static constexpr int MIN_BLOCKS = TMEM_COLS <= 256 ? 2 : 1;
-  static constexpr int CHUNKS = KB / 32;
-  static_assert(KB % 32 == 0 && KB <= 128 && KB_ % 16 == 0, "key block");
-  static_assert(KV_TILE % 1024 == 0 && P_OFF % 1024 == 0, "1024-byte aligned tiles");
-  static_assert(COLS_USED <= 512, "TMEM budget");
-  static_assert(NP == 1 || NP == NS, "P tiles follow the score buffers");
-  static_assert((1 + 2 * KV_STAGES + 2 * NS + NP + 2 * NO + 2) * 8 <= 256, "barrier area");
-};
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -185,333 +148,6 @@ __device__ __forceinline__ uint32_t pack_16bit(float a, float b, bool bf16) {
   }
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// EMU of every four exp2 pairs of a full block go through exp2_poly2.
-template <bool BF16, class Cfg, int EMU>
-__global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
-    attention_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
-  // All shared memory is dynamic (no static part), declared 1024-byte
-  // aligned for the 128B-swizzled tiles; the mbarriers sit after the tiles.
-  extern __shared__ __align__(1024) uint8_t smem[];
-  constexpr int ST = Cfg::KV_STAGES, KB = Cfg::KB, NS = Cfg::NS, NP = Cfg::NP, NO = Cfg::NO;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
-  uint64_t& q_full = bars[0];
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + ST;
-  uint64_t* s_full = kv_empty + ST;
-  uint64_t* s_free = s_full + NS;
-  uint64_t* p_full = s_free + NS;
-  uint64_t* o_full = p_full + NP;
-  uint64_t* o_free = o_full + NO;
-  uint64_t& drain_bar = o_free[NO];
-  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&o_free[NO + 1]);
-  int& abort_flag = *(reinterpret_cast<int*>(&o_free[NO + 1]) + 1);
-  if ((smem_u32(smem) & 1023u) != 0) {
-    // The swizzled tile layout needs 1024-byte alignment; never guess.
-    if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadConfig);
-    return;
-  }
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int nblk = (p.kv_len + KB - 1) / KB;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&q_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-    }
-    for (int i = 0; i < NP; ++i) mbar_init(&p_full[i], 4);
-    for (int i = 0; i < NO; ++i) {
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 4);
-    }
-    mbar_init(&drain_bar, 1);
-    abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  if (warp == 1) {
-    tmem_alloc(&tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = tmem_slot;
-  volatile int* abortp = &abort_flag;
-  // TMEM columns: NS score buffers of KB columns, then NO 64-column O buffers.
-
-  if (warp == 0) {
-    // ───────────── TMA producer ─────────────
-    if (lane == 0) {
-      bool ok = true;
-      int issued = 0, stage = 0;
-      uint32_t phase = 0;
-      mbar_arrive_expect_tx(&q_full, Cfg::TILE);
-      tma_load_4d(smem + Cfg::Q_OFF, &tmQ, &q_full, 0, qb * kAttnBlock, h, b);
-      for (int j = 0; j < nblk; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
-          ok = false;
-          break;
-        }
-        uint8_t* kt = smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE;
-        mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::KV_TILE);
-        tma_load_4d(kt, &tmK, &kv_full[stage], 0, j * KB, h, b);
-        tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, j * KB, h, b);
-        ++issued;
-        if (++stage == ST) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      // Wait (bounded) for every copy this thread issued before the CTA may
-      // retire: on the normal path they have all been consumed already.
-      if (!mbar_wait_quiet(&q_full, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
-      if (!ok) {
-        const int n = issued < ST ? issued : ST;
-        int s = stage;
-        uint32_t ph = phase;
-        for (int i = 0; i < n; ++i) {
-          if (--s < 0) {
-            s = ST - 1;
-            ph ^= 1u;
-          }
-          if (!mbar_wait_quiet(&kv_full[s], ph, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ───────────── MMA issuer ─────────────
-    if (lane == 0) {
-      const uint32_t fmt = BF16 ? 1u : 0u;
-      const uint32_t idesc_s = make_idesc(fmt, 128, KB, 0u, 0u);   // K-major A and B
-      const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);   // P K-major, V MN-major
-      const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF);
-      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
-      bool issued_any = false;
-      int stage = 0;
-      uint32_t phase = 0;
-      int pv_stage = 0;
-      auto issue_pv = [&](int jj) -> bool {
-        const int pb = jj % NP;
-        const uint32_t ppar = (static_cast<uint32_t>(jj / NP)) & 1u;
-        const int ob = jj % NO;
-        const uint32_t opar = (static_cast<uint32_t>(jj / NO)) & 1u;
-        if (!mbar_wait(&p_full[pb], ppar, p.err, kDevTimeoutMma, abortp)) return false;
-        if (!mbar_wait(&o_free[ob], opar ^ 1u, p.err, kDevTimeoutMma, abortp)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + Cfg::P_OFF + pb * 2 * Cfg::TILE);
-        const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + pv_stage * 2 * Cfg::KV_TILE +
-                                         Cfg::KV_TILE);
-        const uint32_t d_tmem = tmem_base + Cfg::O_COL + static_cast<uint32_t>(ob * 64);
-#pragma unroll
-        for (int ks = 0; ks < KB / 16; ++ks) {
-          const uint64_t ad =
-              make_sw128_desc(p_addr + (ks >> 2) * Cfg::TILE + (ks & 3) * 32, 16, 1024);
-          const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, 8192, 1024);
-          umma_f16(d_tmem, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
-        }
-        umma_commit(&o_full[ob]);
-        umma_commit(&kv_empty[pv_stage]);  // K and V of this block are consumed
-        if (++pv_stage == ST) pv_stage = 0;
-        return true;
-      };
-      for (int j = 0; j < nblk && ok; ++j) {
-        const int buf = j % NS;
-        const uint32_t par = (static_cast<uint32_t>(j / NS)) & 1u;
-        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp) ||
-            !mbar_wait(&s_free[buf], par ^ 1u, p.err, kDevTimeoutMma, abortp)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE);
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * KB);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
-          const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
-          umma_f16(d_tmem, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
-        }
-        issued_any = true;
-        umma_commit(&s_full[buf]);
-        if (++stage == ST) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
-      }
-      if (ok && nblk > 0 && !issue_pv(nblk - 1)) ok = false;
-      if (!ok && issued_any) {
-        umma_commit(&drain_bar);
-        if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
-      }
-    }
-  } else {
-    // ───────────── softmax (warps 2..5): one thread per query row ─────────────
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    float o_acc[kAttnD];
-#pragma unroll
-    for (int t = 0; t < kAttnD; ++t) o_acc[t] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
-    const float c = p.scale_log2;
-    bool ok = true;
-    auto consume_o = [&](int jj, float alpha) -> bool {
-      const int buf = jj % NO;
-      const uint32_t par = (static_cast<uint32_t>(jj / NO)) & 1u;
-      if (!mbar_wait(&o_full[buf], par, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs,
-                     p.sleep_ns))
-        return false;
-      tc_fence_after();
-      uint32_t r[32];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem_base + lane_base + Cfg::O_COL + static_cast<uint32_t>(buf * 64 + half * 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int t = 0; t < 32; t += 2)
-          fma2(o_acc[half * 32 + t], o_acc[half * 32 + t + 1], o_acc[half * 32 + t],
-               o_acc[half * 32 + t + 1], alpha, alpha, __uint_as_float(r[t]),
-               __uint_as_float(r[t + 1]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[buf]);
-      return true;
-    };
-    for (int j = 0; j < nblk; ++j) {
-      const int buf = j % NS;
-      const uint32_t par = (static_cast<uint32_t>(j / NS)) & 1u;
-      if (!mbar_wait(&s_full[buf], par, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs,
-                     p.sleep_ns)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_addr = tmem_base + lane_base + static_cast<uint32_t>(buf * KB);
-      const int valid = min(KB, p.kv_len - j * KB);
-      // pass 1: row maximum of the (masked) scores; four independent chains
-      // of three-input max
-      const bool full = valid == KB;
-      float mxc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      uint32_t r[32];
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        tmem_ld32(s_addr + ch * 32, r);
-        tmem_ld_wait();
-        if (full) {
-#pragma unroll
-          for (int t = 0; t < 32; t += 2)
-            mxc[(t >> 1) & 3] = max3f(mxc[(t >> 1) & 3], __uint_as_float(r[t]), __uint_as_float(r[t + 1]));
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (ch * 32 + t < valid) mxc[0] = fmaxf(mxc[0], __uint_as_float(r[t]));
-        }
-      }
-      const float mx = max3f(mxc[0], mxc[1], fmaxf(mxc[2], mxc[3]));
-      const float m_new = fmaxf(m_run, mx * c);
-      const float alpha = ex2_approx(m_run - m_new);  // 0 on the first block
-      // Fold O_{j-1} (its P.V has then also released P tile (j-1) % NP,
-      // which is this block's tile when NP = 1, and O buffer (j-1) % NO).
-      if (j >= 1 && !consume_o(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      // pass 2: P = exp2(c*s - m_new) as 16-bit into the swizzled A tile
-      const int pbuf = j % NP;
-      uint8_t* pbase = smem + Cfg::P_OFF + pbuf * 2 * Cfg::TILE;
-      float sp[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // two packed partial-sum pairs
-      const float nm = -m_new;
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        tmem_ld32(s_addr + ch * 32, r);
-        tmem_ld_wait();
-        float pv[32];
-        if (full) {
-#pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            float x0, x1;
-            fma2(x0, x1, __uint_as_float(r[t]), __uint_as_float(r[t + 1]), c, c, nm, nm);
-            if (((t >> 1) & 3) < EMU) {
-              exp2_poly2(pv[t], pv[t + 1], x0, x1);
-            } else {
-              pv[t] = ex2_approx(x0);
-              pv[t + 1] = ex2_approx(x1);
-            }
-            add2(sp[(t >> 1) & 2], sp[((t >> 1) & 2) + 1], pv[t], pv[t + 1]);
-          }
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const float e = ex2_approx(fmaf(__uint_as_float(r[t]), c, nm));
-            pv[t] = ch * 32 + t < valid ? e : 0.0f;
-            sp[t & 3] += pv[t];
-          }
-        }
-        // keys [ch*32, ch*32+32): atom ch/2, 16-byte chunks (ch%2)*4 .. +3
-        uint8_t* rowp = pbase + (ch >> 1) * Cfg::TILE + row * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = (ch & 1) * 4 + q;
-          *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
-              make_uint4(pack_16bit(pv[8 * q], pv[8 * q + 1], BF16),
-                         pack_16bit(pv[8 * q + 2], pv[8 * q + 3], BF16),
-                         pack_16bit(pv[8 * q + 4], pv[8 * q + 5], BF16),
-                         pack_16bit(pv[8 * q + 6], pv[8 * q + 7], BF16));
-        }
-      }
-      const float sum = (sp[0] + sp[1]) + (sp[2] + sp[3]);
-      l_run = fmaf(l_run, alpha, sum);
-      m_run = m_new;
-      tc_fence_before();
-      fence_proxy_async_smem();  // P writes -> tensor-core (async proxy) reads
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[buf]);
-        mbar_arrive(&p_full[pbuf]);
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && nblk > 0) ok = consume_o(nblk - 1, alpha_prev);
-    const int qrow = qb * kAttnBlock + row;
-    if (ok && qrow < p.q_len) {
-      const float inv = 1.0f / l_run;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
-                     (static_cast<int64_t>(b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
-                      static_cast<int64_t>(h) * kAttnD) * 2;
-#pragma unroll
-      for (int q = 0; q < kAttnD / 8; ++q)
-        reinterpret_cast<uint4*>(dst)[q] =
-            make_uint4(pack_16bit(o_acc[8 * q] * inv, o_acc[8 * q + 1] * inv, BF16),
-                       pack_16bit(o_acc[8 * q + 2] * inv, o_acc[8 * q + 3] * inv, BF16),
-                       pack_16bit(o_acc[8 * q + 4] * inv, o_acc[8 * q + 5] * inv, BF16),
-                       pack_16bit(o_acc[8 * q + 6] * inv, o_acc[8 * q + 7] * inv, BF16));
-    }
-  }
-
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
-  }
 }
 
 // ─────────────── second kernel: O in TMEM, lazily rescaled integer bases ───────────────
@@ -691,8 +327,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       mbar_arrive_expect_tx(&q_full, Cfg::TILE);
       tma_load_4d(smem + Cfg::Q_OFF, &tmQ, &q_full, 0, desc[kQb] * kAttnBlock, h, b);
       for (int j = 0; j < nblk; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp,
-                       kWaitLimitNs, 0, p.suspend_mma)) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
           ok = false;
           break;
         }
@@ -728,13 +363,13 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);
       const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF);
       const uint32_t p_addr = smem_u32(smem + Cfg::P_OFF);
-      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp, kWaitLimitNs, 0, p.suspend_mma);
+      bool ok = mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
       bool issued_any = false;
       int stage = 0, pv_stage = 0;
       uint32_t phase = 0;
       auto issue_pv = [&](int jj) -> bool {
         if (!mbar_wait(&p_full[jj % NS], static_cast<uint32_t>(jj / NS) & 1u, p.err, kDevTimeoutMma,
-                       abortp, kWaitLimitNs, 0, p.suspend_mma))
+                       abortp))
           return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + pv_stage * 2 * Cfg::KV_TILE +
@@ -758,8 +393,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         return true;
       };
       for (int j = 0; j < nblk && ok; ++j) {
-        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp, kWaitLimitNs, 0,
-                       p.suspend_mma)) {
+        if (!mbar_wait(&kv_full[stage], phase, p.err, kDevTimeoutMma, abortp)) {
           ok = false;
           break;
         }
@@ -770,7 +404,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
             break;
           }
         } else if (!mbar_wait(&s_free, (static_cast<uint32_t>(j) & 1u) ^ 1u, p.err, kDevTimeoutMma,
-                              abortp, kWaitLimitNs, 0, p.suspend_mma)) {
+                              abortp)) {
           ok = false;
           break;
         }
@@ -827,7 +461,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
       // Waits end the loop for the whole warp together: the TMEM loads and
       // stores that follow are warp-collective.
       if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j % NS], static_cast<uint32_t>(j / NS) & 1u,
-                                             p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
+                                             p.err, kDevTimeoutEpilogue, abortp))) {
         ok = false;
         break;
       }
@@ -860,7 +494,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         // block overwrites, and its sum is in the O rows a rescale touches.
         if (j >= 1) {
           if (!__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
-                                                 kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
+                                                 kDevTimeoutEpilogue, abortp))) {
             ok = false;
             break;
           }
@@ -934,7 +568,7 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
         if (rescale) {
           if (NS == 2 &&
               !__all_sync(0xffffffffu, mbar_wait(&o_full, static_cast<uint32_t>(j - 1) & 1u, p.err,
-                                                 kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx))) {
+                                                 kDevTimeoutEpilogue, abortp))) {
             ok = false;
             break;
           }
@@ -954,9 +588,9 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
     // With P in TMEM the last P.V alone signals o_last.
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu,
-                      Cfg::PT ? mbar_wait(&o_last, 0u, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx)
+                      Cfg::PT ? mbar_wait(&o_last, 0u, p.err, kDevTimeoutEpilogue, abortp)
                               : mbar_wait(&o_full, static_cast<uint32_t>(nblk - 1) & 1u, p.err,
-                                          kDevTimeoutEpilogue, abortp, kWaitLimitNs, 0, p.suspend_smx));
+                                          kDevTimeoutEpilogue, abortp));
     const int qrow = desc[kQb] * kAttnBlock + row;
     if (ok) {
       tc_fence_after();
@@ -1036,25 +670,26 @@ __global__ void __launch_bounds__(kAttnThreads, Cfg::MIN_BLOCKS)
 }
 
 // Combines the split_k pieces of each split unit, and in part_mode 2 the
-// partial result in part_o / part_ml (one CTA per unit, one thread per query
-// row): with integer bases m_p, m = max m_p,
+// partial result in part_o / part_ml (one CTA per unit of ROWS query rows,
+// one thread per row): with integer bases m_p, m = max m_p,
 // O = sum 2^(m_p - m) O_p / sum 2^(m_p - m) l_p, written as 16-bit O.
-template <bool BF16>
-__global__ void __launch_bounds__(kAttnBlock) attention_merge_kernel(const AttnArgs p) {
+// Workspace slot s holds ws_o[s][ROWS][64] and ws_ml[s][ROWS][2].
+template <bool BF16, int ROWS>
+__global__ void __launch_bounds__(ROWS) attention_merge_kernel(const AttnArgs p) {
   const int u = p.split_first + static_cast<int>(blockIdx.x);
   const int qb = u % p.nqb, h = (u / p.nqb) % p.heads, b = u / (p.nqb * p.heads);
   const int row = threadIdx.x;
-  const int qrow = qb * kAttnBlock + row;
+  const int qrow = qb * ROWS + row;
   if (qrow >= p.q_len) return;
   const int64_t slot0 = static_cast<int64_t>(blockIdx.x) * p.split_k;
   const int64_t prow = (static_cast<int64_t>(b) * p.q_len + qrow) * p.heads + h;
   const int n_in = p.split_k + (p.part_mode == 2 ? 1 : 0);
   // input i < split_k: workspace slot slot0 + i; i == split_k: the partial result
   auto ml_of = [&](int i) -> const float* {
-    return i < p.split_k ? p.ws_ml + ((slot0 + i) * kAttnBlock + row) * 2 : p.part_ml + 2 * prow;
+    return i < p.split_k ? p.ws_ml + ((slot0 + i) * ROWS + row) * 2 : p.part_ml + 2 * prow;
   };
   auto o_of = [&](int i) -> const float* {
-    return i < p.split_k ? p.ws_o + ((slot0 + i) * kAttnBlock + row) * kAttnD
+    return i < p.split_k ? p.ws_o + ((slot0 + i) * ROWS + row) * kAttnD
                          : p.part_o + prow * kAttnD;
   };
   float m = -INFINITY;

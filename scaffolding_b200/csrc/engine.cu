@@ -23,84 +23,18 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <vector>
 
 #include "common.h"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "gemv.cuh"
-#include "attention.cuh"
 #include "rowwise.cuh"
+#include "tma_host.h"
 
 namespace sf {
 
-// ───────────────────────────── TMA descriptors ─────────────────────────────
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-    else
-      cudaGetLastError();
-  });
-  return fn;
-}
-
-// 4-D view: element (i0, i1, i2, i3) at base + i1*s1 + i2*s2 + i3*s3 (elements),
-// i0 contiguous.  Extent-1 batch dims get a packed stride.
-struct MapSpec {
-  const void* base;
-  int esize;
-  CUtensorMapDataType dt;
-  uint64_t d0, d1, d2, d3;
-  int64_t s1, s2, s3;
-  uint32_t box0, box1;
-};
-
-static int32_t encode_map(CUtensorMap* m, const MapSpec& s) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(SF_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
-  const uint64_t e = static_cast<uint64_t>(s.esize);
-  uint64_t st1 = static_cast<uint64_t>(s.s1) * e;
-  uint64_t st2 = s.d2 > 1 ? static_cast<uint64_t>(s.s2) * e : st1 * s.d1;
-  uint64_t st3 = s.d3 > 1 ? static_cast<uint64_t>(s.s3) * e : st2 * s.d2;
-  st2 = (st2 + 15) & ~15ull;
-  st3 = (st3 + 15) & ~15ull;
-  cuuint64_t dims[4] = {s.d0, s.d1, s.d2, s.d3};
-  cuuint64_t strides[3] = {st1, st2, st3};
-  cuuint32_t box[4] = {s.box0, s.box1, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(m, s.dt, 4, const_cast<void*>(s.base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(SF_ERR_CUDA,
-                "cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu,%llu} strides "
-                "{%llu,%llu,%llu} box {%u,%u}",
-                static_cast<int>(r), (unsigned long long)s.d0, (unsigned long long)s.d1,
-                (unsigned long long)s.d2, (unsigned long long)s.d3, (unsigned long long)st1,
-                (unsigned long long)st2, (unsigned long long)st3, s.box0, s.box1);
-  return SF_OK;
-}
-
-static CUtensorMapDataType tma_dtype(int dt) {
-  return dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-         : dt == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-}
-
-static int esize(int dt) { return dt == kF32 ? 4 : 2; }
 
 // ───────────────────────────── problem / plan ─────────────────────────────
 
@@ -138,9 +72,6 @@ struct Plan {
   size_t ws_bytes = 0;
 };
 
-static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-static bool bytes16(int64_t elems, int es) { return ((elems * es) & 15) == 0; }
-static int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 static int pick_bn(int64_t n) {
   if (n <= 16) return 16;
@@ -176,10 +107,6 @@ static int pick_bn_pair_skinny(int64_t n, int clusters) {
 // Reduction length from which narrow 16-bit GEMMs promote their accumulators.
 constexpr int64_t kPromoteMinK = 8192;
 
-static int env_int(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return (v && *v) ? atoi(v) : dflt;
-}
 
 // `have_ptrs` = false when only sizing the workspace (pointers unknown, assumed aligned).
 static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
@@ -1025,335 +952,3 @@ int32_t sf_fill_normal(void* x, int32_t dtype, int64_t n, uint64_t seed, float m
 }
 
 }  // extern "C"
-
-// ───────────────────────────── fused attention ─────────────────────────────
-
-// Fused-attention configurations (see AttnCfg): variant 1 = 128-key blocks,
-// single-buffered scores, two CTAs per SM; 2 = 128-key blocks,
-// double-buffered, one CTA per SM; 3 = 96-key blocks, double-buffered
-// scores, two CTAs per SM.
-using AttnCfgV1 = AttnCfg<128, 1, 1, 2, 2>;
-using AttnCfgV2 = AttnCfg<128, 2, 2, 2, 4>;
-using AttnCfgV3 = AttnCfg<96, 2, 1, 1, 2>;
-// attention_fwd2_kernel (O in TMEM, lazily rescaled integer bases): variant 4 =
-// 64-key blocks, three CTAs per SM; 5 = 128-key blocks, two CTAs per SM;
-// 6 = 64-key blocks with P in TMEM, four CTAs per SM; 7 = 32-key blocks with
-// P in TMEM and two score buffers, four CTAs per SM.
-using Attn2CfgV4 = Attn2Cfg<64, 2>;
-using Attn2CfgV5 = Attn2Cfg<128, 2>;
-using Attn2CfgV6 = Attn2Cfg<64, 2, true>;
-using Attn2CfgV7 = Attn2Cfg<32, 4, true>;
-
-template <bool BF16, class Cfg, int EMU>
-static int32_t launch_attention2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                                 const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
-                                 int device) {
-  static bool attr_set[64] = {false};
-  if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Cfg, EMU>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
-    attr_set[device] = true;
-  }
-  attention_fwd2_kernel<BF16, Cfg, EMU><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
-  return SF_OK;
-}
-
-template <bool BF16, class Cfg>
-static int32_t launch_attention2_emu(int emu, const dim3& grid, const CUtensorMap& mq,
-                                     const CUtensorMap& mk, const CUtensorMap& mv,
-                                     const AttnArgs& a, cudaStream_t s, int device) {
-  switch (emu) {
-    case 1: return launch_attention2<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
-    case 2: return launch_attention2<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
-    default: return launch_attention2<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
-  }
-}
-
-template <bool BF16, class Cfg, int EMU>
-static int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                                const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
-                                int device) {
-  static bool attr_set[64] = {false};
-  if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd_kernel<BF16, Cfg, EMU>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
-    attr_set[device] = true;
-  }
-  attention_fwd_kernel<BF16, Cfg, EMU><<<grid, kAttnThreads, Cfg::BYTES, s>>>(mq, mk, mv, a);
-  return SF_OK;
-}
-
-template <bool BF16, class Cfg>
-static int32_t launch_attention_emu(int emu, const dim3& grid, const CUtensorMap& mq,
-                                    const CUtensorMap& mk, const CUtensorMap& mv,
-                                    const AttnArgs& a, cudaStream_t s, int device) {
-  switch (emu) {
-    case 0: return launch_attention<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
-    case 1: return launch_attention<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
-    case 3: return launch_attention<BF16, Cfg, 3>(grid, mq, mk, mv, a, s, device);
-    default: return launch_attention<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
-  }
-}
-
-template <bool BF16>
-static int32_t launch_attention_variant(int variant, int emu, const dim3& grid,
-                                        const CUtensorMap& mq, const CUtensorMap& mk,
-                                        const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s,
-                                        int device) {
-  switch (variant) {
-    case 4: return launch_attention2_emu<BF16, Attn2CfgV4>(emu, grid, mq, mk, mv, a, s, device);
-    case 5: return launch_attention2_emu<BF16, Attn2CfgV5>(emu, grid, mq, mk, mv, a, s, device);
-    case 6: return launch_attention2_emu<BF16, Attn2CfgV6>(emu, grid, mq, mk, mv, a, s, device);
-    case 7: return launch_attention2_emu<BF16, Attn2CfgV7>(emu, grid, mq, mk, mv, a, s, device);
-    case 2: return launch_attention<BF16, AttnCfgV2, 0>(grid, mq, mk, mv, a, s, device);
-    case 3: return launch_attention_emu<BF16, AttnCfgV3>(emu, grid, mq, mk, mv, a, s, device);
-    default: return launch_attention_emu<BF16, AttnCfgV1>(emu, grid, mq, mk, mv, a, s, device);
-  }
-}
-
-static int attn_key_block(int variant) {
-  switch (variant) {
-    case 2: return AttnCfgV2::KB;
-    case 3: return AttnCfgV3::KB;
-    case 4: return Attn2CfgV4::KB;
-    case 5: return Attn2CfgV5::KB;
-    case 6: return Attn2CfgV6::KB;
-    case 7: return Attn2CfgV7::KB;
-    default: return AttnCfgV1::KB;
-  }
-}
-
-static int attn_ctas_per_sm(int variant) {
-  switch (variant) {
-    case 2: return AttnCfgV2::MIN_BLOCKS;
-    case 3: return AttnCfgV3::MIN_BLOCKS;
-    case 4: return Attn2CfgV4::MIN_BLOCKS;
-    case 5: return Attn2CfgV5::MIN_BLOCKS;
-    case 6: return Attn2CfgV6::MIN_BLOCKS;
-    case 7: return Attn2CfgV7::MIN_BLOCKS;
-    default: return AttnCfgV1::MIN_BLOCKS;
-  }
-}
-
-static int attn_variant() { return env_int("SF_ATTN_VARIANT", 6); }  // tuning knob
-
-// Split dispatch plan (see AttnArgs::split_first).  U units on P resident
-// CTA slots take ceil(U / P) unit times; splitting the R = U mod P units of
-// the last wave into k key-range pieces takes floor(U / P) + ceil(R k / P) / k.
-// k in [2, min(32, key blocks)] minimises that; the split is used when it
-// saves more than 3 %.
-struct AttnSplit {
-  int split_first = -1, split_k = 1, pieces = 0;
-};
-static AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
-  AttnSplit sp;
-  if (env_int("SF_ATTN_SPLIT", 1) == 0 || slots <= 0 || nkb < 2) return sp;  // tuning knob
-  const int64_t full = units / slots, rem = units % slots;
-  if (rem == 0) return sp;
-  double best = 1.0;
-  int best_k = 1;
-  for (int k = 2; k <= std::min(32, nkb); ++k) {
-    const double t = static_cast<double>((rem * k + slots - 1) / slots) / k;
-    if (t < best - 1e-9) {
-      best = t;
-      best_k = k;
-    }
-  }
-  if (best_k == 1 || full + best > 0.97 * static_cast<double>(full + 1)) return sp;
-  sp.split_first = static_cast<int>(units - rem);
-  sp.split_k = best_k;
-  sp.pieces = static_cast<int>(rem) * best_k;
-  return sp;
-}
-
-// Workspace of the split pieces, one per (device, stream) so that calls on
-// different streams never share it (grown on demand, never shrunk; calls on
-// one stream run in order).
-struct AttnWorkspace {
-  void* ptr = nullptr;
-  size_t bytes = 0;
-};
-static std::mutex g_attn_ws_mu;
-static std::map<std::pair<int, void*>, AttnWorkspace> g_attn_ws;
-
-static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
-                              int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
-                              const void* k, int64_t ldk, int64_t k_bstride, const void* v,
-                              int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
-                              int64_t o_bstride, float scale, int32_t dtype, int32_t skip_lo,
-                              int32_t skip_hi, float* part_o, float* part_ml, int32_t part_mode,
-                              void* stream);
-
-// Number of kernel launches of sf_attention_fwd (part_mode 0) or
-// sf_attention_fwd_partial for these sizes on the current device (1, or 2
-// when the last wave is split and merged).
-extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len,
-                                             int32_t kv_len, int32_t part_mode, int32_t* count) {
-  if (!count) return fail(SF_ERR_INVALID_ARGUMENT, "null count");
-  *count = 0;
-  if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0) return SF_OK;
-  DeviceInfo* dev = nullptr;
-  int32_t st = current_device_info(&dev, nullptr);
-  if (st != SF_OK) return st;
-  const int variant = attn_variant();
-  *count = 1;
-  if (variant >= 4 && variant <= 7 && part_mode != 1) {
-    const int64_t units = static_cast<int64_t>(ceil_div(q_len, kAttnBlock)) * heads * batch;
-    const AttnSplit sp = attn_split_plan(units, attn_ctas_per_sm(variant) * dev->sm_count,
-                                         ceil_div(kv_len, attn_key_block(variant)));
-    if (sp.split_first >= 0) *count = 2;
-  }
-  return SF_OK;
-}
-
-extern "C" int32_t sf_attention_fwd(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
-                                    int32_t head_dim, const void* q, int64_t ldq,
-                                    int64_t q_bstride, const void* k, int64_t ldk,
-                                    int64_t k_bstride, const void* v, int64_t ldv,
-                                    int64_t v_bstride, void* o, int64_t ldo, int64_t o_bstride,
-                                    float scale, int32_t dtype, void* stream) {
-  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
-                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, kv_len,
-                        kv_len, nullptr, nullptr, 0, stream);
-}
-
-extern "C" int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len,
-                                            int32_t kv_len, int32_t head_dim, const void* q,
-                                            int64_t ldq, int64_t q_bstride, const void* k,
-                                            int64_t ldk, int64_t k_bstride, const void* v,
-                                            int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
-                                            int64_t o_bstride, float scale, int32_t dtype,
-                                            int32_t skip_lo, int32_t skip_hi, float* part_o,
-                                            float* part_ml, int32_t part_mode, void* stream) {
-  if (part_mode < 0 || part_mode > 2)
-    return fail(SF_ERR_INVALID_ARGUMENT, "partial mode %d", part_mode);
-  if (skip_lo < 0 || skip_hi < skip_lo || skip_hi > kv_len)
-    return fail(SF_ERR_INVALID_ARGUMENT, "skipped keys [%d, %d) outside [0, %d]", skip_lo, skip_hi, kv_len);
-  if (part_mode != 0 && (!part_o || !part_ml || !aligned16(part_o) || (reinterpret_cast<uintptr_t>(part_ml) & 7u)))
-    return fail(SF_ERR_INVALID_ARGUMENT, "partial buffers missing or misaligned");
-  if (part_mode != 2 && skip_hi - skip_lo == kv_len && kv_len > 0)
-    return fail(SF_ERR_INVALID_ARGUMENT, "every key skipped");
-  return attention_impl(batch, heads, q_len, kv_len, head_dim, q, ldq, q_bstride, k, ldk,
-                        k_bstride, v, ldv, v_bstride, o, ldo, o_bstride, scale, dtype, skip_lo,
-                        skip_hi, part_o, part_ml, part_mode, stream);
-}
-
-static int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
-                              int32_t head_dim, const void* q, int64_t ldq, int64_t q_bstride,
-                              const void* k, int64_t ldk, int64_t k_bstride, const void* v,
-                              int64_t ldv, int64_t v_bstride, void* o, int64_t ldo,
-                              int64_t o_bstride, float scale, int32_t dtype, int32_t skip_lo,
-                              int32_t skip_hi, float* part_o, float* part_ml, int32_t part_mode,
-                              void* stream) {
-  if (batch < 0 || heads < 0 || q_len < 0 || kv_len < 0)
-    return fail(SF_ERR_INVALID_ARGUMENT, "negative size");
-  if (batch == 0 || heads == 0 || q_len == 0) return SF_OK;
-  if (kv_len == 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention over zero keys");
-  if (head_dim != kAttnD) return fail(SF_ERR_UNSUPPORTED, "fused attention needs head_dim 64 (got %d)", head_dim);
-  if (dtype != kBF16 && dtype != kF16) return fail(SF_ERR_INVALID_ARGUMENT, "fused attention dtype %d", dtype);
-  if (!q || !k || !v || !o) return fail(SF_ERR_INVALID_ARGUMENT, "null pointer");
-  for (const void* ptr : {q, k, v, static_cast<const void*>(o)})
-    if (!aligned16(ptr)) return fail(SF_ERR_INVALID_ARGUMENT, "attention operands must be 16-byte aligned");
-  for (int64_t st : {ldq, ldk, ldv, ldo, q_bstride, k_bstride, v_bstride, o_bstride})
-    if (!bytes16(st, 2) || st < 0) return fail(SF_ERR_INVALID_ARGUMENT, "attention strides must be 16-byte multiples");
-  const int64_t row_min = static_cast<int64_t>(heads) * head_dim;
-  if (ldq < row_min || ldk < row_min || ldv < row_min || ldo < row_min)
-    return fail(SF_ERR_INVALID_ARGUMENT, "leading dimension < heads * head_dim");
-  if (heads > 65535 || batch > 65535) return fail(SF_ERR_UNSUPPORTED, "attention grid");
-  DeviceInfo* dev = nullptr;
-  int device = 0;
-  int32_t st = current_device_info(&dev, &device);
-  if (st != SF_OK) return st;
-  if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
-  const CUtensorMapDataType dt = tma_dtype(dtype);
-  const int variant = attn_variant();  // see AttnCfgV1..V3, Attn2CfgV4..V7
-  if ((part_mode != 0 || skip_lo != kv_len || skip_hi != kv_len) && (variant < 4 || variant > 7))
-    return fail(SF_ERR_UNSUPPORTED, "partial attention needs the TMEM-accumulator kernel (variants 4-7)");
-  const uint32_t kb = static_cast<uint32_t>(attn_key_block(variant));
-  CUtensorMap mq, mk, mv;
-  MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
-             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldq, head_dim, q_bstride,
-             static_cast<uint32_t>(head_dim), static_cast<uint32_t>(kAttnBlock)};
-  MapSpec sk{k, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
-             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldk, head_dim, k_bstride,
-             static_cast<uint32_t>(head_dim), kb};
-  MapSpec sv{v, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(kv_len),
-             static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldv, head_dim, v_bstride,
-             static_cast<uint32_t>(head_dim), kb};
-  if ((st = encode_map(&mq, sq)) != SF_OK) return st;
-  if ((st = encode_map(&mk, sk)) != SF_OK) return st;
-  if ((st = encode_map(&mv, sv)) != SF_OK) return st;
-  AttnArgs a;
-  a.q_len = q_len;
-  a.kv_len = kv_len;
-  a.heads = heads;
-  a.batch = batch;
-  a.scale_log2 = scale * 1.4426950408889634f;
-  a.o = o;
-  a.out_dtype = dtype;
-  a.ldo = ldo;
-  a.o_bstride = o_bstride;
-  a.err = dev->err_word;
-  a.sleep_ns = env_int("SF_ATTN_SLEEP", 0);  // tuning knob
-  // Suspend-time hints of the TMEM-accumulator kernel's waits (tuning knobs).
-  a.suspend_mma = static_cast<uint32_t>(env_int("SF_ATTN_SUSPEND_MMA", 0));
-  a.suspend_smx = static_cast<uint32_t>(env_int("SF_ATTN_SUSPEND_SMX", 0));
-  a.skip_lo = skip_lo;
-  a.skip_hi = skip_hi;
-  a.part_mode = part_mode;
-  a.part_o = part_o;
-  a.part_ml = part_ml;
-  a.split_first = -1;
-  a.split_k = 1;
-  a.nqb = ceil_div(q_len, kAttnBlock);
-  a.ws_o = a.ws_ml = nullptr;
-  dim3 grid(static_cast<unsigned>(a.nqb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  AttnSplit sp;
-  if (variant >= 4 && variant <= 7 && part_mode != 1)
-    sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
-                         attn_ctas_per_sm(variant) * dev->sm_count, ceil_div(kv_len, static_cast<int>(kb)));
-  // Held until the launches are queued, so that no other thread's call on the
-  // same stream regrows (frees) the workspace in between.
-  std::unique_lock<std::mutex> ws_lock(g_attn_ws_mu, std::defer_lock);
-  if (sp.split_first >= 0) {
-    const size_t need = static_cast<size_t>(sp.pieces) * kAttnBlock * (kAttnD + 2) * sizeof(float);
-    ws_lock.lock();
-    AttnWorkspace& ws = g_attn_ws[std::make_pair(device, stream)];
-    if (ws.bytes < need) {
-      // No allocation while the stream is being captured: use the 3-D grid then.
-      cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-      SF_CUDA_TRY(cudaStreamIsCapturing(s, &cap));
-      if (cap == cudaStreamCaptureStatusNone) {
-        if (ws.ptr) SF_CUDA_TRY(cudaFree(ws.ptr));
-        ws.ptr = nullptr;
-        ws.bytes = 0;
-        SF_CUDA_TRY(cudaMalloc(&ws.ptr, need));
-        ws.bytes = need;
-      }
-    }
-    if (ws.bytes >= need) {
-      a.split_first = sp.split_first;
-      a.split_k = sp.split_k;
-      a.ws_o = static_cast<float*>(ws.ptr);
-      a.ws_ml = a.ws_o + static_cast<size_t>(sp.pieces) * kAttnBlock * kAttnD;
-      grid = dim3(static_cast<unsigned>(sp.split_first + sp.pieces), 1, 1);
-    }
-  }
-  // Share of the exp2 pairs computed on the FMA pipe, in quarters (tuning knob).
-  const int emu = env_int("SF_ATTN_EMU", 0);
-  st = dtype == kBF16
-           ? launch_attention_variant<true>(variant, emu, grid, mq, mk, mv, a, s, device)
-           : launch_attention_variant<false>(variant, emu, grid, mq, mk, mv, a, s, device);
-  if (st != SF_OK) return st;
-  SF_CUDA_TRY(cudaGetLastError());
-  if (a.split_first >= 0) {
-    const unsigned n_split = static_cast<unsigned>(sp.pieces / sp.split_k);
-    if (dtype == kBF16)
-      attention_merge_kernel<true><<<n_split, kAttnBlock, 0, s>>>(a);
-    else
-      attention_merge_kernel<false><<<n_split, kAttnBlock, 0, s>>>(a);
-    SF_CUDA_TRY(cudaGetLastError());
-  }
-  return SF_OK;
-}

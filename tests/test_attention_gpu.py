@@ -42,25 +42,22 @@ def test_sdpa_fp32_golden(gpu, ops, golden):
     assert_close_fp32(o, golden["sdpa_o"], "sdpa fp32")
 
 
-def _sdpa_p_rounded(q, k, v, scale):
-    """Oracle SDPA with the probabilities rounded to bf16, the storage type
-    the device keeps P in before the P.V product (its bf16 operand)."""
-    s = O.batched_matmul_nt(q, k) * np.float32(scale)
-    p = O.round_bf16(O.softmax_rows(s))
-    return O.batched_matmul(p, v)
-
-
 def test_sdpa_bf16_golden(gpu, ops, golden):
-    """bf16 SDPA.  Per-element bar (1e-2) against the oracle on identically
-    rounded GEMM operands (Q, K, V and the stored bf16 P); against the
-    reference's fp32-P output the bf16 rounding of P is visible on outputs
-    that cancel to ~0, so that comparison uses the aggregate bar."""
+    """bf16 SDPA (head_dim 64: the fused kernel).  Per-element bar (1e-2) per
+    (batch, head) against the oracle restating the fused kernel's blockwise
+    softmax on identically rounded Q, K, V (with its rounding-flip allowance);
+    against the reference's fp32-P output the bf16 rounding of P is visible
+    on outputs that cancel to ~0, so that comparison uses the aggregate bar."""
     from scaffolding_b200.nn import functional as F
     bf = np_dtype("bf16")
     qh, kh, vh = (golden[f"sdpa8_{s}"] for s in "qkv")
     q, k, v = (ops.gputensor_from_numpy(t.astype(bf)) for t in (qh, kh, vh))
     o = to_host32(ops, F.scaled_dot_product_attention(q, k, v, scale=0.125))
-    assert_close_16bit(o, _sdpa_p_rounded(qh, kh, vh, 0.125), "sdpa bf16 vs P-rounded oracle")
+    for idx in np.ndindex(*qh.shape[:-2]):
+        ref, allow = O.flash_attention(qh[idx], kh[idx], vh[idx], 0.125, return_allowance=True,
+                                       **attn_oracle_opts())
+        p = O.softmax_rows((qh[idx] @ kh[idx].T * np.float32(0.125)).astype(np.float32))
+        _check_attn(o[idx], ref, O.abs_product(p, vh[idx].T), allow, f"sdpa bf16 {idx}")
     assert O.rel_frobenius(o, golden["sdpa8_o"]) < 1e-2
 
 
@@ -82,9 +79,7 @@ def test_dev_muls_silu_gelu(gpu, ops, golden):
 # midpoint; flash_attention's allowance adds, per output, the change such a
 # flip could cause for every p within 2^-12 of a midpoint.
 def _check_attn(out, ref, absprod, allowance, what):
-    ok, st = O.elementwise_rel_check(out, ref, rtol=1e-2, tau=1e-2, absprod=absprod,
-                                     kappa=1e-2, allowance=allowance)
-    assert ok, f"{what}: {st}"
+    assert_close_16bit(out, ref, what, absprod=absprod, allowance=allowance)
 
 
 def _fused(ops, batch, heads, q_len, kv_len, q, k, v, ldq, ldk, ldv, q_bs, k_bs, v_bs, scale,
@@ -152,20 +147,23 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
 
 
 @pytest.mark.parametrize("split", ["1", "0"])
-@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 6, 7])
-def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant, split):
-    """Each fused-attention configuration (SF_ATTN_VARIANT) on a ragged case
-    with q_len != kv_len and large logits, against the oracle restating that
-    configuration's key block and row bases; with the split last wave (key
-    pieces merged by a second kernel; variants 4-7 at these sizes) and with
-    the one-CTA-per-query-block grid (SF_ATTN_SPLIT=0)."""
+@pytest.mark.parametrize("kernel,emu", [(2, 0), (3, 0), (3, 2), (4, 0), (4, 1), (4, 2), (4, 3),
+                                        (5, 0), (5, 2)])
+def test_fused_attention_every_kernel(gpu, ops, monkeypatch, kernel, emu, split):
+    """Each fused-attention kernel (SF_ATTN_KERNEL; for the two-tile kernel
+    each share of exp2 pairs computed on the FMA pipe, SF_ATTN_EMU) on a
+    ragged case with q_len != kv_len and large logits, against the oracle
+    restating that kernel's key block and row bases; with the split last wave
+    (key pieces merged by a second kernel) and with one CTA per query unit
+    (SF_ATTN_SPLIT=0)."""
     from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
-    monkeypatch.setenv("SF_ATTN_VARIANT", str(variant))
+    monkeypatch.setenv("SF_ATTN_KERNEL", str(kernel))
+    monkeypatch.setenv("SF_ATTN_EMU", str(emu))
     monkeypatch.setenv("SF_ATTN_SPLIT", split)
-    expect = 2 if (variant >= 4 and split == "1") else 1
+    expect = 2 if split == "1" else 1
     assert E.attention_launch_count(1, 2, 300, 641) == expect
-    rng = np.random.default_rng(40 + variant)
+    rng = np.random.default_rng(40 + kernel * 4 + emu)
     B, H, Lq, Lk = 1, 2, 300, 641
     q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
     k32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32) * np.float32(3)
@@ -179,8 +177,9 @@ def test_fused_attention_every_variant(gpu, ops, monkeypatch, variant, split):
         sl = slice(h * 64, (h + 1) * 64)
         p = O.softmax_rows((q[0][:, sl] @ k[0][:, sl].T * np.float32(0.125)).astype(np.float32))
         ref, allow = O.flash_attention(q[0][:, sl], k[0][:, sl], v[0][:, sl], 0.125,
-                                       return_allowance=True, **attn_oracle_opts(variant))
-        _check_attn(out[:, sl], ref, O.abs_product(p, v[0][:, sl].T), allow, f"v{variant} h{h}")
+                                       return_allowance=True, **attn_oracle_opts(kernel))
+        _check_attn(out[:, sl], ref, O.abs_product(p, v[0][:, sl].T), allow,
+                    f"kernel {kernel} emu {emu} h{h}")
     assert device_error(0) == 0
 
 
@@ -254,8 +253,6 @@ def test_fused_attention_split_keys_merge(gpu, ops, lo, hi):
 
     from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
-    if attn_oracle_opts()["integer_base"] is False:
-        pytest.skip("partial attention needs the TMEM-accumulator kernel")
     rng = np.random.default_rng(lo + hi)
     B, H, Lq, Lk = 2, 3, 200, 700
     W = H * 64
