@@ -217,6 +217,23 @@ int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len, in
 int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
                                   int32_t part_mode, int32_t* count);
 
+/* LayerNorm over the last dimension with an optional per-group adaptive
+ * scale / shift (adaLN), for row r < rows, column c < cols:
+ *   h = (x[r,c] - mean_r) / sqrt(var_r + eps) * gamma[c] + beta[c]
+ *   y[r,c] = mod ? h * (1 + mod[g, c]) + mod[g, cols + c] : h,   g = r / group_rows
+ * (population variance, fp32 arithmetic; gamma / beta fp32 [cols] or NULL;
+ * mod [groups][ld_mod >= 2 * cols] in mod_dtype, e.g. the output of a DiT
+ * block's modulation linear, one row per sample of group_rows tokens).
+ * Replaces cuda_layer_norm_f32 (_cuda_ops_decl.h, _cuda_kernels.cu:1070-1093,
+ * behind nn/layers.py:470-493) and the host modulation of AdaLayerNorm
+ * (diffusion/models.py:478-487), as one bandwidth kernel before the QKV and
+ * FFN-up GEMMs. */
+int32_t sf_layernorm_modulate(int64_t rows, int64_t cols, const void* x, int32_t x_dtype,
+                              int64_t ldx, const float* gamma, const float* beta, float eps,
+                              const void* mod, int32_t mod_dtype, int64_t ld_mod,
+                              int64_t group_rows, void* y, int32_t y_dtype, int64_t ldy,
+                              void* stream);
+
 /* y[i] = act(alpha * x[i]).  Replaces cuda_silu_f32 / cuda_gelu_f32 /
  * cuda_muls_f32 (_cuda_ops_decl.h:69, :74, :63; _cuda_kernels.cu:384, :428,
  * :237-277) for the standalone dev_silu / dev_gelu / dev_muls calls. */

@@ -25,7 +25,8 @@ __all__ = [
     "round_bf16", "round_f16", "round_to", "bf16_bits", "bf16_from_bits",
     "linear", "silu", "gelu_tanh", "activation", "linear_act",
     "matmul", "matmul_nt", "batched_matmul", "batched_matmul_nt",
-    "softmax_rows", "sdpa", "dit_attention_chunked", "dit_layer", "dit_block_linears",
+    "softmax_rows", "sdpa", "layer_norm", "ada_layer_norm", "block_attention", "heads_split", "heads_merge",
+    "dit_attention_chunked", "dit_layer", "dit_block_linears",
     "config1_inputs", "square_inputs", "skinny_inputs", "dit_weights",
     "rel_frobenius", "elementwise_rel_check", "abs_product", "ACT_NONE", "ACT_SILU",
     "ACT_GELU_TANH",
@@ -173,6 +174,66 @@ def sdpa(q: np.ndarray, k: np.ndarray, v: np.ndarray,
     s_sum = scores.sum(axis=-1, keepdims=True)
     np.divide(scores, s_sum, out=scores)
     return np.matmul(scores, v)
+
+
+def layer_norm(x: np.ndarray, gamma: np.ndarray | None = None, beta: np.ndarray | None = None,
+               eps: float = 1e-5) -> np.ndarray:
+    """``LayerNorm.forward`` NumPy path, ``nn/layers.py:512-521``: mean and
+    (population) variance over the last axis, ``(x - mean) / sqrt(var + eps)``,
+    then ``* weight + bias``."""
+    x = np.asarray(x, np.float32)
+    mean = np.mean(x, axis=-1, keepdims=True)
+    var = np.var(x, axis=-1, keepdims=True)
+    y = (x - mean) / np.sqrt(var + eps)
+    if gamma is not None:
+        y = y * gamma + beta
+    return y.astype(np.float32)
+
+
+def ada_layer_norm(x: np.ndarray, params: np.ndarray, gamma=None, beta=None,
+                   eps: float = 1e-5) -> np.ndarray:
+    """``AdaLayerNorm.forward`` (``diffusion/models.py:478-487``): LayerNorm,
+    then ``h * (params[..., :C] + 1) + params[..., C:]`` with ``params`` the
+    modulation linear's output for each sample.  ``x`` is ``(B, N, C)`` and
+    ``params`` ``(B, 2C)``; each sample's row of params modulates all of its
+    tokens (``params[:, None, :]``).  The reference broadcasts ``(B, C)``
+    against ``(B, N, C)`` directly, which is the same for B = 1 (the case its
+    golden vectors pin) and misaligned for B > 1."""
+    h = layer_norm(x, gamma, beta, eps)
+    C = h.shape[-1]
+    p = np.asarray(params, np.float32)
+    if p.ndim == 2 and h.ndim == 3:
+        p = p[:, None, :]
+    return (h * (p[..., :C] + 1.0) + p[..., C:]).astype(np.float32)
+
+
+def block_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:
+    """``CrossAttentionBlock._attn`` (``diffusion/models.py:123-133``) on
+    ``(B, H, N, D)`` / ``(B, H, S, D)`` arrays: einsum scores scaled by
+    ``1/sqrt(D)``, max-subtracted exp, division by ``sum + 1e-9``, einsum
+    with v."""
+    B, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    scores = np.einsum('bhnd,bhmd->bhnm', q, k) * scale
+    scores -= scores.max(axis=-1, keepdims=True)
+    exp_s = np.exp(scores)
+    attn = exp_s / (exp_s.sum(axis=-1, keepdims=True) + 1e-9)
+    return np.einsum('bhnm,bhmd->bhnd', attn, v)
+
+
+def heads_split(x: np.ndarray, heads: int) -> np.ndarray:
+    """``[B, N, C] -> (B, H, N, D)``: the reference's
+    ``reshape(B, N, H, D).transpose(0, 2, 1, 3)`` (``diffusion/models.py:148-151``,
+    ``:167-169``; ``nn/video.py:364-371``)."""
+    B, N, C = x.shape
+    return x.reshape(B, N, heads, C // heads).transpose(0, 2, 1, 3).copy()
+
+
+def heads_merge(x: np.ndarray) -> np.ndarray:
+    """``(B, H, N, D) -> [B, N, C]``: ``transpose(0, 2, 1, 3).reshape(B, N, C)``
+    (``diffusion/models.py:153``, ``:174``; ``nn/video.py:376``, ``:408``)."""
+    B, H, N, D = x.shape
+    return x.transpose(0, 2, 1, 3).reshape(B, N, H * D).copy()
 
 
 def dit_attention_chunked(qkv: np.ndarray, batch: int, heads: int,
@@ -443,10 +504,20 @@ def elementwise_rel_check(out: np.ndarray, ref: np.ndarray, rtol: float = 1e-2,
     pure = err / np.where(absr > 0, absr, np.inf)
     needed_floor = int(np.count_nonzero((pure > rtol) & (floored <= rtol)))
     worst = float(floored.max()) if floored.size else 0.0
+    # Which floor each passing element relied on (first that suffices, in
+    # the order row RMS, |A||B|, rounding-flip allowance).
+    raw = np.abs(oo - rr)
+    ok_final = floored <= rtol
+    ok_pure = raw <= rtol * absr
+    ok_row = raw <= rtol * np.maximum(absr, tau * rms)
+    ok_abs = raw <= rtol * den
     stats = {
         "max_rel_floored": worst,
         "max_rel_pure": float(np.nanmax(pure)) if pure.size else 0.0,
         "n_needed_floor": needed_floor,
+        "n_row_floor": int(np.count_nonzero(ok_final & ~ok_pure & ok_row)),
+        "n_absprod_floor": int(np.count_nonzero(ok_final & ~ok_row & ok_abs)),
+        "n_allowance": int(np.count_nonzero(ok_final & ~ok_abs)),
         "n": int(rr.size),
         "tau": tau,
         "rtol": rtol,

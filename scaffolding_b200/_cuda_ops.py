@@ -13,6 +13,8 @@ sm_100a engine (``libsf_engine.so``) instead of cuBLAS:
   and the host-array ``cuda_*`` variants (``:2120-2230``, ``:2453-2471``);
 * the glue the attention path uses: ``dev_muls``, ``dev_softmax``, ``dev_silu``,
   ``dev_gelu``, ``dev_reshape``, ``dev_unsqueeze``, ``dev_squeeze``;
+* ``dev_layer_norm`` and the DiT blocks' adaptive norm ``dev_ada_layer_norm``
+  (the bandwidth step in front of the QKV and FFN-up GEMMs);
 * runtime: devices, caching allocator, streams, events, peer access.
 
 Differences from the reference, all deliberate:
@@ -30,7 +32,7 @@ Differences from the reference, all deliberate:
 * ``gputensor_to_device`` copies ``numel * itemsize`` bytes (the reference
   assumed 4-byte elements, ``_cuda_ops.pyx:868-870``).
 
-Operations outside the matmul path (layer norm, cross-entropy, AdamW, ...)
+Operations outside the matmul path (RMS norm, cross-entropy, AdamW, ...)
 raise ``NotImplementedError`` naming the op.
 """
 from __future__ import annotations
@@ -338,6 +340,54 @@ def dev_softmax(gt: GpuTensor, dim: int = -1) -> GpuTensor:
     return out
 
 
+def _norm_launch(gt: GpuTensor, gamma, beta, eps: float, mod=None, group_rows: int = 1,
+                 out_dtype=None) -> GpuTensor:
+    cols = gt.shape[-1]
+    rows = gt.numel // cols if cols else 0
+    dev = gt.device_id
+    odt = np.dtype(out_dtype) if out_dtype is not None else gt.dtype
+    out = _alloc(gt.shape, odt, dev)
+    for t, name in ((gamma, "gamma"), (beta, "beta")):
+        if t is not None and (t.dtype != np.float32 or t.numel != cols):
+            raise ValueError(f"layer norm {name} must be fp32 with {cols} elements")
+    if (gamma is None) != (beta is None):
+        raise ValueError("layer norm gamma and beta go together")
+    mod_ptr, mod_dt, ld_mod = None, DT_F32, 0
+    if mod is not None:
+        if mod.shape[-1] != 2 * cols:
+            raise ValueError(f"modulation rows must hold 2 x {cols} values, got {mod.shape}")
+        mod_ptr, mod_dt, ld_mod = C.c_void_p(mod.ptr), E.dtype_code(mod.dtype), 2 * cols
+    with E.on_device(dev):
+        s = E.get_stream(dev)
+        check(lib.sf_layernorm_modulate(rows, cols, C.c_void_p(gt.ptr), E.dtype_code(gt.dtype), cols,
+                                        C.c_void_p(gamma.ptr) if gamma is not None else None,
+                                        C.c_void_p(beta.ptr) if beta is not None else None,
+                                        float(eps), mod_ptr, mod_dt, ld_mod, int(group_rows),
+                                        C.c_void_p(out.ptr), E.dtype_code(odt), cols,
+                                        C.c_void_p(s) if s else None), "sf_layernorm_modulate")
+    return out
+
+
+def dev_layer_norm(gt: GpuTensor, gt_gamma: GpuTensor | None = None,
+                   gt_beta: GpuTensor | None = None, eps: float = 1e-5) -> GpuTensor:
+    """LayerNorm over the last dimension (``dev_layer_norm`` behind
+    ``nn/layers.py:470-493``; kernel ``_cuda_kernels.cu:1070-1093``), fp32 /
+    bf16 / fp16 in and out, fp32 gamma and beta."""
+    return _norm_launch(gt, gt_gamma, gt_beta, eps)
+
+
+def dev_ada_layer_norm(gt: GpuTensor, gt_params: GpuTensor, gt_gamma: GpuTensor | None = None,
+                       gt_beta: GpuTensor | None = None, eps: float = 1e-5,
+                       out_dtype=None) -> GpuTensor:
+    """AdaLayerNorm (``diffusion/models.py:478-487``) of ``x [B, N, C]`` with
+    the modulation linear's output ``params [B, 2C]``: LayerNorm, then
+    ``h * (1 + params[b, :C]) + params[b, C:]`` for every token of sample b,
+    in one kernel.  New (the reference modulates on the host)."""
+    if gt.ndim != 3 or gt_params.ndim != 2 or gt_params.shape[0] != gt.shape[0]:
+        raise ValueError(f"adaLN shapes: x {gt.shape}, params {gt_params.shape}")
+    return _norm_launch(gt, gt_gamma, gt_beta, eps, gt_params, gt.shape[1], out_dtype)
+
+
 def dev_unsqueeze(gt: GpuTensor, dim: int) -> GpuTensor:
     shape = list(gt.shape)
     if dim < 0:
@@ -579,7 +629,7 @@ def cublas_set_stream(stream: CudaStream | None = None) -> None:
 _OUT_OF_SCOPE = {
     "dev_exp", "dev_log", "dev_sqrt", "dev_rsqrt", "dev_sigmoid", "dev_tanh", "dev_sin",
     "dev_cos", "dev_neg", "dev_abs", "dev_relu", "dev_add", "dev_sub", "dev_mul", "dev_div",
-    "dev_adds", "dev_clamp", "dev_log_softmax", "dev_cross_entropy", "dev_layer_norm",
+    "dev_adds", "dev_clamp", "dev_log_softmax", "dev_cross_entropy",
     "dev_rms_norm", "dev_dropout", "dev_embedding", "dev_adamw_step", "dev_sum", "dev_fill",
     "dev_copy", "dev_transpose_2d", "dev_pow_scalar", "dev_expand", "dev_slice", "dev_cat",
     "dev_stack", "dev_chunk", "dev_cumsum", "dev_mean_dim", "dev_sum_dim", "dev_sum_tensor",

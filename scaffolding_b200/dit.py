@@ -38,6 +38,47 @@ def block_flops(m: int, C: int = HIDDEN) -> float:
     return 2.0 * m * C * (3 * C + C + 4 * C + 4 * C)
 
 
+def _block_launches(C: int, m: int, w: dict, x_ptr: int, qkv: int, h: int, f: int, y: int):
+    """The four GEMM launches of one block on m token rows as (name, kwargs)
+    for engine.gemm; w holds the device weights, the rest are device pointers."""
+    bf = DT_BF16
+    return [
+        ("qkv", dict(M=m, N=3 * C, K=C, A=x_ptr, lda=C, trans_a=0, B=w["qkv_w"].ptr, ldb=C,
+                     trans_b=1, Cp=qkv, ldc=3 * C, in_dt=bf, out_dt=bf, epi=None)),
+        ("out", dict(M=m, N=C, K=C, A=qkv, lda=3 * C, trans_a=0, B=w["out_w"].ptr,
+                     ldb=C, trans_b=1, Cp=h, ldc=C, in_dt=bf, out_dt=bf,
+                     epi=E.make_epilogue(bias_ptr=w["out_b"].ptr, bias_dt=bf, act=ACT_NONE,
+                                         residual_ptr=x_ptr, residual_dt=bf, ldr=C))),
+        ("up", dict(M=m, N=4 * C, K=C, A=h, lda=C, trans_a=0, B=w["up_w"].ptr,
+                    ldb=C, trans_b=1, Cp=f, ldc=4 * C, in_dt=bf, out_dt=bf,
+                    epi=E.make_epilogue(bias_ptr=w["up_b"].ptr, bias_dt=bf,
+                                        act=ACT_GELU_TANH))),
+        ("down", dict(M=m, N=C, K=4 * C, A=f, lda=4 * C, trans_a=0,
+                      B=w["down_w"].ptr, ldb=4 * C, trans_b=1, Cp=y, ldc=C,
+                      in_dt=bf, out_dt=bf,
+                      epi=E.make_epilogue(bias_ptr=w["down_b"].ptr, bias_dt=bf, act=ACT_NONE,
+                                          residual_ptr=h, residual_dt=bf, ldr=C))),
+    ]
+
+
+def _run_launches(launches, dev: int, stream=None, timer=None) -> None:
+    for name, kw in launches:
+        if timer is not None:
+            timer.start(name)
+        E.gemm(kw["M"], kw["N"], kw["K"], kw["A"], kw["lda"], kw["trans_a"], kw["B"],
+               kw["ldb"], kw["trans_b"], kw["Cp"], kw["ldc"], kw["in_dt"], kw["out_dt"],
+               epi=kw["epi"], device=dev, stream=stream)
+        if timer is not None:
+            timer.stop(name)
+
+
+def _upload_weights(weights: dict, device: int) -> dict:
+    bf = E.bfloat16
+    return {k: (v if isinstance(v, ops.GpuTensor)
+                else ops.gputensor_from_numpy(np.ascontiguousarray(v).astype(bf), device))
+            for k, v in weights.items()}
+
+
 class DitLinears:
     """Device-resident bf16 weights of one block plus activation buffers for
     an m-row token shard."""
@@ -47,8 +88,7 @@ class DitLinears:
         self.C = weights["out_w"].shape[0]
         self.m = m
         self.dev = device
-        up = lambda a: ops.gputensor_from_numpy(np.ascontiguousarray(a).astype(bf), device)  # noqa: E731
-        self.w = {k: up(v) for k, v in weights.items()}
+        self.w = _upload_weights(weights, device)
         C = self.C
         self.qkv = ops._alloc((m, 3 * C), bf, device)
         self.h = ops._alloc((m, C), bf, device)
@@ -57,35 +97,39 @@ class DitLinears:
 
     def launches(self, x_ptr: int):
         """The four GEMM launches of one block as (name, kwargs) for engine.gemm."""
-        C, m, w = self.C, self.m, self.w
-        bf = DT_BF16
-        return [
-            ("qkv", dict(M=m, N=3 * C, K=C, A=x_ptr, lda=C, trans_a=0, B=w["qkv_w"].ptr, ldb=C,
-                         trans_b=1, Cp=self.qkv.ptr, ldc=3 * C, in_dt=bf, out_dt=bf, epi=None)),
-            ("out", dict(M=m, N=C, K=C, A=self.qkv.ptr, lda=3 * C, trans_a=0, B=w["out_w"].ptr,
-                         ldb=C, trans_b=1, Cp=self.h.ptr, ldc=C, in_dt=bf, out_dt=bf,
-                         epi=E.make_epilogue(bias_ptr=w["out_b"].ptr, bias_dt=bf, act=ACT_NONE,
-                                             residual_ptr=x_ptr, residual_dt=bf, ldr=C))),
-            ("up", dict(M=m, N=4 * C, K=C, A=self.h.ptr, lda=C, trans_a=0, B=w["up_w"].ptr,
-                        ldb=C, trans_b=1, Cp=self.f.ptr, ldc=4 * C, in_dt=bf, out_dt=bf,
-                        epi=E.make_epilogue(bias_ptr=w["up_b"].ptr, bias_dt=bf,
-                                            act=ACT_GELU_TANH))),
-            ("down", dict(M=m, N=C, K=4 * C, A=self.f.ptr, lda=4 * C, trans_a=0,
-                          B=w["down_w"].ptr, ldb=4 * C, trans_b=1, Cp=self.y.ptr, ldc=C,
-                          in_dt=bf, out_dt=bf,
-                          epi=E.make_epilogue(bias_ptr=w["down_b"].ptr, bias_dt=bf, act=ACT_NONE,
-                                              residual_ptr=self.h.ptr, residual_dt=bf, ldr=C))),
-        ]
+        return _block_launches(self.C, self.m, self.w, x_ptr, self.qkv.ptr, self.h.ptr,
+                               self.f.ptr, self.y.ptr)
 
     def run(self, x_ptr: int, stream: int | None = None, timer=None) -> None:
-        for name, kw in self.launches(x_ptr):
-            if timer is not None:
-                timer.start(name)
-            E.gemm(kw["M"], kw["N"], kw["K"], kw["A"], kw["lda"], kw["trans_a"], kw["B"],
-                   kw["ldb"], kw["trans_b"], kw["Cp"], kw["ldc"], kw["in_dt"], kw["out_dt"],
-                   epi=kw["epi"], device=self.dev, stream=stream)
-            if timer is not None:
-                timer.stop(name)
+        _run_launches(self.launches(x_ptr), self.dev, stream, timer)
+
+
+class DitBlock:
+    """The block linears as a module (the config-4 workload): ``forward(x)``
+    on ``[m, C]`` bf16 token rows returns ``y [m, C]`` (QKV projection,
+    out projection + bias + residual, FFN-up + GELU, FFN-down + bias +
+    residual; four fused-epilogue GEMM launches).  Every output row depends
+    on its own input row only, so ``parallel.DataParallel`` can split the
+    rows over GPUs."""
+
+    def __init__(self, weights: dict, device: int):
+        self.dev = device
+        self.w = _upload_weights(weights, device)
+        self.C = self.w["out_w"].shape[0]
+
+    def forward(self, x: "ops.GpuTensor") -> "ops.GpuTensor":
+        if x.ndim != 2 or x.shape[1] != self.C:
+            raise ValueError(f"DitBlock expects [m, {self.C}] rows, got {x.shape}")
+        m, C, dev, bf = x.shape[0], self.C, x.device_id, E.bfloat16
+        qkv = ops._alloc((m, 3 * C), bf, dev)
+        h = ops._alloc((m, C), bf, dev)
+        f = ops._alloc((m, 4 * C), bf, dev)
+        y = ops._alloc((m, C), bf, dev)
+        with E.on_device(dev):
+            _run_launches(_block_launches(C, m, self.w, x.ptr, qkv.ptr, h.ptr, f.ptr, y.ptr), dev)
+        return y
+
+    __call__ = forward
 
 
 
@@ -156,11 +200,19 @@ class DitStack:
     The reference runs the same sequence with separate scale / softmax /
     bmm launches and the attention on the host (``nn/functional.py:310-321``,
     ``diffusion/models.py:529-590``).
+
+    ``adaln=True`` adds the block's adaptive LayerNorms (norm1 before the QKV
+    projection, norm3 before FFN-up, ``diffusion/models.py:470-487``): per
+    layer two modulation linears on the per-sample condition vector and two
+    fused norm + modulation kernels (``sf_layernorm_modulate``).  Benchmark
+    config 5 specifies the linears and attention without them, so it is off
+    by default.
     """
 
     def __init__(self, plan: ShardPlan, hidden: int, heads: int, layers: int, device: int,
                  chunk: int = 2048, weights: list | None = None, seed: int = 1,
-                 kv_comm=None, world_comm=None, fused: bool | None = None):
+                 kv_comm=None, world_comm=None, fused: bool | None = None,
+                 adaln: bool = False):
         import ctypes as C
 
         from ._lib import check, lib
@@ -207,6 +259,29 @@ class DitStack:
             self.S = ops._alloc((spr, heads, crow, keys), np.float32, device)
             self.P = ops._alloc((spr, heads, crow, keys), bf, device)
         self.attn = ops._alloc((m, Cw), bf, device)
+        # Adaptive LayerNorm in front of the QKV and FFN-up GEMMs (DiTBlock's
+        # norm1 / norm3, diffusion/models.py:470-487, 555, 584): per layer
+        # two modulation linears (cond [B, C] -> [B, 2C]) and the fused
+        # norm + modulation kernel; cond is one [B, C] vector per sample.
+        self.adaln = bool(adaln)
+        self.xn = self.cond = None
+        self.mod = []
+        if self.adaln:
+            B = plan.batch
+            self.xn = ops._alloc((m, Cw), bf, device)
+            self.cond = ops._alloc((B, Cw), bf, device)
+            check(lib.sf_fill_normal(C.c_void_p(self.cond.ptr), DT_BF16, B * Cw, seed * 7 + 3,
+                                     0.0, 1.0, None), "sf_fill_normal")
+            for li in range(layers):
+                lm = {}
+                for j, name in enumerate(("mod1", "mod3")):
+                    wt = ops._alloc((2 * Cw, Cw), bf, device)
+                    check(lib.sf_fill_normal(C.c_void_p(wt.ptr), DT_BF16, wt.numel,
+                                             seed * 1000003 + li * 16 + 8 + j, 0.0, 0.02, None),
+                          "sf_fill_normal")
+                    lm[name + "_w"] = wt
+                    lm[name + "_p"] = ops._alloc((B, 2 * Cw), bf, device)
+                self.mod.append(lm)
         self.h = ops._alloc((m, Cw), bf, device)
         self.f = ops._alloc((m, 4 * Cw), bf, device)
         self.y = [ops._alloc((m, Cw), bf, device), ops._alloc((m, Cw), bf, device)]
@@ -217,8 +292,7 @@ class DitStack:
         # partial result while the gather runs on a side stream; attention over
         # the gathered keys (minus the local slice) merges it.
         self.overlap = (self.fused and plan.kv_exchange
-                        and os.environ.get("SF_KV_OVERLAP", "1") != "0"
-                        and os.environ.get("SF_ATTN_VARIANT", "6") in ("4", "5", "6", "7"))
+                        and os.environ.get("SF_KV_OVERLAP", "1") != "0")
         self.part_o = self.part_ml = None
         self.comm_stream = self.ev_kv = self.ev_gather = None
         if self.overlap:
@@ -307,10 +381,37 @@ class DitStack:
                        self.kv_full.ptr + Cw * 2, 2 * Cw, 0, self.attn.ptr + c0 * Cw * 2, Cw,
                        bf, bf, batch=bt2)
 
+    def _adaln(self, li: int, which: str, x_ptr: int, stream, timer) -> int:
+        """Modulation linear of ``which`` (mod1 / mod3) for layer ``li``, then
+        LayerNorm + per-sample scale / shift of the rank's rows into ``xn``;
+        returns the pointer of the normalised rows."""
+        import ctypes as C
+
+        from ._lib import check, lib
+        p, Cw, lm = self.plan, self.C, self.mod[li]
+        B, bf = p.batch, DT_BF16
+        prm = lm[which + "_p"]
+        self._gemm(which, timer, stream, B, 2 * Cw, Cw, self.cond.ptr, Cw, 0, lm[which + "_w"].ptr,
+                   Cw, 1, prm.ptr, 2 * Cw, bf, bf)
+        # the rank's rows: whole samples (group = tokens) or one sample's slice
+        group = p.tokens if p.whole_samples else p.m
+        s = stream if stream else E.get_stream(self.dev)
+        if timer is not None:
+            timer.start("adaln")
+        check(lib.sf_layernorm_modulate(p.m, Cw, C.c_void_p(x_ptr), bf, Cw, None, None, 1e-5,
+                                        C.c_void_p(prm.ptr + p.sample0 * 2 * Cw * 2), bf, 2 * Cw,
+                                        group, C.c_void_p(self.xn.ptr), bf, Cw,
+                                        C.c_void_p(s) if s else None), "sf_layernorm_modulate")
+        if timer is not None:
+            timer.stop("adaln")
+        return self.xn.ptr
+
     def qkv(self, li: int, x_ptr: int, stream=None, timer=None) -> None:
         """q and the local K/V rows of layer ``li``."""
         p, Cw, w = self.plan, self.C, self.w[li]
         m, bf = p.m, DT_BF16
+        if self.adaln:
+            x_ptr = self._adaln(li, "mod1", x_ptr, stream, timer)
         self._gemm("q", timer, stream, m, Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr, Cw, 1,
                    self.q.ptr, Cw, bf, bf)
         self._gemm("kv", timer, stream, m, 2 * Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr + Cw * Cw * 2,
@@ -354,7 +455,8 @@ class DitStack:
                    self.h.ptr, Cw, bf, bf,
                    epi=E.make_epilogue(bias_ptr=w["out_b"].ptr, bias_dt=bf, residual_ptr=x_ptr,
                                        residual_dt=bf, ldr=Cw))
-        self._gemm("up", timer, stream, m, 4 * Cw, Cw, self.h.ptr, Cw, 0, w["up_w"].ptr, Cw, 1,
+        up_in = self._adaln(li, "mod3", self.h.ptr, stream, timer) if self.adaln else self.h.ptr
+        self._gemm("up", timer, stream, m, 4 * Cw, Cw, up_in, Cw, 0, w["up_w"].ptr, Cw, 1,
                    self.f.ptr, 4 * Cw, bf, bf,
                    epi=E.make_epilogue(bias_ptr=w["up_b"].ptr, bias_dt=bf, act=ACT_GELU_TANH))
         self._gemm("down", timer, stream, m, Cw, 4 * Cw, self.f.ptr, 4 * Cw, 0, w["down_w"].ptr,
@@ -403,9 +505,22 @@ class DitStack:
             else:
                 n_attn = E.attention_launch_count(p.samples_per_rank, self.H, q_rows, p.tokens, 0,
                                                   device=self.dev)
-            return self.L * (5 + n_attn)
+            return self.L * (5 + n_attn + self._adaln_launches())
         chunks = (q_rows + self.chunk - 1) // self.chunk
-        return self.L * (5 + 3 * chunks)
+        return self.L * (5 + 3 * chunks + self._adaln_launches())
+
+    def _adaln_launches(self) -> int:
+        """Per layer: two modulation linears and two norm kernels (a linear
+        whose split-K needs a workspace is two launches)."""
+        if not self.adaln:
+            return 0
+        import ctypes as C
+
+        from ._lib import check, lib
+        need = C.c_size_t()
+        check(lib.sf_gemm_workspace_size(None, self.plan.batch, 2 * self.C, self.C, 0, 1, DT_BF16,
+                                         DT_BF16, C.byref(need)), "sf_gemm_workspace_size")
+        return 2 * (2 if need.value else 1) + 2
 
 
 def stack_flops(batch: int, tokens: int, hidden: int, heads: int, layers: int) -> float:

@@ -10,9 +10,13 @@ argument meaning and error behaviour:
   optional fused ``activation`` and a storage ``dtype`` (bf16 / fp16).
 * ``functional.linear`` -- ``nn/functional.py:374-395``.
 * ``functional.scaled_dot_product_attention`` -- GPU path of
-  ``nn/functional.py:310-321``: QK^T (one batched launch, scale fused in
-  its epilogue), row softmax, P.V.
+  ``nn/functional.py:310-321``: for bf16/fp16 with head_dim 64 the fused
+  attention kernel (one launch, scores never leave the SM); otherwise QK^T
+  (one batched launch, scale fused in its epilogue), row softmax, P.V.
 * ``functional.silu`` / ``gelu`` / ``softmax`` -- ``nn/functional.py:37-145``.
+* ``Sequential`` -- the container the reference's models stack layers in.
+* ``LayerNorm`` (``nn/layers.py:443-521``) and ``AdaLayerNorm``
+  (``diffusion/models.py:470-487``), the norms in front of the DiT linears.
 """
 from __future__ import annotations
 
@@ -54,6 +58,63 @@ class Linear:
         self._to(x.device_id)
         ops.set_device(x.device_id)
         return ops.dev_linear_forward(x, self.weight, self.bias, activation)
+
+    __call__ = forward
+
+
+class LayerNorm:
+    """``nn.LayerNorm`` (``nn/layers.py:443-521``) over the last dimension:
+    fp32 weight (ones) and bias (zeros) on the device, GPU forward through
+    ``dev_layer_norm``."""
+
+    def __init__(self, normalized_shape, eps: float = 1e-5, elementwise_affine: bool = True,
+                 device=None):
+        if isinstance(normalized_shape, int):
+            normalized_shape = (normalized_shape,)
+        self.normalized_shape = tuple(normalized_shape)
+        self.eps = eps
+        dev = _device_index(device)
+        C = self.normalized_shape[-1]
+        if elementwise_affine:
+            self.weight = ops.gputensor_from_numpy(np.ones(C, np.float32), dev)
+            self.bias = ops.gputensor_from_numpy(np.zeros(C, np.float32), dev)
+        else:
+            self.weight = self.bias = None
+
+    def forward(self, x: GpuTensor) -> GpuTensor:
+        return ops.dev_layer_norm(x, self.weight, self.bias, self.eps)
+
+    __call__ = forward
+
+
+class AdaLayerNorm:
+    """``AdaLayerNorm`` (``diffusion/models.py:470-487``): LayerNorm of
+    ``x [B, N, C]`` modulated per sample by ``linear(cond)`` (``[B, 2C]``:
+    scale ``+ 1`` then shift), the modulation applied in the norm kernel."""
+
+    def __init__(self, dim: int, cond_dim: int, device=None, dtype=np.float32,
+                 rng: np.random.Generator | None = None):
+        self.norm = LayerNorm(dim, device=device)
+        self.linear = Linear(cond_dim, dim * 2, device=device, dtype=dtype, rng=rng)
+
+    def forward(self, x: GpuTensor, cond: GpuTensor) -> GpuTensor:
+        params = self.linear(cond)
+        return ops.dev_ada_layer_norm(x, params, self.norm.weight, self.norm.bias, self.norm.eps)
+
+    __call__ = forward
+
+
+class Sequential:
+    """Modules applied in order (``nn/module.py:345``): each
+    takes and returns a GpuTensor."""
+
+    def __init__(self, *modules):
+        self.layers = list(modules)
+
+    def forward(self, x: GpuTensor) -> GpuTensor:
+        for m in self.layers:
+            x = m(x)
+        return x
 
     __call__ = forward
 
@@ -110,6 +171,8 @@ def _sdpa(q: GpuTensor, k: GpuTensor, v: GpuTensor, attn_mask=None, dropout_p: f
     batch = int(np.prod(lead, dtype=np.int64)) if lead else 1
     dev = q.device_id
     code = E.dtype_code(q.dtype)
+    if d == 64 and code != E.DT_F32 and q.dtype == k.dtype == v.dtype:
+        return _sdpa_fused(q, k, v, float(scale), lead, batch, M, S, code, dev)
     scores = ops._alloc(lead + (M, S), score_dtype, dev)
     probs = ops._alloc(lead + (M, S), q.dtype, dev)
     out = ops._alloc(lead + (M, d), q.dtype, dev)
@@ -122,6 +185,31 @@ def _sdpa(q: GpuTensor, k: GpuTensor, v: GpuTensor, attn_mask=None, dropout_p: f
         bt2 = E.make_batch(batch, 1, a=(M * S, 0), b=(S * d, 0), c=(M * d, 0))
         E.gemm(M, d, S, probs.ptr, S, 0, v.ptr, d, 0, out.ptr, d, code, code, batch=bt2,
                device=dev)
+    return out
+
+
+# Calls of scaled_dot_product_attention served by the fused kernel.
+sdpa_fused_calls = 0
+
+# The fused kernel's grid holds at most 65535 batch items per launch.
+_FUSED_MAX_BATCH = 65535
+
+
+def _sdpa_fused(q, k, v, scale, lead, batch, M, S, code, dev) -> GpuTensor:
+    """16-bit, head_dim 64: one fused launch (QK^T, online softmax and P.V on
+    chip, ``sf_attention_fwd``) per 65535 batch items instead of the three
+    launches and the [.., M, S] score and probability buffers of the chain
+    below.  Each (…, M, 64) matrix is one batch item with a single head."""
+    global sdpa_fused_calls
+    out = ops._alloc(lead + (M, 64), q.dtype, dev)
+    with E.on_device(dev):
+        for b0 in range(0, batch, _FUSED_MAX_BATCH):
+            nb = min(_FUSED_MAX_BATCH, batch - b0)
+            off = b0 * 2
+            E.attention(nb, 1, M, S, q.ptr + off * M * 64, 64, M * 64, k.ptr + off * S * 64, 64,
+                        S * 64, v.ptr + off * S * 64, 64, S * 64, out.ptr + off * M * 64, 64,
+                        M * 64, scale, dtype=code, head_dim=64, device=dev)
+    sdpa_fused_calls += 1
     return out
 
 

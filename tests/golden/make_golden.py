@@ -9,7 +9,9 @@ The reference package is copied to a temporary directory and imported as
 NumPy/OpenBLAS (``tensor.py:20-41``), i.e. exactly the code the oracle
 restates.  Each case below calls the reference's public API
 (``nn.Linear``, ``F.silu``, ``F.gelu``, ``F.linear``, ``F.softmax``,
-``sf.matmul``, ``sf.matmul_nt``, ``F.scaled_dot_product_attention``) on seeded
+``sf.matmul``, ``sf.matmul_nt``, ``F.scaled_dot_product_attention``,
+``nn.LayerNorm`` / ``diffusion.models.AdaLayerNorm`` and
+``CrossAttentionBlock._attn``) on seeded
 inputs and stores inputs + outputs in ``golden.npz`` next to this script.
 Config 1 (512x1024 -> 4096, SiLU) is too large to store whole: its inputs are
 regenerated from the seed and a row subsample plus full-array checksums of
@@ -139,6 +141,29 @@ def main(ref_root: str) -> None:
     out["sdpa8_q"], out["sdpa8_k"], out["sdpa8_v"] = q2, k2, v2
     out["sdpa8_o"] = F.scaled_dot_product_attention(
         Tensor(q2), Tensor(k2), Tensor(v2), scale=0.125)._data
+
+    # ── LayerNorm and AdaLayerNorm (nn/layers.py:443-521, diffusion/models.py:470-487)
+    import importlib
+    M = importlib.import_module("scaffolding.diffusion.models")
+    C, cond_dim, N = 64, 32, 24
+    xa = rn(1, N, C) * np.float32(2) + np.float32(0.5)
+    cond = rn(1, cond_dim)
+    ada = M.AdaLayerNorm(C, cond_dim)
+    ada.norm.weight._data = (1 + 0.1 * rn(C)).astype(np.float32)
+    ada.norm.bias._data = (0.1 * rn(C)).astype(np.float32)
+    ada.linear.weight._data = (0.05 * rn(2 * C, cond_dim)).astype(np.float32)
+    ada.linear.bias._data = (0.05 * rn(2 * C)).astype(np.float32)
+    out["adaln_x"], out["adaln_cond"] = xa, cond
+    out["adaln_gamma"], out["adaln_beta"] = ada.norm.weight._data, ada.norm.bias._data
+    out["adaln_w"], out["adaln_b"] = ada.linear.weight._data, ada.linear.bias._data
+    out["adaln_params"] = ada.linear(Tensor(cond))._data
+    out["adaln_ln"] = ada.norm(Tensor(xa))._data
+    out["adaln_y"] = ada(Tensor(xa), Tensor(cond))._data
+
+    # ── the DiT-family host attention CrossAttentionBlock._attn (diffusion/models.py:123-133)
+    bq, bk, bv = rn(2, 3, 20, 16), rn(2, 3, 9, 16), rn(2, 3, 9, 16)
+    out["battn_q"], out["battn_k"], out["battn_v"] = bq, bk, bv
+    out["battn_o"] = M.CrossAttentionBlock._attn(None, bq, bk, bv)
 
     path = os.path.join(HERE, "golden.npz")
     np.savez_compressed(path, **out)

@@ -124,8 +124,8 @@ def test_drop_in_surface_signatures(ops):
 
 
 def test_out_of_scope_ops_raise(ops):
-    with pytest.raises(NotImplementedError, match="dev_layer_norm"):
-        ops.dev_layer_norm(None, None, None)
+    with pytest.raises(NotImplementedError, match="dev_rms_norm"):
+        ops.dev_rms_norm(None, None, None)
     with pytest.raises(AttributeError):
         ops.definitely_not_an_op
 

@@ -167,3 +167,18 @@ def test_flash_allowance_covers_flips_only():
     # a change larger than the allowance still fails the check
     bad = ref + np.float32(0.05)
     assert not O.elementwise_rel_check(bad, ref, allowance=a)[0]
+
+
+def test_layer_norm_and_adaln_match_reference_golden(golden):
+    """LayerNorm / AdaLayerNorm restatements against the reference's own
+    modules (B = 1, where its broadcast of the modulation is per sample)."""
+    x, g, b = golden["adaln_x"], golden["adaln_gamma"], golden["adaln_beta"]
+    np.testing.assert_array_equal(O.layer_norm(x, g, b), golden["adaln_ln"])
+    params = O.linear(golden["adaln_cond"], golden["adaln_w"], golden["adaln_b"])
+    np.testing.assert_array_equal(params, golden["adaln_params"])
+    np.testing.assert_array_equal(O.ada_layer_norm(x, params, g, b), golden["adaln_y"])
+
+
+def test_block_attention_matches_reference_golden(golden):
+    o = O.block_attention(golden["battn_q"], golden["battn_k"], golden["battn_v"])
+    np.testing.assert_array_equal(o, golden["battn_o"])
