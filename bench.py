@@ -247,6 +247,8 @@ def _cpu_stack_sample(budget_s: float, rows: int = 128, layers: int = 30):
     tok_s = rows / (best * layers)
     what = (f"one DiT layer for {rows} query tokens (linears + attention over {TOKENS} keys, "
             f"30 heads), fp32 NumPy; tokens/s extrapolated to {layers} layers; best of {n}; {cores} threads")
+    _cpu_stack_sample.last = {"extrapolated": True, "sample_rows": rows, "sample_layers": 1,
+                              "sample_s": best, "extrapolated_to": f"{M_TOTAL} tokens x {layers} layers"}
     return tok_s, what, cores
 
 
@@ -265,13 +267,16 @@ def run_reference_arm(args, dist):
             v, sample, _ = _cpu_stack_sample(0.0)
             vals.append(v)
         value = sum(vals) / len(vals)
+        ext = dict(_cpu_stack_sample.last)
         line = {"impl": "reference", "metric": _metric(args.workload), "value": value,
                 "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": M_TOTAL / value * 1e3,
+                # ms_per_step is the extrapolated full forward; each step ran the sample only
+                "extrapolated": True, "sample_ms_per_step": ext["sample_s"] * 1e3,
                 "higher_is_better": True, "dtype": "f32", "data": "synthetic",
                 "config": _config(args, 1),
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                 "sample": sample},
+                                 "sample": sample, **ext},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -317,6 +322,8 @@ def _config(args, world):
     if args.workload == "dit_stack":
         fused = os.environ.get("SF_ATTN_FUSED", "1") != "0"
         attn = "fused attention" if fused else f"unfused attention, query chunks of {args.chunk}"
+        if args.adaln:
+            attn += ", adaptive LayerNorms (beyond config 5)"
         return {"workload": f"dit_stack (config 5): {args.layers} layers, 30 heads x 64, {attn}",
                 "tokens": M_TOTAL, "hidden": HIDDEN, "global_batch": BATCH, "seq_len": TOKENS,
                 "layers": args.layers, "parallelism": f"token-shard{world}",
@@ -418,7 +425,7 @@ def run_gpu_arm(args, dist):
                     "sf_comm_split")
             kv_comm = kp.value
         stack = dit.DitStack(plan, HIDDEN, 30, args.layers, dev, chunk=args.chunk, seed=7,
-                             kv_comm=kv_comm, world_comm=comm)
+                             kv_comm=kv_comm, world_comm=comm, adaln=args.adaln)
         x_full = ops._alloc((M_TOTAL, HIDDEN), bf, dev)
         E.check(lib.sf_fill_normal(C.c_void_p(x_full.ptr), 2, M_TOTAL * HIDDEN, 11, 0.0, 1.0, None),
                 "sf_fill_normal")
@@ -637,6 +644,14 @@ def run_gpu_arm(args, dist):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, cores = cpu_reference_sample(args.workload, budget_s=args.cpu_budget)
         cpu = {"value": v, "unit": _unit(args.workload), "cores": cores, "kind": "port", "sample": sample}
+        if args.workload == "dit_stack":
+            cpu.update(_cpu_stack_sample.last)
+
+    gemm_suite = None
+    if rank == 0 and world == 1 and args.workload == "dit_stack" and not args.no_gemm_suite:
+        stack = None
+        ops.empty_cache()
+        gemm_suite = run_gemm_suite(lib, E, C, ops, dev, stream, l2_flush)
 
     if comm is not None:
         E.stream_sync(stream)
@@ -664,8 +679,197 @@ def run_gpu_arm(args, dist):
             "clocks": clocks.summary(),
             "device_error_word": err,
             "wall_s_timed": t_wall,
+            "gemm": gemm_suite,
         }
         print(json.dumps(line), flush=True)
+
+
+def _traffic(key):
+    """DRAM bytes per launch of a profiled kernel (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f).get(key)
+        return t.get("bytes_per_launch") if isinstance(t, dict) else t
+    except Exception:
+        return None
+
+
+def run_gemm_suite(lib, E, C, ops, dev, stream, l2_flush):
+    """The GEMM half of the benchmark metric, measured in the same run as the
+    DiT stack (rank 0, one GPU): config 1 (fp32 linear + SiLU), config 2
+    (square NT GEMM 8192^3 and 16384^3 in bf16, fp16 and fp32/3xTF32),
+    config 3 (skinny-M linears, HBM GB/s by CUDA graph replay over four
+    rotating weight copies) and config 4 (the four DiT block linears at
+    M = 35552).  Each record carries its CUDA-event time and its roofline
+    against MEASURED_PEAKS.json; the suite's own SM clock record is beside
+    them."""
+    hbm, burst, sustained, src = _peaks()
+    recs = []
+
+    def fill(t, std):
+        E.check(lib.sf_fill_normal(C.c_void_p(t.ptr), E.dtype_code(t.dtype), t.numel, 5 + len(recs),
+                                   0.0, float(std), C.c_void_p(stream)), "sf_fill_normal")
+
+    def timed(fn, reps, flush=True):
+        """Mean CUDA-event time (ms) of `fn` over `reps` calls after 2 warm-ups."""
+        for _ in range(2):
+            fn()
+        t = EventTimer(lib, stream)
+        for _ in range(reps):
+            if flush:
+                l2_flush()
+            t.start("x")
+            fn()
+            t.stop("x")
+        E.stream_sync(stream)
+        v = t.collect()["x"]
+        return sum(v) / len(v)
+
+    def tensor_rec(config, name, flops, ms, peak_basis, key, tensor_flops=None):
+        tf = flops / (ms / 1e3) / 1e12
+        tfl = (tensor_flops or flops) / (ms / 1e3) / 1e12
+        recs.append({"config": config, "name": name, "value": tf, "unit": "TFLOP/s", "ms": ms,
+                     "roofline": {"bound": "tensor", "achieved": tfl, "peak": peak_basis,
+                                  "unit": "TFLOP/s", "frac": tfl / peak_basis,
+                                  "peak_source": f"{src} burst bf16 (dense)",
+                                  "traffic": _traffic(key)}})
+
+    with ClockSampler([dev]) as clocks:
+        # config 2: square NT GEMMs, operands ~N(0,1)/sqrt(K), inputs > L2
+        for n in (8192, 16384):
+            for dt in ("bf16", "f16", "f32"):
+                npdt = {"bf16": E.bfloat16, "f16": np.float16, "f32": np.float32}[dt]
+                code = E.dtype_code(npdt)
+                a, b = ops._alloc((n, n), npdt, dev), ops._alloc((n, n), npdt, dev)
+                c = ops._alloc((n, n), npdt, dev)
+                fill(a, 1.0 / math.sqrt(n))
+                fill(b, 1.0 / math.sqrt(n))
+
+                def g(a=a, b=b, c=c, n=n, code=code):
+                    E.gemm(n, n, n, a.ptr, n, 0, b.ptr, n, 1, c.ptr, n, code, code, device=dev,
+                           stream=stream)
+                ms = timed(g, 3 if n == 16384 else 5)
+                fl = 2.0 * n ** 3
+                if dt == "f32":
+                    # 3xTF32: three tf32 products per fp32 product; the dense
+                    # tf32 tensor rate is half the bf16 rate
+                    tensor_rec("2", f"square {n}^3 NT fp32 (3xTF32)", fl, ms, burst / 2,
+                               f"square_{n}_f32", tensor_flops=3 * fl)
+                else:
+                    tensor_rec("2", f"square {n}^3 NT {dt}", fl, ms, burst, f"square_{n}_{dt}")
+                del a, b, c
+                ops.empty_cache()
+        # config 1: fp32 linear 512x1024 -> 4096 + SiLU (3xTF32), L2-resident operands
+        x, w, bb = (ops._alloc(s_, np.float32, dev) for s_ in ((512, 1024), (4096, 1024), (4096,)))
+        y = ops._alloc((512, 4096), np.float32, dev)
+        fill(x, 1.0)
+        fill(w, 1.0 / 32 / math.sqrt(3))
+        fill(bb, 1.0 / 32 / math.sqrt(3))
+        epi = E.make_epilogue(bias_ptr=bb.ptr, bias_dt=E.DT_F32, act=1)
+        ms = timed(lambda: E.gemm(512, 4096, 1024, x.ptr, 1024, 0, w.ptr, 1024, 1, y.ptr, 4096,
+                                  E.DT_F32, E.DT_F32, epi=epi, device=dev, stream=stream), 20,
+                   flush=False)
+        tensor_rec("1", "linear fp32 512x1024->4096 + SiLU (3xTF32)", 2.0 * 512 * 1024 * 4096, ms,
+                   burst / 2, "config1_f32", tensor_flops=3 * 2.0 * 512 * 1024 * 4096)
+        recs[-1]["l2"] = "operands L2-resident (27 MB); launch-inclusive event time"
+        del x, w, bb, y
+        # config 4: the four DiT block linears at M = 35552 (bf16)
+        from scaffolding_b200 import dit
+        blk = dit.DitLinears(_dit_weights_np(), M_TOTAL, dev)
+        xb = ops._alloc((M_TOTAL, HIDDEN), E.bfloat16, dev)
+        fill(xb, 1.0)
+        kt = EventTimer(lib, stream)
+        blk.run(xb.ptr, stream=stream)
+        for _ in range(3):
+            l2_flush()
+            blk.run(xb.ptr, stream=stream, timer=kt)
+        E.stream_sync(stream)
+        per = {k: sum(v) / len(v) for k, v in kt.collect().items()}
+        fl = {"qkv": 6.0, "out": 2.0, "up": 8.0, "down": 8.0}
+        for k in ("qkv", "out", "up", "down"):
+            tensor_rec("4", f"DiT block {k} M={M_TOTAL}", fl[k] * M_TOTAL * HIDDEN * HIDDEN, per[k],
+                       burst, f"dit_block_{k}")
+        tensor_rec("4", f"DiT block, four linears M={M_TOTAL}", dit.block_flops(M_TOTAL),
+                   sum(per.values()), burst, "dit_block")
+        del blk, xb
+        ops.empty_cache()
+        # the adaptive LayerNorm in front of the QKV / FFN-up GEMMs (bandwidth)
+        xn_in = ops._alloc((M_TOTAL, HIDDEN), E.bfloat16, dev)
+        xn_out = ops._alloc((M_TOTAL, HIDDEN), E.bfloat16, dev)
+        prm = ops._alloc((BATCH, 2 * HIDDEN), E.bfloat16, dev)
+        fill(xn_in, 1.0)
+        fill(prm, 0.1)
+
+        def norm():
+            E.check(lib.sf_layernorm_modulate(M_TOTAL, HIDDEN, C.c_void_p(xn_in.ptr), E.DT_BF16,
+                                              HIDDEN, None, None, 1e-5, C.c_void_p(prm.ptr),
+                                              E.DT_BF16, 2 * HIDDEN, TOKENS, C.c_void_p(xn_out.ptr),
+                                              E.DT_BF16, HIDDEN, C.c_void_p(stream)),
+                    "sf_layernorm_modulate")
+        ms = timed(norm, 10)
+        nbytes = 2.0 * 2 * M_TOTAL * HIDDEN + 2.0 * BATCH * 2 * HIDDEN
+        gbs = nbytes / (ms / 1e3) / 1e9
+        recs.append({"config": "f3", "name": f"LayerNorm + adaLN modulation {M_TOTAL}x{HIDDEN} bf16",
+                     "value": gbs, "unit": "GB/s", "ms": ms,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                  "frac": gbs / hbm, "algorithmic_bytes_per_launch": nbytes,
+                                  "peak_source": f"{src} HBM copy",
+                                  "traffic": _traffic("layernorm_modulate")}})
+        del xn_in, xn_out, prm
+        # config 3: skinny-M linears, K = 4096, bias + GELU, graph replay over
+        # four rotating weight copies (4 x 34-90 MB > L2)
+        for N in (4096, 11008):
+            Ws = [ops._alloc((N, 4096), E.bfloat16, dev) for _ in range(4)]
+            for W_ in Ws:
+                fill(W_, 0.02)
+            bias = ops._alloc((N,), E.bfloat16, dev)
+            fill(bias, 0.02)
+            epi3 = E.make_epilogue(bias_ptr=bias.ptr, bias_dt=E.DT_BF16, act=2)
+            for Ms in (1, 8, 64, 226):
+                xs = ops._alloc((Ms, 4096), E.bfloat16, dev)
+                ys = ops._alloc((Ms, N), E.bfloat16, dev)
+                fill(xs, 1.0)
+
+                def lin(W_, xs=xs, ys=ys, Ms=Ms, N=N):
+                    E.gemm(Ms, N, 4096, xs.ptr, 4096, 0, W_.ptr, 4096, 1, ys.ptr, N, E.DT_BF16,
+                           E.DT_BF16, epi=epi3, device=dev, stream=stream)
+                lin(Ws[0])  # sizes the workspace before the capture
+                E.stream_sync(stream)
+                gp = C.c_void_p()
+                E.check(lib.sf_graph_begin(C.c_void_p(stream)), "sf_graph_begin")
+                for W_ in Ws:
+                    lin(W_)
+                E.check(lib.sf_graph_end(C.c_void_p(stream), C.byref(gp)), "sf_graph_end")
+                reps = 25
+                for _ in range(3):
+                    E.check(lib.sf_graph_launch(gp, C.c_void_p(stream)), "sf_graph_launch")
+                t = EventTimer(lib, stream)
+                t.start("g")
+                for _ in range(reps):
+                    E.check(lib.sf_graph_launch(gp, C.c_void_p(stream)), "sf_graph_launch")
+                t.stop("g")
+                E.stream_sync(stream)
+                ms = t.collect()["g"][0] / (reps * 4)
+                lib.sf_graph_destroy(gp)
+                nbytes = 2.0 * (N * 4096 + Ms * 4096 + N + Ms * N)
+                gbs = nbytes / (ms / 1e3) / 1e9
+                recs.append({"config": "3", "name": f"skinny M={Ms} K=4096 N={N} bias+GELU bf16",
+                             "value": gbs, "unit": "GB/s", "ms": ms,
+                             "tflops": 2.0 * Ms * N * 4096 / (ms / 1e3) / 1e12,
+                             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm,
+                                          "unit": "GB/s", "frac": gbs / hbm,
+                                          "frac_of_8tbs": gbs / 8000.0,
+                                          "algorithmic_bytes_per_launch": nbytes,
+                                          "peak_source": f"{src} HBM copy",
+                                          "traffic": _traffic(f"skinny_m{Ms}_n{N}")},
+                             "timing": "CUDA graph replay, 4 rotating weight copies"})
+                del xs, ys
+            del Ws, bias
+            ops.empty_cache()
+        time.sleep(0.25)
+    return {"records": recs, "clocks": clocks.summary(),
+            "timing": "CUDA events on the launching stream; 512 MiB L2 flush between timed calls "
+                      "(configs 2 and 4)"}
 
 
 def run_skinny_graph(args, dist, lib, E, C, stream, dev, step, Ms, N, K, copies):
@@ -730,6 +934,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--adaln", action="store_true",
+                    help="dit_stack: add the blocks' adaptive LayerNorms (not part of config 5)")
+    ap.add_argument("--no-gemm-suite", action="store_true",
+                    help="skip the configs 1-4 GEMM records of the default line")
     args = ap.parse_args()
     if args.size is None:
         args.size = {"dit_stack": 0, "dit_block": 0, "square": 8192, "skinny": 8}[args.workload]
