@@ -310,12 +310,13 @@ def run_reference_arm(args, dist):
 def _metric(workload):
     return {"dit_stack": "DiT-stack tokens/s (30-layer forward, bf16, token-sharded)",
             "dit_block": "GEMM TFLOP/s (DiT-block linears, bf16, M-sharded)",
-            "square": "GEMM TFLOP/s (square NT GEMM, bf16)",
+            "square": "GEMM TFLOP/s (square NT GEMM)",
+            "norm": "LayerNorm + adaLN modulation HBM GB/s (35552 x 1920, bf16)",
             "skinny": "GEMM TFLOP/s (skinny-M linear, bf16)"}[workload]
 
 
 def _unit(workload):
-    return "tokens/s" if workload == "dit_stack" else "TFLOP/s"
+    return {"dit_stack": "tokens/s", "norm": "GB/s"}.get(workload, "TFLOP/s")
 
 
 def _config(args, world):
@@ -332,8 +333,11 @@ def _config(args, world):
         return {"workload": "dit_block_linears (config 4)", "tokens": M_TOTAL, "hidden": HIDDEN,
                 "global_batch": BATCH, "seq_len": TOKENS, "parallelism": f"m-shard{world}",
                 "l2": "flushed between steps (512 MiB write)"}
+    if args.workload == "norm":
+        return {"workload": f"LayerNorm + adaLN modulation {M_TOTAL}x{HIDDEN} bf16 (section 8 f3)",
+                "parallelism": f"replicas{world}", "l2": "flushed between steps (512 MiB write)"}
     if args.workload == "square":
-        return {"workload": f"square NT GEMM {args.size}^3 (config 2)",
+        return {"workload": f"square NT GEMM {args.size}^3 {args.dtype} (config 2)",
                 "parallelism": f"replicas{world}", "l2": "flushed between steps (512 MiB write)"}
     return {"workload": f"skinny linear M={args.size} K=4096 N={args.skinny_n} (config 3)",
             "parallelism": f"replicas{world}", "l2": "flushed between steps (512 MiB write)"}
@@ -467,24 +471,50 @@ def run_gpu_arm(args, dist):
         in_ptr_host = None
     elif args.workload == "square":
         n = args.size
-        rng = np.random.default_rng(0)
-        s = np.float32(1.0 / math.sqrt(n))
-        a = ops.gputensor_from_numpy((rng.standard_normal((n, n), dtype=np.float32) * s).astype(bf), dev)
-        b = ops.gputensor_from_numpy((rng.standard_normal((n, n), dtype=np.float32) * s).astype(bf), dev)
-        c = ops._alloc((n, n), bf, dev)
+        sdt = {"bf16": bf, "f16": np.float16, "f32": np.float32}[args.dtype]
+        scode = E.dtype_code(sdt)
+        a, b, c = (ops._alloc((n, n), sdt, dev) for _ in range(3))
+        for i, t in enumerate((a, b)):
+            E.check(lib.sf_fill_normal(C.c_void_p(t.ptr), scode, n * n, 21 + i, 0.0,
+                                       1.0 / math.sqrt(n), None), "sf_fill_normal")
         flops_rank = 2.0 * n ** 3
         flops_job = flops_rank * world
+        esz = np.dtype(sdt).itemsize
 
         def step(timer=None, x_ptr=None):
             if timer:
                 timer.start("gemm")
-            E.gemm(n, n, n, a.ptr if x_ptr is None else x_ptr, n, 0, b.ptr, n, 1, c.ptr, n, 2, 2,
-                   device=dev, stream=stream)
+            E.gemm(n, n, n, a.ptr if x_ptr is None else x_ptr, n, 0, b.ptr, n, 1, c.ptr, n, scode,
+                   scode, device=dev, stream=stream)
             if timer:
                 timer.stop("gemm")
+        # 3xTF32 launches two operand-split kernels before the GEMM
+        launches_per_step = 3 if args.dtype == "f32" else 1
+        h2d_bytes = n * n * esz
+        d2h_bytes = n * n * esz
+    elif args.workload == "norm":
+        m, Cn = M_TOTAL, HIDDEN
+        xin = ops._alloc((m, Cn), bf, dev)
+        xout = ops._alloc((m, Cn), bf, dev)
+        prm = ops._alloc((BATCH, 2 * Cn), bf, dev)
+        for i, t in enumerate((xin, prm)):
+            E.check(lib.sf_fill_normal(C.c_void_p(t.ptr), 2, t.numel, 31 + i, 0.0, 1.0, None),
+                    "sf_fill_normal")
+        flops_rank = flops_job = 0.0
+        norm_bytes = 2.0 * 2 * m * Cn + 2.0 * BATCH * 2 * Cn
+
+        def step(timer=None, x_ptr=None):
+            if timer:
+                timer.start("norm")
+            E.check(lib.sf_layernorm_modulate(m, Cn, C.c_void_p(xin.ptr if x_ptr is None else x_ptr),
+                                              2, Cn, None, None, 1e-5, C.c_void_p(prm.ptr), 2,
+                                              2 * Cn, TOKENS, C.c_void_p(xout.ptr), 2, Cn,
+                                              C.c_void_p(stream)), "sf_layernorm_modulate")
+            if timer:
+                timer.stop("norm")
         launches_per_step = 1
-        h2d_bytes = n * n * 2
-        d2h_bytes = n * n * 2
+        h2d_bytes = m * Cn * 2
+        d2h_bytes = m * Cn * 2
     else:
         Ms, N, K = args.size, args.skinny_n, 4096
         rng = np.random.default_rng(0)
@@ -547,6 +577,8 @@ def run_gpu_arm(args, dist):
     tflops_job = value
     if args.workload == "dit_stack":
         value = M_TOTAL * args.steps / job_s
+    if args.workload == "norm":
+        value = norm_bytes * world * args.steps / job_s / 1e9
 
     # roofline of the dominant kernel
     hbm, burst, sustained, src = _peaks()
@@ -558,6 +590,11 @@ def run_gpu_arm(args, dist):
             "frac": achieved / peak, "kernel": "sf::gemm_tc_kernel (tcgen05)",
             "launch_ms_mean": gemm_ms / max(1, n_launch),
             "peak_source": f"{src} ({'sustained' if peak == sustained else 'burst'} bf16)"}
+    if args.workload == "norm":
+        gbs = norm_bytes * args.steps / (gemm_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                "kernel": "sf::layernorm_mod_vec_kernel", "algorithmic_bytes_per_launch": norm_bytes,
+                "launch_ms_mean": gemm_ms / max(1, n_launch), "peak_source": f"{src} HBM copy"}
     if stack is not None:
         totals = {k: sum(v) for k, v in kern_ms.items()}
         top = max(totals, key=totals.get)
@@ -588,7 +625,8 @@ def run_gpu_arm(args, dist):
             roof["frac"] = roof["achieved"] / peak
             roof["launch_ms_mean"] = ms_top
             if top == "attn":
-                roof["kernel"] = "sf::attention_fwd2_kernel (tcgen05, fused QK^T-softmax-PV, P in TMEM)"
+                roof["kernel"] = ("sf::attention_pp_kernel<AttnPpCfg<2, 64, 4>> (tcgen05, fused "
+                                  "QK^T-softmax-PV, two query tiles per CTA, P in TMEM)")
                 roof["algorithmic_flops_per_launch"] = fl
         roof["kernel_share"] = totals[top] / sum(totals.values())
         roof["top_kernel"] = top
@@ -611,12 +649,14 @@ def run_gpu_arm(args, dist):
         if args.workload == "dit_stack":
             src_ptr = x_full.ptr + x_off
         else:
-            src_ptr = (x.ptr if args.workload == "dit_block" else (a.ptr if args.workload == "square" else xs.ptr))
+            src_ptr = {"dit_block": lambda: x.ptr, "square": lambda: a.ptr,
+                       "norm": lambda: xin.ptr}.get(args.workload, lambda: xs.ptr)()
         E.memcpy(pin_in.ptr, src_ptr, h2d_bytes, 1, stream)
         if args.workload == "dit_stack":
             res_ptr = stack.y[(args.layers - 1) % 2].ptr
         else:
-            res_ptr = (block.y.ptr if args.workload == "dit_block" else (c.ptr if args.workload == "square" else y.ptr))
+            res_ptr = {"dit_block": lambda: block.y.ptr, "square": lambda: c.ptr,
+                       "norm": lambda: xout.ptr}.get(args.workload, lambda: y.ptr)()
         e2e_t = EventTimer(lib, stream)
         for _ in range(max(1, args.warmup // 2)):
             E.memcpy(dev_in.ptr, pin_in.ptr, h2d_bytes, 0, stream)
@@ -634,7 +674,9 @@ def run_gpu_arm(args, dist):
         E.stream_sync(stream)
         dist.barrier()
         e2e_s = dist.max(sum(e2e_t.collect()["e2e"]) / 1e3)
-        e2e_val = (M_TOTAL * args.steps / e2e_s) if args.workload == "dit_stack" else flops_job * args.steps / e2e_s / 1e12
+        e2e_val = ((M_TOTAL * args.steps / e2e_s) if args.workload == "dit_stack"
+                   else (norm_bytes * world * args.steps / e2e_s / 1e9) if args.workload == "norm"
+                   else flops_job * args.steps / e2e_s / 1e12)
         e2e = {"value": e2e_val, "unit": _unit(args.workload),
                "h2d_bytes_per_step": h2d_bytes * world, "d2h_bytes_per_step": d2h_bytes * world,
                "ms_per_step": e2e_s / args.steps * 1e3}
@@ -665,7 +707,8 @@ def run_gpu_arm(args, dist):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": job_s / args.steps * 1e3, "higher_is_better": True,
             "scaling": "strong" if args.workload.startswith("dit") else "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None,
+            "dtype": args.dtype if args.workload == "square" else "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": _config(args, world),
             "tflops": tflops_job,
@@ -926,7 +969,10 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="dit_stack", choices=["dit_stack", "dit_block", "square", "skinny"])
+    ap.add_argument("--workload", default="dit_stack",
+                    choices=["dit_stack", "dit_block", "square", "skinny", "norm"])
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16", "f32"],
+                    help="square workload: operand and output type (f32 = 3xTF32)")
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--skinny-n", type=int, default=11008)
     ap.add_argument("--chunk", type=int, default=2048, help="attention query chunk (dit_stack)")
@@ -940,7 +986,8 @@ def main():
                     help="skip the configs 1-4 GEMM records of the default line")
     args = ap.parse_args()
     if args.size is None:
-        args.size = {"dit_stack": 0, "dit_block": 0, "square": 8192, "skinny": 8}[args.workload]
+        args.size = {"dit_stack": 0, "dit_block": 0, "square": 8192, "skinny": 8,
+                     "norm": 0}[args.workload]
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()

@@ -176,6 +176,21 @@ def gputensor_to_device(gt: GpuTensor, target_dev: int) -> GpuTensor:
     return out
 
 
+def gputensor_astype(gt: GpuTensor, dtype) -> GpuTensor:
+    """Copy of ``gt`` converted to ``dtype`` on its device (fp32 / bf16 / fp16,
+    round to nearest even), e.g. fp32 weights stored as bf16 after upload.
+    New: the reference uploads fp32 only (``nn/layers.py:18-35``)."""
+    dt = np.dtype(dtype)
+    if dt == gt.dtype:
+        return gt
+    out = _alloc(gt.shape, dt, gt.device_id)
+    if gt.numel:
+        with E.on_device(gt.device_id):
+            E.unary(gt.ptr, E.dtype_code(gt.dtype), out.ptr, E.dtype_code(dt), gt.numel, 1.0,
+                    ACT_NONE, device=gt.device_id)
+    return out
+
+
 def numpy_to_gpu(arr: np.ndarray, stream=None):
     gt = gputensor_from_numpy(arr)
     return gt.buffer, arr.shape, arr.dtype

@@ -3,16 +3,9 @@
 // TMA descriptors, kernel choice, the split dispatch of the last wave and
 // its workspace.
 //
-// Kernels (attention_pp.cuh, attention.cuh):
-//   attention_pp_kernel     one CTA per SM with NT 128-query tiles sharing
-//                           each K/V block: NT = 4 with 64-key blocks
-//                           (default), NT = 2 with 128-key blocks
-//                           (SF_ATTN_KERNEL=3);
-//   attention_fwd2_kernel   four CTAs per SM, one 128-query tile each,
-//                           64-key blocks (SF_ATTN_KERNEL=2).
-// Both keep S and P in TMEM and O in a TMEM accumulator, with integer row
-// bases raised lazily, and support the key skips and partial modes of
-// sf_attention_fwd_partial.
+// Kernel: attention_pp_kernel (attention_pp.cuh) with two 128-row query tiles
+// per CTA and 64-key blocks (S and P in TMEM, O in a TMEM accumulator, integer
+// row bases raised lazily), plus attention_merge_kernel for the split pieces.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -29,82 +22,21 @@
 namespace sf {
 namespace {
 
-using Attn2CfgV6 = Attn2Cfg<64, 2, true>;
-using AttnPp2 = AttnPpCfg<2, 128, 4>;  // kernel 3: two query tiles, 128-key blocks
-using AttnPp4 = AttnPpCfg<4, 64, 6>;   // kernel 4: four query tiles, 64-key blocks
-using AttnPp5 = AttnPpCfg<2, 64, 4>;   // kernel 5: two query tiles, 64-key blocks, 2 CTAs/SM
-
-// Which kernel runs: 2 (attention_fwd2_kernel), 3 or 4 (attention_pp_kernel
-// with two or four query tiles per CTA).
-int attn_kernel() {
-  const int k = env_int("SF_ATTN_KERNEL", 5);
-  return (k >= 2 && k <= 5) ? k : 5;
-}
-int attn_unit_rows(int kernel) {
-  return kernel == 2 ? kAttnBlock : kernel == 3 ? AttnPp2::ROWS : kernel == 5 ? AttnPp5::ROWS : AttnPp4::ROWS;
-}
-int attn_key_block(int kernel) {
-  return kernel == 2 ? Attn2CfgV6::KB : kernel == 3 ? AttnPp2::KB : kernel == 5 ? AttnPp5::KB : AttnPp4::KB;
-}
-int attn_ctas_per_sm(int kernel) {
-  return kernel == 2 ? Attn2CfgV6::MIN_BLOCKS : kernel == 3 ? AttnPp2::MIN_BLOCKS
-         : kernel == 5 ? AttnPp5::MIN_BLOCKS : AttnPp4::MIN_BLOCKS;
-}
+// Two 128-row query tiles per CTA, 64-key blocks, 4-stage K/V ring: 256 TMEM
+// columns and ~96 KB of shared memory, two CTAs per SM.
+using AttnCfg = AttnPpCfg<2, 64, 4>;
 
 template <bool BF16>
-int32_t launch_fwd2(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                    const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
+                         const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
   static bool attr_set[64] = {false};
   if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_fwd2_kernel<BF16, Attn2CfgV6, 0>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2CfgV6::BYTES));
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_pp_kernel<BF16, AttnCfg>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg::BYTES));
     attr_set[device] = true;
   }
-  attention_fwd2_kernel<BF16, Attn2CfgV6, 0><<<grid, kAttnThreads, Attn2CfgV6::BYTES, s>>>(mq, mk, mv, a);
+  attention_pp_kernel<BF16, AttnCfg><<<grid, AttnCfg::THREADS, AttnCfg::BYTES, s>>>(mq, mk, mv, a);
   return SF_OK;
-}
-
-template <bool BF16, class Cfg, int EMU>
-int32_t launch_pp_emu(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                      const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
-  static bool attr_set[64] = {false};
-  if (device < 64 && !attr_set[device]) {
-    SF_CUDA_TRY(cudaFuncSetAttribute(attention_pp_kernel<BF16, Cfg, EMU>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::BYTES));
-    attr_set[device] = true;
-  }
-  attention_pp_kernel<BF16, Cfg, EMU><<<grid, Cfg::THREADS, Cfg::BYTES, s>>>(mq, mk, mv, a);
-  return SF_OK;
-}
-
-template <bool BF16, class Cfg>
-int32_t launch_pp(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                  const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
-  switch (env_int("SF_ATTN_EMU", 0)) {
-    case 1: return launch_pp_emu<BF16, Cfg, 1>(grid, mq, mk, mv, a, s, device);
-    case 2: return launch_pp_emu<BF16, Cfg, 2>(grid, mq, mk, mv, a, s, device);
-    case 3: return launch_pp_emu<BF16, Cfg, 3>(grid, mq, mk, mv, a, s, device);
-    default: return launch_pp_emu<BF16, Cfg, 0>(grid, mq, mk, mv, a, s, device);
-  }
-}
-
-template <bool BF16>
-int32_t launch_kernel(int kernel, const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                      const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
-  if (kernel == 2) return launch_fwd2<BF16>(grid, mq, mk, mv, a, s, device);
-  if (kernel == 3) return launch_pp<BF16, AttnPp2>(grid, mq, mk, mv, a, s, device);
-  if (kernel == 5) return launch_pp<BF16, AttnPp5>(grid, mq, mk, mv, a, s, device);
-  return launch_pp<BF16, AttnPp4>(grid, mq, mk, mv, a, s, device);
-}
-
-template <bool BF16>
-void launch_merge(int rows, unsigned n, const AttnArgs& a, cudaStream_t s) {
-  if (rows == kAttnBlock)
-    attention_merge_kernel<BF16, kAttnBlock><<<n, kAttnBlock, 0, s>>>(a);
-  else if (rows == AttnPp2::ROWS)
-    attention_merge_kernel<BF16, AttnPp2::ROWS><<<n, AttnPp2::ROWS, 0, s>>>(a);
-  else
-    attention_merge_kernel<BF16, AttnPp4::ROWS><<<n, AttnPp4::ROWS, 0, s>>>(a);
 }
 
 // Split dispatch plan (see AttnArgs::split_first).  U units on P resident
@@ -117,6 +49,7 @@ struct AttnSplit {
 };
 AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
   AttnSplit sp;
+  // Test hook: SF_ATTN_SPLIT=0 keeps the one-CTA-per-unit grid.
   if (env_int("SF_ATTN_SPLIT", 1) == 0 || slots <= 0 || nkb < 2) return sp;
   const int64_t full = units / slots, rem = units % slots;
   if (rem == 0) return sp;
@@ -212,9 +145,8 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
   if (st != SF_OK) return st;
   if (dev->cc_major != 10) return fail(SF_ERR_UNSUPPORTED, "fused attention needs sm_100");
   const CUtensorMapDataType dt = tma_dtype(dtype);
-  const int kernel = attn_kernel();
-  const int rows = attn_unit_rows(kernel);
-  const uint32_t kb = static_cast<uint32_t>(attn_key_block(kernel));
+  const int rows = AttnCfg::ROWS;
+  const uint32_t kb = static_cast<uint32_t>(AttnCfg::KB);
   CUtensorMap mq, mk, mv;
   MapSpec sq{q, 2, dt, static_cast<uint64_t>(head_dim), static_cast<uint64_t>(q_len),
              static_cast<uint64_t>(heads), static_cast<uint64_t>(batch), ldq, head_dim, q_bstride,
@@ -253,7 +185,7 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
   AttnSplit sp;
   if (part_mode != 1)
     sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
-                         attn_ctas_per_sm(kernel) * dev->sm_count,
+                         AttnCfg::MIN_BLOCKS * dev->sm_count,
                          static_cast<int>(ceil_div(kv_len, static_cast<int>(kb))));
   // Held until the launches are queued, so that no other thread's call on the
   // same stream regrows (frees) the workspace in between.
@@ -280,16 +212,16 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
       grid = dim3(static_cast<unsigned>(sp.split_first + sp.pieces), 1, 1);
     }
   }
-  st = dtype == kBF16 ? launch_kernel<true>(kernel, grid, mq, mk, mv, a, s, device)
-                      : launch_kernel<false>(kernel, grid, mq, mk, mv, a, s, device);
+  st = dtype == kBF16 ? launch_attention<true>(grid, mq, mk, mv, a, s, device)
+                      : launch_attention<false>(grid, mq, mk, mv, a, s, device);
   if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
   if (a.split_first >= 0) {
     const unsigned n_split = static_cast<unsigned>(sp.pieces / sp.split_k);
     if (dtype == kBF16)
-      launch_merge<true>(rows, n_split, a, s);
+      attention_merge_kernel<true, AttnCfg::ROWS><<<n_split, AttnCfg::ROWS, 0, s>>>(a);
     else
-      launch_merge<false>(rows, n_split, a, s);
+      attention_merge_kernel<false, AttnCfg::ROWS><<<n_split, AttnCfg::ROWS, 0, s>>>(a);
     SF_CUDA_TRY(cudaGetLastError());
   }
   return SF_OK;
@@ -324,12 +256,11 @@ extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32
   DeviceInfo* dev = nullptr;
   int32_t st = current_device_info(&dev, nullptr);
   if (st != SF_OK) return st;
-  const int kernel = attn_kernel();
   *count = 1;
   if (part_mode != 1) {
-    const int64_t units = ceil_div(q_len, attn_unit_rows(kernel)) * heads * batch;
-    const AttnSplit sp = attn_split_plan(units, attn_ctas_per_sm(kernel) * dev->sm_count,
-                                         static_cast<int>(ceil_div(kv_len, attn_key_block(kernel))));
+    const int64_t units = ceil_div(q_len, AttnCfg::ROWS) * heads * batch;
+    const AttnSplit sp = attn_split_plan(units, AttnCfg::MIN_BLOCKS * dev->sm_count,
+                                         static_cast<int>(ceil_div(kv_len, AttnCfg::KB)));
     if (sp.split_first >= 0) *count = 2;
   }
   return SF_OK;

@@ -3,19 +3,22 @@
 //
 //   O[b, :, h] = softmax(scale * Q[b, :, h] K[b, :, h]^T) V[b, :, h]
 //
-// One CTA per SM (all 512 TMEM columns) works on a unit of NT * 128 query
-// rows of one (head, batch): tiles t = 0 .. NT-1 that share every block of KB
-// keys.  NT * 4 + 2 warps:
+// A CTA works on a unit of NT * 128 query rows of one (head, batch): tiles
+// t = 0 .. NT-1 that share every block of KB keys.  NT * 4 + 2 warps:
 //   warps 4t .. 4t+3   softmax of tile t, one thread per query row (TMEM lane);
 //   warp 4 NT          TMA producer: the Q tiles once, then K and V blocks of
 //                      KB keys into a KV_STAGES-deep ring (K-major 128B-swizzled
 //                      tiles; V's tile is the MN-major B operand of P.V);
 //   warp 4 NT + 1      TMEM owner and MMA issuer.
 // TMEM: S_t (fp32 scores) in columns [t KB, (t+1) KB), O_t (fp32 output
-// accumulator) in [NT KB + 64 t, NT KB + 64 (t+1)).  The default NT = 4,
-// KB = 64 uses all 512 columns: 16 softmax warps per SM (four per scheduler,
-// enough to keep the transcendental unit fed), one K/V stream and one MMA
-// thread per SM for 512 query rows.
+// accumulator) in [NT KB + 64 t, NT KB + 64 (t+1)); a CTA allocates 256 or
+// 512 columns, so two or one CTAs share an SM.  The engine's configuration
+// is NT = 2, KB = 64: 256 columns and ~96 KB of shared memory, two CTAs
+// (four tiles, sixteen softmax warps) per SM, each K/V block loaded once
+// for two tiles.  Measured on B200 it is the fastest of the shapes tried:
+// one CTA per SM with two tiles of 128-key blocks (eight softmax warps per
+// SM) leaves the softmax warps latency-bound, and four tiles per CTA queue
+// behind the single MMA thread.
 //
 // For each tile t and key block j the MMA thread issues
 //     O_t += P_t(j-1) V(j-1),  S_t(j) = Q_t K(j)^T
@@ -37,9 +40,7 @@
 // 2^(m_old - m_new) (warp-collective load, multiply, store; factor 1 on the
 // warp's other rows).  Because m is an integer, the 16-bit rounding of
 // p = 2^(c s - m) does not depend on which base is in force (a change of
-// base is an exact power-of-two scale).  EMU of every 8 exp2 pairs of a full
-// block are computed on the FMA pipe (exp2_poly3) instead of the
-// transcendental unit.
+// base is an exact power-of-two scale).
 //
 // Tiles of a unit that hold no query rows (past q_len) are skipped.  Keys
 // past kv_len (TMA zero-fills them) and skipped keys are masked to p = 0;
@@ -82,35 +83,6 @@ struct AttnPpCfg {
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-// 2^x for a pair of arguments on the FMA pipe: 2^x = 2^n * 2^f with
-// n = round(x) (the 1.5 * 2^23 rounding trick) and f = x - n in [-0.5, 0.5];
-// 2^f from a degree-3 polynomial with p(0) = 1 whose coefficients were fitted
-// to 2^f on [-0.5, 0.5] by iteratively reweighted least squares (Lawson's
-// minimax method, relative error below 1.02e-4, under the 2^-9 rounding of
-// the 16-bit P it feeds); n is added to the exponent field.  With
-// j = x + 1.5 * 2^23, the bits of j are 0x4B400000 + n, and
-// (0x4B400000 << 23) vanishes mod 2^32, so adding (bits(j) << 23) adds n to
-// the exponent.  Arguments are clamped at -127 (results below 2^-126 are not
-// needed: they round to 0 in the 16-bit P and vanish against the row sum).
-__device__ __forceinline__ void exp2_poly3(float& y0, float& y1, float x0, float x1) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c1 = 0.6932829022407532f, c2 = 0.24221095442771912f, c3 = 0.05500892922282219f;
-  x0 = fmaxf(x0, -127.0f);
-  x1 = fmaxf(x1, -127.0f);
-  float j0 = x0, j1 = x1;
-  add2(j0, j1, kRound, kRound);
-  float n0 = j0, n1 = j1;
-  add2(n0, n1, -kRound, -kRound);
-  float f0 = x0, f1 = x1;
-  add2(f0, f1, -n0, -n1);
-  float p0, p1;
-  fma2(p0, p1, f0, f1, c3, c3, c2, c2);
-  fma2(p0, p1, p0, p1, f0, f1, c1, c1);
-  fma2(p0, p1, p0, p1, f0, f1, 1.0f, 1.0f);
-  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(j0) << 23));
-  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(j1) << 23));
-}
-
 // Work of one CTA: unit (query rows [qb * ROWS, +ROWS) of head h, batch b)
 // and its key blocks, [k0, e0) then [s1, k1) ([e0, s1) skipped), KB keys each.
 template <int KB>
@@ -152,7 +124,7 @@ __device__ __forceinline__ PpWork<KB> pp_work(const AttnArgs& p) {
   return w;
 }
 
-template <bool BF16, class Cfg, int EMU>
+template <bool BF16, class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     attention_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -404,12 +376,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
           for (int i = 0; i < 32; i += 2) {
             float x0, x1;
             fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
-            if (((i >> 1) & 7) < EMU) {
-              exp2_poly3(pv[i], pv[i + 1], x0, x1);
-            } else {
-              pv[i] = ex2_approx(x0);
-              pv[i + 1] = ex2_approx(x1);
-            }
+            pv[i] = ex2_approx(x0);
+            pv[i + 1] = ex2_approx(x1);
             add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
           }
         } else {

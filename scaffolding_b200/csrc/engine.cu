@@ -156,14 +156,13 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     if (p.K >= kPromoteMinK && pl.bn <= 128) pl.promote = true;
     return pl;
   }
-  // The balanced GEMV kernel (K % 256 == 0) for M <= SF_GEMV_MAX_M (default 2;
-  // from M = 3 the swap-AB tensor-core path streams the weights faster on
-  // B200), the plain GEMV kernel for M <= 4 otherwise.
-  const int gemv_max_m = (p.K % 256 == 0 && env_int("SF_GEMV_SEG", 1))
-                             ? std::min(8, env_int("SF_GEMV_MAX_M", 2))
-                             : 4;
+  // The balanced GEMV kernel (K % 256 == 0) for M <= 2 (from M = 3 the
+  // swap-AB tensor-core path streams the weights faster on B200), the plain
+  // GEMV kernel for M <= 4 otherwise.  Test hook: SF_GEMV_MAX_M (<= 8) widens
+  // the balanced kernel's range so its code paths for M up to 8 are covered.
+  const int gemv_max_m = (p.K % 256 == 0) ? std::min(8, env_int("SF_GEMV_MAX_M", 2)) : 4;
   if (batch == 1 && p.M <= gemv_max_m && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
-      ovr != SF_KERNEL_TCGEN05 && ovr != SF_KERNEL_TCGEN05_1CTA && env_int("SF_GEMV", 1)) {
+      ovr != SF_KERNEL_TCGEN05 && ovr != SF_KERNEL_TCGEN05_1CTA) {
     // Decode-style shapes: a pure weight stream, served by the GEMV kernel.
     pl.kind = kPlanGemv;
     return pl;
@@ -171,7 +170,9 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   // Skinny M on B200 (graph-replayed, K = 4096): with k-balanced split-K the
   // swap-AB kernel (weights fill the 128-row MMA side) is fastest up to
   // M = 128, and at N = 4096 up to M = 256; wide outputs with M = 129..256
-  // run on CTA pairs holding every activation row in one pair tile.
+  // run on CTA pairs holding every activation row in one pair tile.  Test
+  // hooks: SF_SKINNY_PAIR=0 and SF_SKINNY_PAIR_MIN_M / _MIN_N move shapes
+  // between the two paths so that both are checked on every skinny shape.
   const int pair_min_m = env_int("SF_SKINNY_PAIR_MIN_M", 129);
   const int pair_min_n = env_int("SF_SKINNY_PAIR_MIN_N", 8192);
   if (batch == 1 && p.M <= 256 && p.M >= pair_min_m && p.N >= std::max(1024, pair_min_n) &&
@@ -191,7 +192,7 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
     const int64_t tiles = ceil_div(p.N, 128);
     const int64_t kb = ceil_div(p.K, 64);
     int64_t splits = 1;
-    if (env_int("SF_SWAP_BALANCE", 1) && kb >= 8) {  // tuning knob
+    if (kb >= 8) {
       // The weight stream is shared evenly only when every SM has the same
       // number of k-blocks: pick the split count s (>= 4 k-blocks per split)
       // minimising the busiest SM's k-blocks, ceil(tiles*s / SMs) * ceil(kb/s),
@@ -224,13 +225,11 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   pl.kind = kPlanTc;
   pl.bn = pick_bn(p.N);
   if (pl.bn < 64 && p.M > 4096) pl.bn = 64;
-  const int forced = env_int("SF_TILE_N", 0);  // tuning knob
-  if (forced == 64 || forced == 128 || forced == 192 || forced == 256) pl.bn = forced;
   // CTA pairs over 256-row tiles: a third less operand traffic per SM than
   // 1-CTA 128-row tiles.  Measured on B200 they win only for wide (BN = 256),
   // tall GEMMs (the DiT FFN-up shape); elsewhere the 1-CTA kernel is as fast
-  // or faster, so AUTO picks pairs for that class only.  SF_PAIR=1 forces
-  // pairs for every eligible GEMM, SF_PAIR=0 disables them.
+  // or faster, so AUTO picks pairs for that class only.  Test hook: SF_PAIR=1
+  // puts every eligible GEMM on the pair kernel (parity of its code paths).
   if (pl.bn >= 128 && p.M >= 1024 && p.K >= 256 && ovr != SF_KERNEL_TCGEN05_1CTA) {
     const int knob = env_int("SF_PAIR", -1);
     if (knob == 1 || (knob < 0 && pl.bn == 256 && p.N >= 4096 && p.M >= 16384)) pl.pair = true;
@@ -542,7 +541,7 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   const int64_t total = int64_t(a.m_tiles) * a.n_tiles * p.nb0 * p.nb1;
   if (total * pl.splits > INT32_MAX) return fail(SF_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
-  a.group_m = std::max(1, env_int("SF_GROUP_M", 8));  // raster group height (tuning knob)
+  a.group_m = 8;  // raster group height
   a.k_splits = pl.splits;
   a.kb_per_split = static_cast<int>(ceil_div(a.k_blocks, pl.splits));
   a.C = p.C;
@@ -561,16 +560,15 @@ static int32_t run_tc(const Problem& p, const Plan& pl, const DeviceInfo& dev, i
   a.ws_slice = 0;
   a.epi = to_epi(p.epi, p.out_dt);
   a.err = dev.err_word;
-  a.epi_sleep_ns = env_int("SF_EPI_SLEEP", 0);  // tuning knob
   a.a_box_rows = pl.pair ? pl.a_box_rows : 128;
   a.tma_store = 0;
-  // Programmatic dependent launch of the 1-CTA kernel (tuning knobs: SF_PDL=0
-  // off; SF_PDL_PF_TC weight k-blocks prefetched before the wait, skinny only).
-  a.pdl = (!pl.pair && env_int("SF_PDL", 1)) ? 1 : 0;
-  a.pdl_pf = (a.pdl && p.M <= 256) ? std::max(0, env_int("SF_PDL_PF_TC", 8)) : 0;
+  // Programmatic dependent launch of the 1-CTA kernel; skinny shapes prefetch
+  // their first 8 weight k-blocks into L2 before waiting for the previous grid.
+  a.pdl = pl.pair ? 0 : 1;
+  a.pdl_pf = p.M <= 256 ? 8 : 0;
   a.pdl_pf_b = swap ? 0 : 1;
   memset(&t_map_c, 0, sizeof(t_map_c));
-  if (!swap && pl.splits == 1 && a.vec_ok && env_int("SF_TMA_STORE", 1)) {
+  if (!swap && pl.splits == 1 && a.vec_ok) {
     // Epilogue chunks of CH columns x 32 rows, stored by TMA with the swizzle
     // matching the chunk's row bytes.
     const int ch = pl.bn < 32 ? pl.bn : 32;
@@ -657,10 +655,10 @@ static int32_t launch_gemv_seg(const Problem& p, const EpilogueArgs& e, int sm_c
   const size_t smem = static_cast<size_t>(ceil_div(p.N, G)) * MM * 4;
   const uint16_t* x = static_cast<const uint16_t*>(p.A);
   const uint16_t* w = static_cast<const uint16_t*>(p.B);
-  // Programmatic dependent launch (tuning knobs: SF_PDL=0 turns it off,
-  // SF_PDL_PF sets the weight units each warp prefetches before its wait).
-  const bool pdl = env_int("SF_PDL", 1) != 0;
-  const int pf_units = pdl ? std::max(0, std::min(32, env_int("SF_PDL_PF", 8))) : 0;
+  // Programmatic dependent launch: each warp prefetches its first 8 weight
+  // units into L2 before waiting for the previous grid.
+  const bool pdl = true;
+  const int pf_units = 8;
   const int n = static_cast<int>(p.N), k = static_cast<int>(p.K);
   const dim3 grid(static_cast<unsigned>(G)), block(kSegWarps * 32);
   if (p.in_dt == kBF16)
@@ -671,7 +669,7 @@ static int32_t launch_gemv_seg(const Problem& p, const EpilogueArgs& e, int sm_c
 }
 
 static bool gemv_seg_ok(const Problem& p) {
-  return p.K % 256 == 0 && aligned16(p.A) && aligned16(p.B) && env_int("SF_GEMV_SEG", 1);
+  return p.K % 256 == 0 && aligned16(p.A) && aligned16(p.B);
 }
 
 static int32_t run_gemv(const Problem& p, const DeviceInfo& dev) {
@@ -863,13 +861,11 @@ int32_t sf_softmax_rows(const void* x, int32_t x_dtype, int64_t ldx, void* y, in
   for (int dt : {x_dtype, y_dtype})
     if (dt != kF32 && dt != kF16 && dt != kBF16) return fail(SF_ERR_INVALID_ARGUMENT, "dtype %d", dt);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t nv = cols / 4;
   const bool vec = x_dtype == kF32 && (cols % 4) == 0 && aligned16(x) && (ldx % 4) == 0 &&
                    (y_dtype == kF32 ? (aligned16(y) && ldy % 4 == 0)
                                     : ((reinterpret_cast<uintptr_t>(y) & 7u) == 0 && ldy % 4 == 0));
   const unsigned grid = static_cast<unsigned>(rows);
-  const int variant = env_int("SF_SOFTMAX", 0);  // 0: streaming two-pass, 1: register-resident
-  if (vec && variant == 0) {
+  if (vec) {
     const float* xf = static_cast<const float*>(x);
     if (y_dtype == kF32)
       softmax_rows_online_kernel<false><<<grid, kSoftmaxOnlineThreads, 0, s>>>(
@@ -877,20 +873,6 @@ int32_t sf_softmax_rows(const void* x, int32_t x_dtype, int64_t ldx, void* y, in
     else
       softmax_rows_online_kernel<true><<<grid, kSoftmaxOnlineThreads, 0, s>>>(
           xf, ldx, y, y_dtype, ldy, static_cast<int>(cols), scale);
-  } else if (vec && nv <= int64_t(kSoftmaxThreads) * 16) {
-    const int64_t vpt = ceil_div(nv, kSoftmaxThreads);
-    const float* xf = static_cast<const float*>(x);
-    const int c = static_cast<int>(cols);
-    if (vpt <= 1)
-      softmax_rows_vec_kernel<1><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
-    else if (vpt <= 2)
-      softmax_rows_vec_kernel<2><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
-    else if (vpt <= 4)
-      softmax_rows_vec_kernel<4><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
-    else if (vpt <= 9)
-      softmax_rows_vec_kernel<9><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
-    else
-      softmax_rows_vec_kernel<16><<<grid, kSoftmaxThreads, 0, s>>>(xf, ldx, y, y_dtype, ldy, c, scale);
   } else {
     softmax_rows_generic_kernel<<<grid, kSoftmaxThreads, 0, s>>>(x, x_dtype, ldx, y, y_dtype, ldy,
                                                                  static_cast<int>(cols), scale);

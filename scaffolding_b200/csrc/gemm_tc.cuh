@@ -72,7 +72,6 @@ struct GemmTcArgs {
   int64_t ws_slice;     // 0: splits red.add into ws; > 0: split s stores into ws + s * ws_slice
   EpilogueArgs epi;
   int* err;             // device error word
-  int epi_sleep_ns;     // poll back-off of the epilogue's accumulator waits (0 = spin)
   int a_box_rows;       // pair kernel: rows per A box (128, or fewer for skinny M)
   // Programmatic dependent launch (host: launch with the attribute when pdl
   // is set).  Before waiting for the previous grid the producer prefetches
@@ -568,8 +567,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       // Warp-uniform: does any row of this warp's 32-row quadrant exist?
       const bool rows_live = mb * BM + quad * 32 < p.M;
       if constexpr (PKB == 0) {
-        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs,
-                       p.epi_sleep_ns))
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp))
           break;
         tc_fence_after();
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -599,8 +597,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 #pragma unroll
         for (int t = 0; t < OWN; ++t) racc[t] = 0.0f;
         for (int kc = kb0; kc < kb1; kc += PKB) {
-          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp,
-                         kWaitLimitNs, p.epi_sleep_ns)) {
+          if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) {
             ok = false;
             break;
           }

@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       tile_coords(u, p, mb, nb, b0, b1);
       const int row0 = mb * Cfg::PAIR_M + static_cast<int>(rank) * BM;
       const int i = row0 + row;
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp, kWaitLimitNs, p.epi_sleep_ns)) break;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.err, kDevTimeoutEpilogue, abortp)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * Cfg::ACC_COLS);

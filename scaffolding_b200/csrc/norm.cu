@@ -13,10 +13,13 @@
 //
 // One warp per row; the row is held in registers (16-byte vector loads,
 // NV vectors per lane), so x is read from HBM once and y written once:
-// 4 B per element for 16-bit in and out.  Mean, then the sum of squared
-// deviations (two passes over the registers, as the reference kernel and
-// NumPy's var do), fp32 throughout; rows wider than the register budget take
-// a loop that re-reads the row from L1/L2 instead.
+// 4 B per element for 16-bit in and out.  The row stays packed as loaded and
+// is unpacked in each pass (half the registers for 16-bit rows).  The
+// per-group scale / shift rows and gamma / beta are read as 16-byte vectors
+// too (they stay in L1 / L2).  Mean, then the sum of squared deviations (two
+// passes over the registers, as the reference kernel and NumPy's var do),
+// fp32 throughout; rows wider than the register budget take a loop that
+// re-reads the row from L1/L2 instead.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -69,9 +72,9 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Unpacks 16 bytes of `dt` elements (8 x 16-bit or 4 x fp32) into f[0..E).
-template <int E>
-__device__ __forceinline__ void unpack16(const uint4& u, int dt, float* f) {
+// Unpacks 16 bytes of elements (4 x fp32 when E == 4, else 8 x bf16 / fp16).
+template <int E, bool BF16>
+__device__ __forceinline__ void unpack16(const uint4& u, float* f) {
   if constexpr (E == 4) {
     f[0] = __uint_as_float(u.x);
     f[1] = __uint_as_float(u.y);
@@ -81,12 +84,11 @@ __device__ __forceinline__ void unpack16(const uint4& u, int dt, float* f) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      if (dt == kBF16) {
+      if constexpr (BF16) {
         f[2 * i] = __uint_as_float(w[i] << 16);
         f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
       } else {
-        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-        const float2 t = __half22float2(h);
+        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
         f[2 * i] = t.x;
         f[2 * i + 1] = t.y;
       }
@@ -94,79 +96,101 @@ __device__ __forceinline__ void unpack16(const uint4& u, int dt, float* f) {
   }
 }
 
-// Row held in registers: NV 16-byte vectors per lane of E elements each.
-template <int E, int NV>
-__global__ void __launch_bounds__(256) layernorm_mod_vec_kernel(const NormArgs a) {
+// Row held in registers: NV 16-byte vectors per lane of E elements each;
+// each warp loads RPW rows at once (more bytes in flight per warp).  x, y
+// and the modulation rows share one element type (fp32 when E == 4, else
+// bf16 / fp16 as BF16 says).
+template <int E, bool BF16, int NV, int RPW>
+__global__ void __launch_bounds__(256, 2) layernorm_mod_vec_kernel(const NormArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int nvec = a.cols / E;  // vectors per row
   const float inv_c = 1.0f / static_cast<float>(a.cols);
-  for (int64_t r = warp0; r < a.rows; r += nwarps) {
-    const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const char*>(a.x) +
-                                                     r * a.ldx * (E == 4 ? 4 : 2));
-    float v[NV][E];
-    float s = 0.0f;
+  constexpr int ES = E == 4 ? 4 : 2;
+  for (int64_t r0 = warp0 * RPW; r0 < a.rows; r0 += nwarps * RPW) {
+    uint4 raw[RPW][NV];  // the rows, packed as loaded
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int vi = lane + 32 * k;
-      if (vi < nvec) {
-        unpack16<E>(__ldg(xr + vi), a.x_dtype, v[k]);
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t r = r0 + q;
+      const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const char*>(a.x) + r * a.ldx * ES);
 #pragma unroll
-        for (int e = 0; e < E; ++e) s += v[k][e];
-      }
+      for (int k = 0; k < NV; ++k)
+        if (r < a.rows && lane + 32 * k < nvec) raw[q][k] = __ldg(xr + lane + 32 * k);
     }
-    const float mean = warp_sum(s) * inv_c;
-    float q = 0.0f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k)
-      if (lane + 32 * k < nvec)
+    for (int q = 0; q < RPW; ++q) {
+      const int64_t r = r0 + q;
+      if (r >= a.rows) break;
+      float s = 0.0f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float d = v[k][e] - mean;
-          q += d * d;
+      for (int k = 0; k < NV; ++k)
+        if (lane + 32 * k < nvec) {
+          float f[E];
+          unpack16<E, BF16>(raw[q][k], f);
+#pragma unroll
+          for (int e = 0; e < E; ++e) s += f[e];
         }
-    const float rstd = 1.0f / sqrtf(warp_sum(q) * inv_c + a.eps);
-    const int64_t g = a.mod ? r / a.group_rows : 0;
+      const float mean = warp_sum(s) * inv_c;
+      float ss = 0.0f;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      const int vi = lane + 32 * k;
-      if (vi >= nvec) continue;
+      for (int k = 0; k < NV; ++k)
+        if (lane + 32 * k < nvec) {
+          float f[E];
+          unpack16<E, BF16>(raw[q][k], f);
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const int c = vi * E + e;
-        float h = (v[k][e] - mean) * rstd;
-        if (a.gamma) h *= a.gamma[c];
-        if (a.beta) h += a.beta[c];
-        if (a.mod) {
-          const float sc = load_elem(a.mod, a.mod_dtype, g * a.ld_mod + c);
-          const float sh = load_elem(a.mod, a.mod_dtype, g * a.ld_mod + a.cols + c);
-          h = h * (sc + 1.0f) + sh;
-        }
-        v[k][e] = h;
-      }
-      char* yr = static_cast<char*>(a.y) + (r * a.ldy + static_cast<int64_t>(vi) * E) *
-                                               (a.y_dtype == kF32 ? 4 : 2);
-      if (a.y_dtype == kF32) {
-#pragma unroll
-        for (int e = 0; e < E; e += 4)
-          *reinterpret_cast<float4*>(yr + e * 4) = make_float4(v[k][e], v[k][e + 1], v[k][e + 2], v[k][e + 3]);
-      } else {
-        uint32_t w[E / 2];
-#pragma unroll
-        for (int e = 0; e < E; e += 2) {
-          if (a.y_dtype == kBF16) {
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[k][e], v[k][e + 1]);
-            w[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
-          } else {
-            const __half2 h2 = __floats2half2_rn(v[k][e], v[k][e + 1]);
-            w[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+          for (int e = 0; e < E; ++e) {
+            const float d = f[e] - mean;
+            ss += d * d;
           }
         }
-        if constexpr (E == 8) {
-          *reinterpret_cast<uint4*>(yr) = make_uint4(w[0], w[1], w[2], w[3]);
+      const float rstd = 1.0f / sqrtf(warp_sum(ss) * inv_c + a.eps);
+      // scale / shift rows of this row's group (16-byte vectors, from L1 / L2)
+      const uint4* msc = a.mod ? reinterpret_cast<const uint4*>(static_cast<const char*>(a.mod) +
+                                                                (r / a.group_rows) * a.ld_mod * ES)
+                               : nullptr;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = lane + 32 * k;
+        if (vi >= nvec) continue;
+        float v[E];
+        unpack16<E, BF16>(raw[q][k], v);
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = (v[e] - mean) * rstd;
+        if (a.gamma) {
+#pragma unroll
+          for (int e = 0; e < E; e += 4) {
+            const float4 g4 = __ldg(reinterpret_cast<const float4*>(a.gamma + vi * E + e));
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(a.beta + vi * E + e));
+            v[e] = v[e] * g4.x + b4.x;
+            v[e + 1] = v[e + 1] * g4.y + b4.y;
+            v[e + 2] = v[e + 2] * g4.z + b4.z;
+            v[e + 3] = v[e + 3] * g4.w + b4.w;
+          }
+        }
+        if (msc) {
+          float sc[E], sh[E];
+          unpack16<E, BF16>(__ldg(msc + vi), sc);
+          unpack16<E, BF16>(__ldg(msc + nvec + vi), sh);
+#pragma unroll
+          for (int e = 0; e < E; ++e) v[e] = v[e] * (sc[e] + 1.0f) + sh[e];
+        }
+        char* yr = static_cast<char*>(a.y) + (r * a.ldy + static_cast<int64_t>(vi) * E) * ES;
+        if constexpr (E == 4) {
+          *reinterpret_cast<float4*>(yr) = make_float4(v[0], v[1], v[2], v[3]);
         } else {
-          *reinterpret_cast<uint2*>(yr) = make_uint2(w[0], w[1]);
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            if constexpr (BF16) {
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[e], v[e + 1]);
+              w[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            } else {
+              const __half2 h2 = __floats2half2_rn(v[e], v[e + 1]);
+              w[e / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+          }
+          *reinterpret_cast<uint4*>(yr) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
@@ -202,16 +226,15 @@ __global__ void __launch_bounds__(256) layernorm_mod_generic_kernel(const NormAr
   }
 }
 
-template <int E>
-int32_t launch_vec(const NormArgs& a, int nv, unsigned grid, cudaStream_t s) {
+template <int E, bool BF16>
+void launch_vec(const NormArgs& a, int nv, unsigned grid, cudaStream_t s) {
   switch (nv) {
-    case 1: layernorm_mod_vec_kernel<E, 1><<<grid, 256, 0, s>>>(a); break;
-    case 2: layernorm_mod_vec_kernel<E, 2><<<grid, 256, 0, s>>>(a); break;
-    case 4: layernorm_mod_vec_kernel<E, 4><<<grid, 256, 0, s>>>(a); break;
-    case 8: layernorm_mod_vec_kernel<E, 8><<<grid, 256, 0, s>>>(a); break;
-    default: layernorm_mod_vec_kernel<E, 16><<<grid, 256, 0, s>>>(a); break;
+    case 1: layernorm_mod_vec_kernel<E, BF16, 1, 4><<<grid, 256, 0, s>>>(a); break;
+    case 2: layernorm_mod_vec_kernel<E, BF16, 2, 4><<<grid, 256, 0, s>>>(a); break;
+    case 4: layernorm_mod_vec_kernel<E, BF16, 4, 2><<<grid, 256, 0, s>>>(a); break;
+    case 8: layernorm_mod_vec_kernel<E, BF16, 8, 2><<<grid, 256, 0, s>>>(a); break;
+    default: layernorm_mod_vec_kernel<E, BF16, 16, 1><<<grid, 256, 0, s>>>(a); break;
   }
-  return SF_OK;
 }
 
 }  // namespace
@@ -244,19 +267,27 @@ extern "C" int32_t sf_layernorm_modulate(int64_t rows, int64_t cols, const void*
   NormArgs a{rows, static_cast<int>(cols), x, x_dtype, ldx, gamma, beta, eps, mod, mod_dtype, ld_mod,
              group_rows, y, y_dtype, ldy};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // 8 warps (rows) per CTA, at most 16 CTAs per SM, grid-stride over the rows.
+  // 8 warps per CTA, at most 16 CTAs per SM, grid-stride over the rows.
   const unsigned grid = static_cast<unsigned>(
       std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 8), dev->sm_count * 16LL)));
-  // Register-resident rows need 16-byte vectors on both sides: same element
-  // size in and out, 16-byte aligned bases and row strides.
+  // Register-resident rows need 16-byte vectors on both sides: one element
+  // type in and out, 16-byte aligned bases and row strides.
   const int es = x_dtype == kF32 ? 4 : 2;
   const int E = 16 / es;
-  const bool vec = (x_dtype == kF32) == (y_dtype == kF32) && cols % E == 0 && aligned16(x) &&
-                   aligned16(y) && bytes16(ldx, es) && bytes16(ldy, es);
+  // The modulation rows are read as vectors of x's type; gamma / beta as float4.
+  const bool vec = x_dtype == y_dtype && cols % E == 0 && aligned16(x) &&
+                   aligned16(y) && bytes16(ldx, es) && bytes16(ldy, es) &&
+                   (!mod || (mod_dtype == x_dtype && aligned16(mod) && bytes16(ld_mod, es))) &&
+                   (!gamma || (aligned16(gamma) && aligned16(beta)));
   const int64_t per_lane = ceil_div(cols / E, 32);
   if (vec && per_lane <= 16) {
     const int nv = per_lane <= 1 ? 1 : per_lane <= 2 ? 2 : per_lane <= 4 ? 4 : per_lane <= 8 ? 8 : 16;
-    st = E == 8 ? launch_vec<8>(a, nv, grid, s) : launch_vec<4>(a, nv, grid, s);
+    if (x_dtype == kF32)
+      launch_vec<4, false>(a, nv, grid, s);
+    else if (x_dtype == kBF16)
+      launch_vec<8, true>(a, nv, grid, s);
+    else
+      launch_vec<8, false>(a, nv, grid, s);
   } else {
     layernorm_mod_generic_kernel<<<grid, 256, 0, s>>>(a);
   }

@@ -63,51 +63,6 @@ __device__ __forceinline__ void store4(void* y, int64_t idx, int dtype, float a,
   }
 }
 
-// Vectorised register-resident softmax: requires cols % 4 == 0 and 16-byte
-// aligned fp32 rows (x), 8-byte aligned rows (16-bit y) or 16-byte (fp32 y).
-template <int VPT>
-static __global__ void __launch_bounds__(kSoftmaxThreads)
-    softmax_rows_vec_kernel(const float* __restrict__ x, int64_t ldx, void* __restrict__ y,
-                            int y_dtype, int64_t ldy, int cols, float scale) {
-  __shared__ float red[32];
-  const int64_t r = blockIdx.x;
-  const float4* xr = reinterpret_cast<const float4*>(x + r * ldx);
-  const int nv = cols >> 2;
-  float4 v[VPT];
-  float m = -INFINITY;
-#pragma unroll
-  for (int t = 0; t < VPT; ++t) {
-    const int c = threadIdx.x + t * kSoftmaxThreads;
-    if (c < nv) {
-      float4 q = __ldcs(xr + c);
-      q.x *= scale; q.y *= scale; q.z *= scale; q.w *= scale;
-      v[t] = q;
-      m = fmaxf(m, fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
-    }
-  }
-  m = block_reduce_max(m, red);
-  float s = 0.0f;
-#pragma unroll
-  for (int t = 0; t < VPT; ++t) {
-    const int c = threadIdx.x + t * kSoftmaxThreads;
-    if (c < nv) {
-      v[t].x = expf(v[t].x - m);
-      v[t].y = expf(v[t].y - m);
-      v[t].z = expf(v[t].z - m);
-      v[t].w = expf(v[t].w - m);
-      s += (v[t].x + v[t].y) + (v[t].z + v[t].w);
-    }
-  }
-  s = block_reduce_sum(s, red);
-#pragma unroll
-  for (int t = 0; t < VPT; ++t) {
-    const int c = threadIdx.x + t * kSoftmaxThreads;
-    if (c < nv)
-      store4(y, r * ldy + 4 * (int64_t)c, y_dtype, v[t].x / s, v[t].y / s, v[t].z / s,
-             v[t].w / s);
-  }
-}
-
 // Two-pass streaming softmax for long fp32 rows (cols % 4 == 0, aligned):
 // pass 1 streams the row once from HBM keeping a running (max, sum of exp)
 // pair per thread -- on a new maximum the sum is rescaled by exp(old - new) --

@@ -7,7 +7,9 @@ argument meaning and error behaviour:
   ``[out]`` drawn U(-1/sqrt(in), 1/sqrt(in)) (Kaiming-uniform, ``:66-74``);
   ``forward`` moves parameters to the input's device on first use
   (``:89-105``) and calls ``dev_linear_forward`` (``:108-110``).  New: an
-  optional fused ``activation`` and a storage ``dtype`` (bf16 / fp16).
+  optional fused ``activation`` and a storage ``dtype`` (bf16 / fp16);
+  ``to(device, dtype)`` (``Module.to``, ``nn/module.py:208-235``) and
+  ``from_weights`` convert fp32 weights to bf16 / fp16 on the device at load.
 * ``functional.linear`` -- ``nn/functional.py:374-395``.
 * ``functional.scaled_dot_product_attention`` -- GPU path of
   ``nn/functional.py:310-321``: for bf16/fp16 with head_dim 64 the fused
@@ -47,6 +49,38 @@ class Linear:
             self.bias = ops.gputensor_from_numpy(b.astype(dtype), dev)
         else:
             self.bias = None
+
+    @classmethod
+    def from_weights(cls, weight: np.ndarray, bias: np.ndarray | None = None, device=None,
+                     dtype=np.float32) -> "Linear":
+        """A layer holding the given host weights (``[out, in]``, ``[out]``):
+        each array is uploaded in fp32 as the reference's ``_param_to_device``
+        does (``nn/layers.py:18-35``) and converted to ``dtype`` on the device
+        (bf16 / fp16 storage for the 16-bit GEMM paths), one parameter at a
+        time."""
+        out_f, in_f = weight.shape
+        lin = cls.__new__(cls)
+        lin.in_features, lin.out_features = in_f, out_f
+        dev = _device_index(device)
+        lin.weight = ops.gputensor_astype(
+            ops.gputensor_from_numpy(np.ascontiguousarray(weight, dtype=np.float32), dev), dtype)
+        lin.bias = None
+        if bias is not None:
+            lin.bias = ops.gputensor_astype(
+                ops.gputensor_from_numpy(np.ascontiguousarray(bias, dtype=np.float32), dev), dtype)
+        return lin
+
+    def to(self, device=None, dtype=None) -> "Linear":
+        """``Module.to`` (``nn/module.py:208-235``): move the parameters to
+        ``device`` and/or convert them to ``dtype`` on the device, one at a
+        time (the old buffers return to the pool before the next one)."""
+        if device is not None:
+            self._to(_device_index(device))
+        if dtype is not None:
+            self.weight = ops.gputensor_astype(self.weight, dtype)
+            if self.bias is not None:
+                self.bias = ops.gputensor_astype(self.bias, dtype)
+        return self
 
     def _to(self, dev: int) -> None:
         if self.weight.device_id != dev:
@@ -115,6 +149,12 @@ class Sequential:
         for m in self.layers:
             x = m(x)
         return x
+
+    def to(self, device=None, dtype=None) -> "Sequential":
+        for m in self.layers:
+            if hasattr(m, "to"):
+                m.to(device, dtype)
+        return self
 
     __call__ = forward
 

@@ -67,12 +67,7 @@ def fp32_mode(mode):
     check(lib.sf_set_fp32_mode(mode), "sf_set_fp32_mode")
 
 
-def attn_oracle_opts(kernel=None):
-    """oracle.flash_attention settings that restate a fused-attention kernel:
-    its key block and integer row bases.  SF_ATTN_KERNEL selects the kernel,
-    as in the engine: 5 (default) = two query tiles per CTA, 64-key blocks,
-    two CTAs per SM; 4 = four query tiles, 64-key blocks; 3 = two query
-    tiles, 128-key blocks; 2 = one query tile per CTA, 64-key blocks."""
-    import os
-    k = int(kernel or os.environ.get("SF_ATTN_KERNEL", "5") or 5)
-    return {"block": 128 if k == 3 else 64, "integer_base": True}
+def attn_oracle_opts():
+    """oracle.flash_attention settings that restate the fused-attention
+    kernel: 64-key blocks and integer row bases."""
+    return {"block": 64, "integer_base": True}

@@ -147,24 +147,20 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
 
 
 @pytest.mark.parametrize("split", ["1", "0"])
-@pytest.mark.parametrize("kernel,emu", [(2, 0), (3, 0), (3, 2), (4, 0), (4, 1), (4, 2), (4, 3),
-                                        (5, 0), (5, 2)])
-def test_fused_attention_every_kernel(gpu, ops, monkeypatch, kernel, emu, split):
-    """Each fused-attention kernel (SF_ATTN_KERNEL; for the two-tile kernel
-    each share of exp2 pairs computed on the FMA pipe, SF_ATTN_EMU) on a
-    ragged case with q_len != kv_len and large logits, against the oracle
-    restating that kernel's key block and row bases; with the split last wave
-    (key pieces merged by a second kernel) and with one CTA per query unit
-    (SF_ATTN_SPLIT=0)."""
+@pytest.mark.parametrize("B,H,Lq,Lk", [(1, 2, 300, 641), (1, 3, 128, 64), (2, 1, 129, 700),
+                                      (1, 2, 257, 65)])
+def test_fused_attention_grid_shapes(gpu, ops, monkeypatch, B, H, Lq, Lk, split):
+    """Ragged query units (one or both tiles of a 256-row unit holding rows,
+    the second tile a single row), ragged and single key blocks, q_len !=
+    kv_len and large logits, against the oracle restating the kernel's key
+    block and row bases; with the split last wave (key pieces merged by a
+    second kernel) and with one CTA per unit (SF_ATTN_SPLIT=0)."""
     from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
-    monkeypatch.setenv("SF_ATTN_KERNEL", str(kernel))
-    monkeypatch.setenv("SF_ATTN_EMU", str(emu))
     monkeypatch.setenv("SF_ATTN_SPLIT", split)
-    expect = 2 if split == "1" else 1
-    assert E.attention_launch_count(1, 2, 300, 641) == expect
-    rng = np.random.default_rng(40 + kernel * 4 + emu)
-    B, H, Lq, Lk = 1, 2, 300, 641
+    if split == "0":
+        assert E.attention_launch_count(B, H, Lq, Lk) == 1
+    rng = np.random.default_rng(Lq * 7 + Lk)
     q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
     k32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32) * np.float32(3)
     v32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32)
@@ -173,13 +169,14 @@ def test_fused_attention_every_kernel(gpu, ops, monkeypatch, kernel, emu, split)
     gv, v = to_device(ops, v32, "bf16")
     out = _fused(ops, B, H, Lq, Lk, gq, gk, gv, H * 64, H * 64, H * 64, Lq * H * 64, Lk * H * 64,
                  Lk * H * 64, 0.125)
-    for h in range(H):
-        sl = slice(h * 64, (h + 1) * 64)
-        p = O.softmax_rows((q[0][:, sl] @ k[0][:, sl].T * np.float32(0.125)).astype(np.float32))
-        ref, allow = O.flash_attention(q[0][:, sl], k[0][:, sl], v[0][:, sl], 0.125,
-                                       return_allowance=True, **attn_oracle_opts(kernel))
-        _check_attn(out[:, sl], ref, O.abs_product(p, v[0][:, sl].T), allow,
-                    f"kernel {kernel} emu {emu} h{h}")
+    for b in range(B):
+        for h in range(H):
+            sl = slice(h * 64, (h + 1) * 64)
+            p = O.softmax_rows((q[b][:, sl] @ k[b][:, sl].T * np.float32(0.125)).astype(np.float32))
+            ref, allow = O.flash_attention(q[b][:, sl], k[b][:, sl], v[b][:, sl], 0.125,
+                                           return_allowance=True, **attn_oracle_opts())
+            _check_attn(out[b * Lq:(b + 1) * Lq, sl], ref, O.abs_product(p, v[b][:, sl].T), allow,
+                        f"B{B} H{H} {Lq}x{Lk} b{b} h{h} split={split}")
     assert device_error(0) == 0
 
 

@@ -212,3 +212,27 @@ def test_trans_a(gpu, ops, dt):
         E.gemm(M, N, K, gat.ptr, M, 1, bb.ptr, K if trans_b else N, trans_b, c.ptr, N, code, code)
         check(to_host32(ops, c), ref, f"trans_a {dt} trans_b={trans_b}")
     assert device_error(0) == 0
+
+
+def test_weights_converted_to_bf16_at_load(gpu, ops):
+    """fp32 weights uploaded as the reference does (nn/layers.py:18-35) and
+    converted to bf16 on the device (Linear.from_weights, Linear.to): the
+    stored bits are the round-to-nearest-even bf16 of the fp32 weights, and
+    the layer then runs the bf16 GEMM path."""
+    from scaffolding_b200 import nn
+    bf = np_dtype("bf16")
+    rng = np.random.default_rng(31)
+    W = rng.standard_normal((384, 256), dtype=np.float32) * np.float32(0.05)
+    b = rng.standard_normal((384,), dtype=np.float32) * np.float32(0.05)
+    lin = nn.Linear.from_weights(W, b, device=0, dtype=bf)
+    assert lin.weight.dtype == bf and lin.bias.dtype == bf
+    assert np.array_equal(ops.gputensor_to_numpy(lin.weight).view(np.uint16),
+                          W.astype(bf).view(np.uint16))
+    lin32 = nn.Linear.from_weights(W, b, device=0).to(0, bf)
+    assert np.array_equal(ops.gputensor_to_numpy(lin32.weight).view(np.uint16),
+                          ops.gputensor_to_numpy(lin.weight).view(np.uint16))
+    gx, x = to_device(ops, rng.standard_normal((100, 256), dtype=np.float32), "bf16")
+    y = lin(gx, activation="gelu_tanh")
+    assert y.dtype == bf
+    ref = O.linear_act(x, O.round_bf16(W), O.round_bf16(b), O.ACT_GELU_TANH)
+    assert_close_16bit(to_host32(ops, y), ref, "bf16-loaded Linear")
