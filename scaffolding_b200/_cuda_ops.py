@@ -479,6 +479,44 @@ def cuda_linear_forward(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | No
     return y.reshape(x.shape[:-1] + (weight.shape[0],))
 
 
+def _host_unary(x: np.ndarray, fn) -> np.ndarray:
+    """Host array -> device -> ``fn`` -> host, in the array's dtype (fp32 for
+    anything the engine does not store), shape kept."""
+    dt = _host_dtype(x)
+    g = gputensor_from_numpy(np.ascontiguousarray(x, dtype=dt))
+    return gputensor_to_numpy(fn(g)).reshape(np.shape(x))
+
+
+def cuda_muls(a: np.ndarray, scalar: float) -> np.ndarray:
+    """Host ``scalar * a`` through the device (``_cuda_ops.pyx:1926-1944``)."""
+    return _host_unary(a, lambda g: dev_muls(g, scalar))
+
+
+def cuda_silu(x: np.ndarray) -> np.ndarray:
+    """Host SiLU through the device (``_cuda_ops.pyx:1954-1955``): the path
+    ``F.silu`` takes for a ``cuda`` tensor without device data."""
+    return _host_unary(x, dev_silu)
+
+
+def cuda_gelu(x: np.ndarray) -> np.ndarray:
+    """Host GELU-tanh through the device (``_cuda_ops.pyx:1957-1958``)."""
+    return _host_unary(x, dev_gelu)
+
+
+def cuda_softmax(x: np.ndarray, dim: int = -1) -> np.ndarray:
+    """Host softmax over the last dimension (``_cuda_ops.pyx:2011-2040``)."""
+    return _host_unary(x, lambda g: dev_softmax(g, -1))
+
+
+def cuda_layer_norm(x: np.ndarray, gamma: np.ndarray | None, beta: np.ndarray | None,
+                    eps: float = 1e-5) -> np.ndarray:
+    """Host LayerNorm of an (N, D) array (``_cuda_ops.pyx:2231-2270``)."""
+    g = gputensor_from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    gg = gputensor_from_numpy(np.ascontiguousarray(gamma, dtype=np.float32)) if gamma is not None else None
+    gb = gputensor_from_numpy(np.ascontiguousarray(beta, dtype=np.float32)) if beta is not None else None
+    return gputensor_to_numpy(dev_layer_norm(g, gg, gb, eps))
+
+
 def set_tf32_enabled(enable: bool) -> None:
     """``allow_tf32``: True permits single-pass TF32 for fp32 GEMMs; False
     (default) keeps fp32 accuracy via 3xTF32 (``_cuda_ops.pyx:2474-2477``)."""
@@ -650,9 +688,9 @@ _OUT_OF_SCOPE = {
     "dev_stack", "dev_chunk", "dev_cumsum", "dev_mean_dim", "dev_sum_dim", "dev_sum_tensor",
     "dev_mean_tensor", "cuda_exp", "cuda_log", "cuda_sqrt", "cuda_rsqrt", "cuda_sigmoid",
     "cuda_tanh", "cuda_sin", "cuda_cos", "cuda_neg", "cuda_abs", "cuda_add", "cuda_sub",
-    "cuda_mul", "cuda_div", "cuda_adds", "cuda_muls", "cuda_relu", "cuda_silu", "cuda_gelu",
-    "cuda_silu_fwd", "cuda_clamp", "cuda_softmax", "cuda_log_softmax", "cuda_cross_entropy",
-    "cuda_layer_norm", "cuda_rms_norm", "cuda_adamw_step", "cuda_dropout", "cuda_embedding",
+    "cuda_mul", "cuda_div", "cuda_adds", "cuda_relu",
+    "cuda_silu_fwd", "cuda_clamp", "cuda_log_softmax", "cuda_cross_entropy",
+    "cuda_rms_norm", "cuda_adamw_step", "cuda_dropout", "cuda_embedding",
     "cuda_transpose_2d", "cuda_sum", "cuda_fill",
 }
 
