@@ -8,7 +8,7 @@ tensors), replayed through the drop-in module.
   signature that accepts the recorded arguments.
 * GPU (-m gpu): the calls run in recorded order, each taking the drop-in's own
   results of the earlier calls, and every result matches the recorded one:
-  transfers bit for bit, fp32 arithmetic within the 1e-5 relative Frobenius
+  uploads bit for bit, computed results within the 1e-5 relative Frobenius
   bar.
 """
 import inspect
@@ -20,7 +20,9 @@ import pytest
 
 HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 TRACE = json.load(open(os.path.join(HERE, "dropin_trace.json")))["calls"]
-EXACT = {"gputensor_from_numpy", "gputensor_to_numpy", "gputensor_to_device", "set_device"}
+# uploads and device moves copy bytes; everything else (downloads of computed
+# results included) is checked against the fp32 bar
+EXACT = {"gputensor_from_numpy", "gputensor_to_device", "set_device"}
 
 
 def _arrays():
