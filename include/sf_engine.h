@@ -208,14 +208,16 @@ int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len, in
                                  float scale, int32_t dtype, int32_t skip_lo, int32_t skip_hi,
                                  float* part_o, float* part_ml, int32_t part_mode, void* stream);
 
-/* Kernel launches one sf_attention_fwd (part_mode 0) or
- * sf_attention_fwd_partial call of these sizes makes on the current device:
- * 1, or 2 when the last wave of query blocks is split into key-range pieces
- * and merged by a second kernel; 0 for empty sizes.  Lets callers count
- * their launches (no reference counterpart: the reference's attention chain,
- * nn/functional.py:310-321, launches a fixed sequence). */
+/* Kernel launches one sf_attention_fwd or sf_attention_fwd_partial call of
+ * these sizes makes on the current device (keys [skip_lo, skip_hi) skipped;
+ * skip_lo = skip_hi = kv_len for sf_attention_fwd): 1, or 2 when the last,
+ * partial wave of query blocks runs as a stream-K tail (its key blocks shared
+ * evenly by all CTA slots) and a merge kernel combines the split units; 0 for
+ * empty sizes.  Lets callers count their launches (no reference counterpart:
+ * the reference's attention chain, nn/functional.py:310-321, launches a fixed
+ * sequence). */
 int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,
-                                  int32_t part_mode, int32_t* count);
+                                  int32_t skip_lo, int32_t skip_hi, int32_t* count);
 
 /* LayerNorm over the last dimension with an optional per-group adaptive
  * scale / shift (adaLN), for row r < rows, column c < cols:

@@ -82,7 +82,7 @@ SIGNATURES: dict[str, list] = {
     "sf_attention_fwd_partial": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64,
                                  _vp, _i64, _i64, _vp, _i64, _i64, C.c_float, _i32, _i32, _i32,
                                  _vp, _vp, _i32, _vp],
-    "sf_attention_launch_count": [_i32, _i32, _i32, _i32, _i32, _P(_i32)],
+    "sf_attention_launch_count": [_i32, _i32, _i32, _i32, _i32, _i32, _P(_i32)],
     "sf_unary": [_vp, _i32, _vp, _i32, _i64, C.c_float, _i32, _vp],
     "sf_layernorm_modulate": [_i64, _i64, _vp, _i32, _i64, _vp, _vp, C.c_float, _vp, _i32, _i64,
                               _i64, _vp, _i32, _i64, _vp],

@@ -1,11 +1,12 @@
 // Fused-attention entry points of the C ABI (sf_attention_fwd,
 // sf_attention_fwd_partial, sf_attention_launch_count): argument checks,
-// TMA descriptors, kernel choice, the split dispatch of the last wave and
+// TMA descriptors, kernel choice, the stream-K tail of the last wave and
 // its workspace.
 //
 // Kernel: attention_pp_kernel (attention_pp.cuh) with two 128-row query tiles
 // per CTA and 64-key blocks (S and P in TMEM, O in a TMEM accumulator, integer
-// row bases raised lazily), plus attention_merge_kernel for the split pieces.
+// row bases raised lazily), plus attention_merge_kernel for the parts of the
+// units that the stream-K tail splits.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -39,37 +40,47 @@ int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensor
   return SF_OK;
 }
 
-// Split dispatch plan (see AttnArgs::split_first).  U units on P resident
-// CTA slots take ceil(U / P) unit times; splitting the R = U mod P units of
-// the last wave into k key-range pieces takes floor(U / P) + ceil(R k / P) / k.
-// k in [2, min(32, key blocks)] minimises that; the split is used when it
-// saves more than 3 %.
-struct AttnSplit {
-  int split_first = -1, split_k = 1, pieces = 0;
-};
-AttnSplit attn_split_plan(int64_t units, int slots, int nkb) {
-  AttnSplit sp;
-  // Test hook: SF_ATTN_SPLIT=0 keeps the one-CTA-per-unit grid.
-  if (env_int("SF_ATTN_SPLIT", 1) == 0 || slots <= 0 || nkb < 2) return sp;
-  const int64_t full = units / slots, rem = units % slots;
-  if (rem == 0) return sp;
-  double best = 1.0;
-  int best_k = 1;
-  for (int k = 2; k <= std::min(32, nkb); ++k) {
-    const double t = static_cast<double>((rem * k + slots - 1) / slots) / k;
-    if (t < best - 1e-9) {
-      best = t;
-      best_k = k;
-    }
-  }
-  if (best_k == 1 || full + best > 0.97 * static_cast<double>(full + 1)) return sp;
-  sp.split_first = static_cast<int>(units - rem);
-  sp.split_k = best_k;
-  sp.pieces = static_cast<int>(rem) * best_k;
-  return sp;
+// Key blocks of a unit over keys [0, kv_len) minus [skip_lo, skip_hi):
+// *na blocks from key 0, then blocks from skip_hi; *ne in all.
+void attn_key_blocks(int kv_len, int skip_lo, int skip_hi, int* na, int* ne) {
+  const int kb = AttnCfg::KB;
+  *na = skip_lo > 0 ? static_cast<int>(ceil_div(skip_lo, kb)) : 0;
+  *ne = *na + (kv_len > skip_hi ? static_cast<int>(ceil_div(kv_len - skip_hi, kb)) : 0);
 }
 
-// Workspace of the split pieces, one per (device, stream) so that calls on
+// Stream-K tail plan (see AttnArgs::split_first).  U units on P resident CTA
+// slots run floor(U / P) full waves of whole units; the other R = U mod P
+// units' ne key blocks each are shared by T = min(P, max(R, R ne /
+// kTailMinBlocks)) tail CTAs.  Cost in block steps: the last wave of whole
+// units takes ne; the tail takes ceil(R ne / T) plus about kTailCost for the
+// second segment's pipeline restart, the parts' fp32 traffic and the merge
+// launch (measured on B200: 70-block units lose with the tail, 139-block
+// units gain 7 %).  The tail is used when it saves more than 3 %.
+constexpr int kTailMinBlocks = 16;
+constexpr double kTailCost = 16.0;
+struct AttnTail {
+  int split_first = -1, ctas = 0, units = 0;
+};
+AttnTail attn_tail_plan(int64_t units, int slots, int ne) {
+  AttnTail tp;
+  // Test hook: SF_ATTN_SPLIT=0 keeps the one-CTA-per-unit grid, 2 forces the
+  // tail whenever the last wave is partial.
+  const int hook = env_int("SF_ATTN_SPLIT", 1);
+  if (hook == 0 || slots <= 0 || ne < 2) return tp;
+  const int64_t full = units / slots, rem = units % slots;
+  if (rem == 0) return tp;
+  const int64_t ctas = std::min<int64_t>(slots, std::max<int64_t>(rem, rem * ne / kTailMinBlocks));
+  if (hook != 2) {
+    const double tail = static_cast<double>((rem * ne + ctas - 1) / ctas) + kTailCost;
+    if (tail > 0.97 * ne - 0.03 * static_cast<double>(full) * ne) return tp;
+  }
+  tp.split_first = static_cast<int>(full * slots);
+  tp.ctas = static_cast<int>(ctas);
+  tp.units = static_cast<int>(rem);
+  return tp;
+}
+
+// Workspace of the tail's parts, one per (device, stream) so that calls on
 // different streams never share it; calls on one stream run in order.  The
 // per-thread default stream (cudaStreamPerThread) is a different stream in
 // every host thread, so its key also carries the thread.  A workspace grows
@@ -176,22 +187,20 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
   a.part_mode = part_mode;
   a.part_o = part_o;
   a.part_ml = part_ml;
+  attn_key_blocks(kv_len, skip_lo, skip_hi, &a.nkb_a, &a.nkb_e);
   a.split_first = -1;
-  a.split_k = 1;
+  a.tail_ctas = a.tail_units = 0;
   a.nqb = static_cast<int>(ceil_div(q_len, rows));
   a.ws_o = a.ws_ml = nullptr;
   dim3 grid(static_cast<unsigned>(a.nqb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  AttnSplit sp;
-  if (part_mode != 1)
-    sp = attn_split_plan(static_cast<int64_t>(a.nqb) * heads * batch,
-                         AttnCfg::MIN_BLOCKS * dev->sm_count,
-                         static_cast<int>(ceil_div(kv_len, static_cast<int>(kb))));
+  const AttnTail tp = attn_tail_plan(static_cast<int64_t>(a.nqb) * heads * batch,
+                                     AttnCfg::MIN_BLOCKS * dev->sm_count, a.nkb_e);
   // Held until the launches are queued, so that no other thread's call on the
   // same stream regrows (frees) the workspace in between.
   std::unique_lock<std::mutex> ws_lock(g_attn_ws_mu, std::defer_lock);
-  if (sp.split_first >= 0) {
-    const size_t need = static_cast<size_t>(sp.pieces) * rows * (kAttnD + 2) * sizeof(float);
+  if (tp.split_first >= 0) {
+    const size_t need = static_cast<size_t>(2 * tp.ctas) * rows * (kAttnD + 2) * sizeof(float);
     ws_lock.lock();
     const AttnWsKey key{device, stream, s == cudaStreamPerThread ? this_thread_tag() : 0};
     AttnWorkspace& ws = g_attn_ws[key];
@@ -205,11 +214,12 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
     }
     if (ws.bytes >= need) {
       if (cap != cudaStreamCaptureStatusNone) ws.captured = true;
-      a.split_first = sp.split_first;
-      a.split_k = sp.split_k;
+      a.split_first = tp.split_first;
+      a.tail_ctas = tp.ctas;
+      a.tail_units = tp.units;
       a.ws_o = static_cast<float*>(ws.ptr);
-      a.ws_ml = a.ws_o + static_cast<size_t>(sp.pieces) * rows * kAttnD;
-      grid = dim3(static_cast<unsigned>(sp.split_first + sp.pieces), 1, 1);
+      a.ws_ml = a.ws_o + static_cast<size_t>(2 * tp.ctas) * rows * kAttnD;
+      grid = dim3(static_cast<unsigned>(tp.split_first + tp.ctas), 1, 1);
     }
   }
   st = dtype == kBF16 ? launch_attention<true>(grid, mq, mk, mv, a, s, device)
@@ -217,11 +227,11 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
   if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
   if (a.split_first >= 0) {
-    const unsigned n_split = static_cast<unsigned>(sp.pieces / sp.split_k);
+    const unsigned n_merge = static_cast<unsigned>(a.tail_units);
     if (dtype == kBF16)
-      attention_merge_kernel<true, AttnCfg::ROWS><<<n_split, AttnCfg::ROWS, 0, s>>>(a);
+      attention_merge_kernel<true, AttnCfg::ROWS><<<n_merge, AttnCfg::ROWS, 0, s>>>(a);
     else
-      attention_merge_kernel<false, AttnCfg::ROWS><<<n_split, AttnCfg::ROWS, 0, s>>>(a);
+      attention_merge_kernel<false, AttnCfg::ROWS><<<n_merge, AttnCfg::ROWS, 0, s>>>(a);
     SF_CUDA_TRY(cudaGetLastError());
   }
   return SF_OK;
@@ -245,24 +255,26 @@ void attention_release_stream(void* stream) {
 
 using namespace sf;
 
-// Number of kernel launches of sf_attention_fwd (part_mode 0) or
-// sf_attention_fwd_partial for these sizes on the current device (1, or 2
-// when the last wave is split and merged).
+// Number of kernel launches of sf_attention_fwd (part_mode 0, no skipped
+// keys: skip_lo = skip_hi = kv_len) or sf_attention_fwd_partial for these
+// sizes on the current device: 1, or 2 when the last wave runs as a
+// stream-K tail and a merge kernel follows.
 extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len,
-                                             int32_t kv_len, int32_t part_mode, int32_t* count) {
+                                             int32_t kv_len, int32_t skip_lo, int32_t skip_hi,
+                                             int32_t* count) {
   if (!count) return fail(SF_ERR_INVALID_ARGUMENT, "null count");
   *count = 0;
   if (batch <= 0 || heads <= 0 || q_len <= 0 || kv_len <= 0) return SF_OK;
+  if (skip_lo < 0 || skip_hi < skip_lo || skip_hi > kv_len)
+    return fail(SF_ERR_INVALID_ARGUMENT, "skipped keys [%d, %d) outside [0, %d]", skip_lo, skip_hi, kv_len);
   DeviceInfo* dev = nullptr;
   int32_t st = current_device_info(&dev, nullptr);
   if (st != SF_OK) return st;
-  *count = 1;
-  if (part_mode != 1) {
-    const int64_t units = ceil_div(q_len, AttnCfg::ROWS) * heads * batch;
-    const AttnSplit sp = attn_split_plan(units, AttnCfg::MIN_BLOCKS * dev->sm_count,
-                                         static_cast<int>(ceil_div(kv_len, AttnCfg::KB)));
-    if (sp.split_first >= 0) *count = 2;
-  }
+  int na = 0, ne = 0;
+  attn_key_blocks(kv_len, skip_lo, skip_hi, &na, &ne);
+  const int64_t units = ceil_div(q_len, AttnCfg::ROWS) * heads * batch;
+  const AttnTail tp = attn_tail_plan(units, AttnCfg::MIN_BLOCKS * dev->sm_count, ne);
+  *count = tp.split_first >= 0 ? 2 : 1;
   return SF_OK;
 }
 

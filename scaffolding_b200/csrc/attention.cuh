@@ -1,6 +1,6 @@
 // Shared parts of the fused attention forward for sm_100a (head_dim 64):
 // the launch arguments (AttnArgs), the packed fp32x2 / exp2 / 16-bit packing
-// helpers the softmax uses, and the merge kernel of the split dispatch.  The
+// helpers the softmax uses, and the merge kernel of the stream-K tail.  The
 // kernel itself is attention_pp_kernel (attention_pp.cuh).
 //
 // The fused attention computes O[b, h] = softmax(scale * Q[b, h] K[b, h]^T)
@@ -39,17 +39,24 @@ struct AttnArgs {
   int part_mode;
   float* part_o;
   float* part_ml;
-  // Split dispatch (part_mode 0 or 2), so that the
-  // last wave of CTAs is not mostly empty: a 1-D grid whose blocks
-  // [0, split_first) are whole units u (query block u % nqb, head
-  // (u / nqb) % heads, batch u / (nqb * heads)); block split_first + j is
-  // piece j % split_k of unit split_first + j / split_k, a contiguous share
-  // of the key blocks, and writes its unnormalised fp32 O rows and (m, l)
-  // to slot j of ws_o [slot][rows][64] / ws_ml [slot][rows][2] (zeros and
-  // m = -inf when all its keys are skipped); attention_merge_kernel then
-  // combines the pieces of each split unit (and part_o / part_ml in mode 2).
-  int split_first;  // -1: 3-D grid (query unit, head, batch), no pieces
-  int split_k;
+  // Key blocks of a unit: nkb_a blocks of KB keys from key 0 cover
+  // [0, skip_lo), then blocks from skip_hi cover [skip_hi, kv_len); nkb_e
+  // blocks in all (the unit's effective blocks).
+  int nkb_a, nkb_e;
+  // Stream-K tail, so that the last wave of CTAs is not partly empty: a 1-D
+  // grid whose blocks [0, split_first) are whole units u (query block
+  // u % nqb, head (u / nqb) % heads, batch u / (nqb * heads)) and whose
+  // tail_ctas further blocks share the effective key blocks of the last
+  // tail_units units laid end to end: tail CTA c takes blocks
+  // [c W / T, (c + 1) W / T) (W = tail_units * nkb_e, T = tail_ctas >=
+  // tail_units), one or two segments (parts of consecutive units).  A
+  // segment that covers a whole unit writes its output as usual; a part of
+  // a unit writes its unnormalised fp32 O rows and (m, l) to workspace slot
+  // 2 c + (segment index) of ws_o [slot][rows][64] / ws_ml [slot][rows][2],
+  // and attention_merge_kernel combines the parts of each split unit (with
+  // part_o / part_ml in mode 2, into part_o / part_ml in mode 1).
+  int split_first;  // -1: 3-D grid (query unit, head, batch), no tail
+  int tail_ctas, tail_units;
   int nqb;
   float* ws_o;
   float* ws_ml;
@@ -57,6 +64,19 @@ struct AttnArgs {
 
 constexpr int kAttnBlock = 128;   // query rows per tile
 constexpr int kAttnD = 64;        // head dim
+
+// First effective block (within the tail's blocks laid end to end) of tail
+// CTA c; c = tail_ctas gives the end.
+__device__ __forceinline__ int64_t attn_tail_lo(const AttnArgs& p, int c) {
+  return static_cast<int64_t>(c) * (static_cast<int64_t>(p.tail_units) * p.nkb_e) / p.tail_ctas;
+}
+
+// The tail CTA whose block range holds tail block g: the largest c with
+// attn_tail_lo(c) <= g.
+__device__ __forceinline__ int attn_tail_cta(const AttnArgs& p, int64_t g) {
+  const int64_t w = static_cast<int64_t>(p.tail_units) * p.nkb_e;
+  return static_cast<int>(((g + 1) * p.tail_ctas - 1) / w);
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -102,41 +122,48 @@ __device__ __forceinline__ uint32_t pack_16bit(float a, float b, bool bf16) {
 // them by more than this (p then stays below 2^8 before the rescale).
 constexpr float kAttnRescaleLog2 = 8.0f;
 
-// Combines the split_k pieces of each split unit, and in part_mode 2 the
-// partial result in part_o / part_ml (one CTA per unit of ROWS query rows,
-// one thread per row): with integer bases m_p, m = max m_p,
-// O = sum 2^(m_p - m) O_p / sum 2^(m_p - m) l_p, written as 16-bit O.
-// Workspace slot s holds ws_o[s][ROWS][64] and ws_ml[s][ROWS][2].
+// Combines the parts of each split tail unit, and in part_mode 2 the
+// partial result in part_o / part_ml (one CTA per tail unit of ROWS query
+// rows, one thread per row): with integer bases m_i, m = max m_i,
+// O = sum 2^(m_i - m) O_i / sum 2^(m_i - m) l_i, written as 16-bit O; in
+// part_mode 1 the combined unnormalised sum and (m, l) go to part_o /
+// part_ml instead.  A unit that one CTA ran whole was written by it.
 template <bool BF16, int ROWS>
 __global__ void __launch_bounds__(ROWS) attention_merge_kernel(const AttnArgs p) {
-  const int u = p.split_first + static_cast<int>(blockIdx.x);
+  const int i = static_cast<int>(blockIdx.x);
+  const int64_t ne = p.nkb_e;
+  const int c0 = attn_tail_cta(p, i * ne), c1 = attn_tail_cta(p, (i + 1) * ne - 1);
+  if (c0 == c1) return;
+  const int u = p.split_first + i;
   const int qb = u % p.nqb, h = (u / p.nqb) % p.heads, b = u / (p.nqb * p.heads);
   const int row = threadIdx.x;
   const int qrow = qb * ROWS + row;
   if (qrow >= p.q_len) return;
-  const int64_t slot0 = static_cast<int64_t>(blockIdx.x) * p.split_k;
   const int64_t prow = (static_cast<int64_t>(b) * p.q_len + qrow) * p.heads + h;
-  const int n_in = p.split_k + (p.part_mode == 2 ? 1 : 0);
-  // input i < split_k: workspace slot slot0 + i; i == split_k: the partial result
-  auto ml_of = [&](int i) -> const float* {
-    return i < p.split_k ? p.ws_ml + ((slot0 + i) * ROWS + row) * 2 : p.part_ml + 2 * prow;
+  // input c in [c0, c1]: the part tail CTA c ran (its first or second
+  // segment); c1 + 1: the partial result of mode 2
+  const int n_in = c1 + 1 + (p.part_mode == 2 ? 1 : 0);
+  auto slot_of = [&](int c) -> int64_t {
+    return 2 * c + (attn_tail_lo(p, c) / ne == i ? 0 : 1);
   };
-  auto o_of = [&](int i) -> const float* {
-    return i < p.split_k ? p.ws_o + ((slot0 + i) * ROWS + row) * kAttnD
-                         : p.part_o + prow * kAttnD;
+  auto ml_of = [&](int c) -> const float* {
+    return c <= c1 ? p.ws_ml + (slot_of(c) * ROWS + row) * 2 : p.part_ml + 2 * prow;
+  };
+  auto o_of = [&](int c) -> const float* {
+    return c <= c1 ? p.ws_o + (slot_of(c) * ROWS + row) * kAttnD : p.part_o + prow * kAttnD;
   };
   float m = -INFINITY;
-  for (int i = 0; i < n_in; ++i) m = fmaxf(m, ml_of(i)[0]);
+  for (int c = c0; c < n_in; ++c) m = fmaxf(m, ml_of(c)[0]);
   float l = 0.0f;
   float acc[kAttnD];
 #pragma unroll
   for (int t = 0; t < kAttnD; ++t) acc[t] = 0.0f;
-  for (int i = 0; i < n_in; ++i) {
-    const float* ml = ml_of(i);
-    if (ml[0] == -INFINITY) continue;  // every key of this piece skipped
+  for (int c = c0; c < n_in; ++c) {
+    const float* ml = ml_of(c);
+    if (ml[0] == -INFINITY) continue;  // every key of this input skipped
     const float a = ex2_approx(ml[0] - m);
     l += ml[1] * a;
-    const float4* po = reinterpret_cast<const float4*>(o_of(i));
+    const float4* po = reinterpret_cast<const float4*>(o_of(c));
 #pragma unroll
     for (int q = 0; q < kAttnD / 4; ++q) {
       const float4 v = po[q];
@@ -145,6 +172,15 @@ __global__ void __launch_bounds__(ROWS) attention_merge_kernel(const AttnArgs p)
       acc[4 * q + 2] += v.z * a;
       acc[4 * q + 3] += v.w * a;
     }
+  }
+  if (p.part_mode == 1) {
+    p.part_ml[2 * prow] = m;
+    p.part_ml[2 * prow + 1] = l;
+    float4* po = reinterpret_cast<float4*>(p.part_o + prow * kAttnD);
+#pragma unroll
+    for (int q = 0; q < kAttnD / 4; ++q)
+      po[q] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+    return;
   }
   const float inv = 1.0f / l;
   uint4* dst = reinterpret_cast<uint4*>(

@@ -79,49 +79,70 @@ struct AttnPpCfg {
   static_assert(KB == 64 || KB == 128, "key block");
   static_assert(NT * (KB + 64) <= 512, "TMEM budget");
   static_assert(KV_TILE % 1024 == 0 && KV_OFF % 1024 == 0, "1024-byte aligned tiles");
-  static_assert((1 + 2 * KV_STAGES + 3 * NT + 1) * 8 + 8 <= 512, "barrier area");
+  static_assert((1 + 2 * KV_STAGES + 3 * NT + 2) * 8 + 8 <= 512, "barrier area");
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-// Work of one CTA: unit (query rows [qb * ROWS, +ROWS) of head h, batch b)
-// and its key blocks, [k0, e0) then [s1, k1) ([e0, s1) skipped), KB keys each.
+// One segment of a CTA's work: query rows [qb * ROWS, +ROWS) of head h,
+// batch b, and the unit's effective key blocks [ea, eb) -- block i < nkb_a
+// starts at key i * KB, block i >= nkb_a at skip_hi + (i - nkb_a) * KB --
+// as nblk blocks [k0, e0) then [s1, k1), KB keys each.  slot >= 0: a part of
+// a split tail unit, written to workspace slot `slot`.
 template <int KB>
-struct PpWork {
-  int qb, h, b, slot, k0, k1, e0, s1, nb0, nblk;
+struct PpSeg {
+  int qb, h, b, slot, k0, e0, s1, k1, nb0, nblk;
   __device__ __forceinline__ int start(int j) const { return j < nb0 ? k0 + j * KB : s1 + (j - nb0) * KB; }
   __device__ __forceinline__ int valid(int j) const { return min(KB, (j < nb0 ? e0 : k1) - start(j)); }
 };
 
+// Segments of this CTA: one for a whole unit, one or two for a tail CTA
+// (its block range is at most one unit long, so it meets at most two units).
+__device__ __forceinline__ int pp_nseg(const AttnArgs& p) {
+  if (p.split_first < 0 || static_cast<int>(blockIdx.x) < p.split_first) return 1;
+  const int c = static_cast<int>(blockIdx.x) - p.split_first;
+  const int64_t lo = attn_tail_lo(p, c), hi = attn_tail_lo(p, c + 1);
+  if (hi <= lo) return 0;
+  return static_cast<int>((hi - 1) / p.nkb_e - lo / p.nkb_e) + 1;
+}
+
 template <int KB>
-__device__ __forceinline__ PpWork<KB> pp_work(const AttnArgs& p) {
-  PpWork<KB> w;
-  int u = static_cast<int>(blockIdx.x), k0 = 0, k1 = p.kv_len, slot = -1;
+__device__ __forceinline__ PpSeg<KB> pp_seg(const AttnArgs& p, int i) {
+  PpSeg<KB> w;
+  int ea = 0, eb = p.nkb_e, u = static_cast<int>(blockIdx.x);
+  w.slot = -1;
   if (p.split_first < 0) {
     w.qb = blockIdx.x;
     w.h = blockIdx.y;
     w.b = blockIdx.z;
   } else {
     if (u >= p.split_first) {
-      const int j = u - p.split_first;
-      const int piece = j % p.split_k;
-      const int nkb = (p.kv_len + KB - 1) / KB;
-      u = p.split_first + j / p.split_k;
-      k0 = (piece * nkb / p.split_k) * KB;
-      k1 = min(p.kv_len, ((piece + 1) * nkb / p.split_k) * KB);
-      slot = j;
+      const int c = u - p.split_first;
+      const int64_t lo = attn_tail_lo(p, c), hi = attn_tail_lo(p, c + 1);
+      const int64_t ur = lo / p.nkb_e + i, u0 = ur * p.nkb_e;
+      ea = static_cast<int>(max(lo, u0) - u0);
+      eb = static_cast<int>(min(hi, u0 + p.nkb_e) - u0);
+      u = p.split_first + static_cast<int>(ur);
+      if (ea > 0 || eb < p.nkb_e) w.slot = 2 * c + i;
     }
     w.qb = u % p.nqb;
     w.h = (u / p.nqb) % p.heads;
     w.b = u / (p.nqb * p.heads);
   }
-  w.slot = slot;
-  w.k0 = k0;
-  w.k1 = k1;
-  w.e0 = min(k1, p.skip_lo);
-  w.s1 = max(k0, p.skip_hi);
-  w.nb0 = w.e0 > k0 ? (w.e0 - k0 + KB - 1) / KB : 0;
-  w.nblk = w.nb0 + (k1 > w.s1 ? (k1 - w.s1 + KB - 1) / KB : 0);
+  const int na = p.nkb_a;
+  w.nb0 = max(0, min(eb, na) - ea);
+  w.k0 = ea * KB;
+  w.e0 = min(min(eb, na) * KB, p.skip_lo);
+  w.s1 = p.skip_hi + (max(ea, na) - na) * KB;
+  w.k1 = min(p.kv_len, p.skip_hi + (eb - na) * KB);
+  w.nblk = eb - ea;
   return w;
+}
+
+// Query tiles of a segment that hold rows (past q_len they are skipped; a
+// unit is never empty).
+template <class Cfg, int KB>
+__device__ __forceinline__ int pp_tiles(const AttnArgs& p, const PpSeg<KB>& w) {
+  return min(Cfg::NT, (p.q_len - w.qb * Cfg::ROWS + 127) / 128);
 }
 
 template <bool BF16, class Cfg>
@@ -137,20 +158,19 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
   uint64_t* kv_empty = kv_full + ST;
   uint64_t* s_full = kv_empty + ST;   // [NT]: S_t(j) ready (covers O_t += P_t(j-1) V)
   uint64_t* p_full = s_full + NT;     // [NT]: P_t(j) stored (4 warp arrivals)
-  uint64_t* o_last = p_full + NT;     // [NT]: the last P.V of tile t done
+  uint64_t* o_last = p_full + NT;     // [NT]: the last P.V of tile t's segment done
   uint64_t& drain_bar = o_last[NT];
-  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&o_last[NT + 1]);
-  int& abort_flag = *(reinterpret_cast<int*>(&o_last[NT + 1]) + 1);
-  if ((smem_u32(smem) & 1023u) != 0) {
+  uint64_t& q_empty = o_last[NT + 1]; // a segment's S MMAs done: its Q tiles are free
+  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&o_last[NT + 2]);
+  int& abort_flag = *(reinterpret_cast<int*>(&o_last[NT + 2]) + 1);
+  const int nseg = pp_nseg(p);
+  if (nseg == 0) return;  // a tail CTA without blocks (the whole CTA)
+  if ((smem_u32(smem) & 1023u) != 0 || nseg > 2) {
     if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadConfig);
     return;
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const PpWork<KB> w = pp_work<KB>(p);
-  const int nblk = w.nblk;
-  // Only tiles that hold query rows run (the unit is never empty).
-  const int ntiles = min(NT, (p.q_len - w.qb * Cfg::ROWS + 127) / 128);
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -164,6 +184,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       mbar_init(&o_last[t], 1);
     }
     mbar_init(&drain_bar, 1);
+    mbar_init(&q_empty, 1);
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -182,33 +203,49 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
   const uint32_t tmem_base = tmem_slot;
   volatile int* abortp = &abort_flag;
 
+  // Segments run one after another through the same barriers; every
+  // barrier's phase parity is taken from a count that runs across them:
+  // q_full / q_empty per segment with blocks, kv_full / kv_empty per K/V
+  // block, s_full / p_full per block of tile t, o_last per segment of tile t.
   if (warp == Cfg::TMA_WARP) {
     // ───────────── TMA producer ─────────────
     if (lane == 0) {
       bool ok = true;
-      int issued = 0, stage = 0;
+      int issued = 0, stage = 0, nq = 0;
       uint32_t phase = 0;
-      mbar_arrive_expect_tx(&q_full, ntiles * Cfg::Q_TILE);
-      for (int t = 0; t < ntiles; ++t)
-        tma_load_4d(smem + Cfg::Q_OFF + t * Cfg::Q_TILE, &tmQ, &q_full, 0,
-                    w.qb * Cfg::ROWS + t * 128, w.h, w.b);
-      for (int j = 0; j < nblk; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+      for (int si = 0; si < nseg && ok; ++si) {
+        const PpSeg<KB> w = pp_seg<KB>(p, si);
+        if (w.nblk == 0) continue;
+        const int nt = pp_tiles<Cfg>(p, w);
+        if (nq > 0 && !mbar_wait(&q_empty, static_cast<uint32_t>(nq - 1) & 1u, p.err,
+                                 kDevTimeoutProducer, abortp)) {
           ok = false;
           break;
         }
-        uint8_t* kt = smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE;
-        mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::KV_TILE);
-        const int ks = w.start(j);
-        tma_load_4d(kt, &tmK, &kv_full[stage], 0, ks, w.h, w.b);
-        tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, ks, w.h, w.b);
-        ++issued;
-        if (++stage == ST) {
-          stage = 0;
-          phase ^= 1u;
+        mbar_arrive_expect_tx(&q_full, nt * Cfg::Q_TILE);
+        for (int t = 0; t < nt; ++t)
+          tma_load_4d(smem + Cfg::Q_OFF + t * Cfg::Q_TILE, &tmQ, &q_full, 0,
+                      w.qb * Cfg::ROWS + t * 128, w.h, w.b);
+        ++nq;
+        for (int j = 0; j < w.nblk; ++j) {
+          if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+            ok = false;
+            break;
+          }
+          uint8_t* kt = smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE;
+          mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::KV_TILE);
+          const int ks = w.start(j);
+          tma_load_4d(kt, &tmK, &kv_full[stage], 0, ks, w.h, w.b);
+          tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, ks, w.h, w.b);
+          ++issued;
+          if (++stage == ST) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-      if (!mbar_wait_quiet(&q_full, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      if (nq > 0 && !mbar_wait_quiet(&q_full, static_cast<uint32_t>(nq - 1) & 1u, 200000000ull))
+        atomicCAS(p.err, 0, kDevTimeoutDrain);
       if (!ok) {
         // Wait for the copies still in flight before the CTA exits.
         const int n = issued < ST ? issued : ST;
@@ -231,80 +268,104 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     // slow tile never holds back the others.  A K/V stage is released once
     // every running tile has issued its P.V on it (the commit covers all
     // MMAs issued before it).  Tiles can drift apart by up to KV_STAGES-1
-    // blocks; the producer refills stages in block order.
+    // blocks; the producer refills stages in block order.  The first P.V of
+    // a segment overwrites O_t: the softmax warps of tile t have read the
+    // previous segment's O_t before they store the P that lets it issue.
     if (lane == 0) {
       const uint32_t fmt = BF16 ? 1u : 0u;
       const uint32_t idesc_s = make_idesc(fmt, 128, KB, 0u, 0u);
       const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);
-      bool ok = nblk == 0 || mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
-      bool issued_any = false;
-      int jt[NT];                 // next block each tile issues S for (P.V of jt-1 with it)
+      bool ok = true, issued_any = false;
+      int pbase[NT];              // p_full phases of tile t before this segment
       int pv_done[ST];            // tiles that have issued their P.V on each stage's block
 #pragma unroll
-      for (int t = 0; t < NT; ++t) jt[t] = 0;
+      for (int t = 0; t < NT; ++t) pbase[t] = 0;
 #pragma unroll
       for (int s2 = 0; s2 < ST; ++s2) pv_done[s2] = 0;
-      int finished = 0;
-      unsigned long long t_last = global_timer_ns();
-      while (ok && finished < ntiles) {
-        bool progress = false;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (t >= ntiles) continue;
-          const int j = jt[t];
-          if (j > nblk) continue;
-          if (j > 0 && !mbar_test(&p_full[t], static_cast<uint32_t>(j - 1) & 1u)) continue;
-          if (j < nblk && !mbar_test(&kv_full[j % ST], static_cast<uint32_t>(j / ST) & 1u)) continue;
-          tc_fence_after();
-          if (j > 0) {
-            // O_t += P_t(j-1) V(j-1), P from TMEM, V MN-major from its stage.
-            const int ps = (j - 1) % ST;
-            const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + ps * 2 * Cfg::KV_TILE + Cfg::KV_TILE);
-#pragma unroll
-            for (int ks = 0; ks < KB / 16; ++ks) {
-              const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, Cfg::KV_TILE, 1024);
-              umma_f16_tmem_a(tmem_base + Cfg::O_COL + t * 64,
-                              tmem_base + Cfg::S_COL + t * KB + ks * 8, bd, idesc_o,
-                              (j > 1 || ks > 0) ? 1u : 0u);
-            }
-            if (++pv_done[ps] == ntiles) {
-              pv_done[ps] = 0;
-              umma_commit(&kv_empty[ps]);
-            }
-            if (j == nblk) umma_commit(&o_last[t]);
-          }
-          if (j < nblk) {
-            const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF + t * Cfg::Q_TILE);
-            const uint32_t k_addr = smem_u32(smem + Cfg::KV_OFF + (j % ST) * 2 * Cfg::KV_TILE);
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
-              const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
-              umma_f16(tmem_base + Cfg::S_COL + t * KB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
-            }
-            issued_any = true;
-            umma_commit(&s_full[t]);
-          }
-          jt[t] = j + 1;
-          if (j == nblk) ++finished;
-          progress = true;
-        }
-        if (progress) {
-          t_last = global_timer_ns();
-        } else if (*abortp) {
+      int g0 = 0, nq = 0;         // K/V blocks and Q loads of the earlier segments
+      for (int si = 0; si < nseg && ok; ++si) {
+        const PpSeg<KB> w = pp_seg<KB>(p, si);
+        const int nblk = w.nblk;
+        if (nblk == 0) continue;
+        const int nt = pp_tiles<Cfg>(p, w);
+        if (!mbar_wait(&q_full, static_cast<uint32_t>(nq) & 1u, p.err, kDevTimeoutMma, abortp)) {
           ok = false;
-        } else if (global_timer_ns() - t_last > kWaitLimitNs) {
-          *abortp = 1;
-          atomicCAS(p.err, 0, kDevTimeoutMma);
-          ok = false;
+          break;
         }
+        int jt[NT];               // next block each tile issues S for (P.V of jt-1 with it)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) jt[t] = 0;
+        int finished = 0;
+        unsigned long long t_last = global_timer_ns();
+        while (ok && finished < nt) {
+          bool progress = false;
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            if (t >= nt) continue;
+            const int j = jt[t];
+            if (j > nblk) continue;
+            if (j > 0 && !mbar_test(&p_full[t], static_cast<uint32_t>(pbase[t] + j - 1) & 1u)) continue;
+            const int g = g0 + j;
+            if (j < nblk && !mbar_test(&kv_full[g % ST], static_cast<uint32_t>(g / ST) & 1u)) continue;
+            tc_fence_after();
+            if (j > 0) {
+              // O_t += P_t(j-1) V(j-1), P from TMEM, V MN-major from its stage.
+              const int ps = (g - 1) % ST;
+              const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + ps * 2 * Cfg::KV_TILE + Cfg::KV_TILE);
+#pragma unroll
+              for (int ks = 0; ks < KB / 16; ++ks) {
+                const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, Cfg::KV_TILE, 1024);
+                umma_f16_tmem_a(tmem_base + Cfg::O_COL + t * 64,
+                                tmem_base + Cfg::S_COL + t * KB + ks * 8, bd, idesc_o,
+                                (j > 1 || ks > 0) ? 1u : 0u);
+              }
+              if (++pv_done[ps] == nt) {
+                pv_done[ps] = 0;
+                umma_commit(&kv_empty[ps]);
+              }
+              if (j == nblk) umma_commit(&o_last[t]);
+            }
+            if (j < nblk) {
+              const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF + t * Cfg::Q_TILE);
+              const uint32_t k_addr = smem_u32(smem + Cfg::KV_OFF + (g % ST) * 2 * Cfg::KV_TILE);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
+                const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
+                umma_f16(tmem_base + Cfg::S_COL + t * KB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+              }
+              issued_any = true;
+              umma_commit(&s_full[t]);
+            }
+            jt[t] = j + 1;
+            if (j == nblk) ++finished;
+            progress = true;
+          }
+          if (progress) {
+            t_last = global_timer_ns();
+          } else if (*abortp) {
+            ok = false;
+          } else if (global_timer_ns() - t_last > kWaitLimitNs) {
+            *abortp = 1;
+            atomicCAS(p.err, 0, kDevTimeoutMma);
+            ok = false;
+          }
+        }
+        if (!ok) break;
+        // Every S MMA of the segment is issued: its Q tiles free once they complete.
+        umma_commit(&q_empty);
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < nt) pbase[t] += nblk;
+        g0 += nblk;
+        ++nq;
       }
       if (!ok && issued_any) {
         umma_commit(&drain_bar);
         if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
       }
     }
-  } else if ((warp >> 2) < ntiles) {
+  } else {
     // ───────────── softmax of tile t: one thread per query row ─────────────
     const int t = warp >> 2;
     const int quad = warp & 3;
@@ -312,9 +373,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_base + Cfg::S_COL + t * KB;
     const uint32_t o_addr = tmem_base + lane_base + Cfg::O_COL + t * 64;
-    float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
     const float c = p.scale_log2;
     bool ok = true;
+    int sbase = 0, ocnt = 0;  // s_full phases and finished segments of this tile so far
     uint32_t r[KB > 64 ? KB : 64];
     // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
     auto rescale_o = [&](float alpha) {
@@ -327,91 +388,99 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
         tmem_st32(o_addr + half * 32, r);
       }
     };
-    for (int j = 0; j < nblk; ++j) {
-      // Waits end the loop for the whole warp together: the TMEM loads and
-      // stores that follow are warp-collective.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1u, p.err,
-                                             kDevTimeoutEpilogue, abortp))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-      tmem_ld_wait();
-      const int valid = w.valid(j);
-      const bool full = valid == KB;
-      float mx;
-      if (full) {
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < KB; i += 8) {
-          m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-          m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-          m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+    for (int si = 0; si < nseg && ok; ++si) {
+      const PpSeg<KB> w = pp_seg<KB>(p, si);
+      if (t >= pp_tiles<Cfg>(p, w)) continue;
+      const int nblk = w.nblk;
+      float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
+      for (int j = 0; j < nblk; ++j) {
+        // Waits end the loop for the whole warp together: the TMEM loads and
+        // stores that follow are warp-collective.
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(sbase + j) & 1u,
+                                               p.err, kDevTimeoutEpilogue, abortp))) {
+          ok = false;
+          break;
         }
-        mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-      } else {
-        mx = -INFINITY;
+        tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < KB; ++i)
-          if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      const float cand = ceilf(mx * c);
-      const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-      const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-      const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
-      if (need) {
-        l_run *= alpha;
-        m_run = cand;
-      }
-      const float nm = -m_run;
-      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        float* pv = reinterpret_cast<float*>(r + ch * 32);
+        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+        tmem_ld_wait();
+        const int valid = w.valid(j);
+        const bool full = valid == KB;
+        float mx;
         if (full) {
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float x0, x1;
-            fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
-            pv[i] = ex2_approx(x0);
-            pv[i + 1] = ex2_approx(x1);
-            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
+          for (int i = 0; i < KB; i += 8) {
+            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
           }
+          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
         } else {
+          mx = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = ex2_approx(fmaf(pv[i], c, nm));
-            pv[i] = ch * 32 + i < valid ? e : 0.0f;
-            sp[i & 7] += pv[i];
-          }
+          for (int i = 0; i < KB; ++i)
+            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
-        // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first),
-        // over score columns this thread has already read.
-        uint32_t pk[16];
+        const float cand = ceilf(mx * c);
+        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+        const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+        const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
+        if (need) {
+          l_run *= alpha;
+          m_run = cand;
+        }
+        const float nm = -m_run;
+        float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_16bit(pv[2 * i], pv[2 * i + 1], BF16);
-        tmem_st16(s_addr + ch * 16, pk);
+        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
+          float* pv = reinterpret_cast<float*>(r + ch * 32);
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              float x0, x1;
+              fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
+              pv[i] = ex2_approx(x0);
+              pv[i + 1] = ex2_approx(x1);
+              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e = ex2_approx(fmaf(pv[i], c, nm));
+              pv[i] = ch * 32 + i < valid ? e : 0.0f;
+              sp[i & 7] += pv[i];
+            }
+          }
+          // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first),
+          // over score columns this thread has already read.
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = pack_16bit(pv[2 * i], pv[2 * i + 1], BF16);
+          tmem_st16(s_addr + ch * 16, pk);
+        }
+        l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+        // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
+        // is issued only after the arrival below.
+        if (rescale) rescale_o(alpha);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
-      l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-      // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
-      // is issued only after the arrival below.
-      if (rescale) rescale_o(alpha);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    if (ok && nblk > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
-    const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
-    if (ok) {
+      if (ok && nblk > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], static_cast<uint32_t>(ocnt) & 1u, p.err,
+                                               kDevTimeoutEpilogue, abortp));
+      sbase += nblk;
+      if (nblk > 0) ++ocnt;
+      if (!ok) break;
       tc_fence_after();
+      const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
       const bool live = qrow < p.q_len;
       const int64_t prow = (static_cast<int64_t>(w.b) * p.q_len + qrow) * p.heads + w.h;
-      // A split piece writes its partial result to its workspace slot.
+      // A part of a split unit writes its partial result to its workspace slot.
       const int mode = w.slot >= 0 ? 1 : p.part_mode;
       const int urow = t * 128 + row;
       float* const pml = w.slot >= 0 ? p.ws_ml + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * 2
@@ -473,6 +542,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
                          pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
                          pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
       }
+      // This tile's O_t reads are complete (tcgen05.wait::ld above) before its
+      // next P arrival lets the next segment's first P.V overwrite O_t.
+      tc_fence_before();
     }
   }
 

@@ -406,16 +406,26 @@ class DitStack:
             timer.stop("adaln")
         return self.xn.ptr
 
+    def _qkv_input(self, li: int, x_ptr: int, stream, timer) -> int:
+        """The rows the QKV projection reads: x, or norm1(x) with adaLN."""
+        return self._adaln(li, "mod1", x_ptr, stream, timer) if self.adaln else x_ptr
+
+    def _q(self, li: int, x_ptr: int, stream, timer) -> None:
+        p, Cw, w = self.plan, self.C, self.w[li]
+        self._gemm("q", timer, stream, p.m, Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr, Cw, 1,
+                   self.q.ptr, Cw, DT_BF16, DT_BF16)
+
+    def _kv(self, li: int, x_ptr: int, stream, timer) -> None:
+        p, Cw, w = self.plan, self.C, self.w[li]
+        self._gemm("kv", timer, stream, p.m, 2 * Cw, Cw, x_ptr, Cw, 0,
+                   w["qkv_w"].ptr + Cw * Cw * 2, Cw, 1, self.kv_local.ptr, 2 * Cw, DT_BF16,
+                   DT_BF16)
+
     def qkv(self, li: int, x_ptr: int, stream=None, timer=None) -> None:
         """q and the local K/V rows of layer ``li``."""
-        p, Cw, w = self.plan, self.C, self.w[li]
-        m, bf = p.m, DT_BF16
-        if self.adaln:
-            x_ptr = self._adaln(li, "mod1", x_ptr, stream, timer)
-        self._gemm("q", timer, stream, m, Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr, Cw, 1,
-                   self.q.ptr, Cw, bf, bf)
-        self._gemm("kv", timer, stream, m, 2 * Cw, Cw, x_ptr, Cw, 0, w["qkv_w"].ptr + Cw * Cw * 2,
-                   Cw, 1, self.kv_local.ptr, 2 * Cw, bf, bf)
+        x_in = self._qkv_input(li, x_ptr, stream, timer)
+        self._q(li, x_in, stream, timer)
+        self._kv(li, x_in, stream, timer)
 
     def exchange(self, stream=None, timer=None) -> None:
         """All-gather the K/V rows of this rank's sample inside its K/V group."""
@@ -465,8 +475,17 @@ class DitStack:
                                        residual_ptr=self.h.ptr, residual_dt=bf, ldr=Cw))
 
     def layer(self, li: int, x_ptr: int, out_ptr: int, stream=None, timer=None) -> None:
-        self.qkv(li, x_ptr, stream, timer)
-        self.exchange(stream, timer)
+        x_in = self._qkv_input(li, x_ptr, stream, timer)
+        if self.comm_stream is not None:
+            # K/V first, so that their gather on the side stream runs during
+            # the Q projection as well as the attention over the own keys
+            self._kv(li, x_in, stream, timer)
+            self.exchange(stream, timer)
+            self._q(li, x_in, stream, timer)
+        else:
+            self._q(li, x_in, stream, timer)
+            self._kv(li, x_in, stream, timer)
+            self.exchange(stream, timer)
         self._attention(stream, timer)
         self.post(li, x_ptr, out_ptr, stream, timer)
 
@@ -501,9 +520,11 @@ class DitStack:
         if self.fused:
             # five linears, then the attention call(s): a split last wave adds a merge launch
             if self.overlap:
-                n_attn = 1 + E.attention_launch_count(1, self.H, p.m, p.tokens, 2, device=self.dev)
+                n_attn = (E.attention_launch_count(1, self.H, p.m, p.m, device=self.dev)
+                          + E.attention_launch_count(1, self.H, p.m, p.tokens, p.token0,
+                                                     p.token0 + p.m, device=self.dev))
             else:
-                n_attn = E.attention_launch_count(p.samples_per_rank, self.H, q_rows, p.tokens, 0,
+                n_attn = E.attention_launch_count(p.samples_per_rank, self.H, q_rows, p.tokens,
                                                   device=self.dev)
             return self.L * (5 + n_attn + self._adaln_launches())
         chunks = (q_rows + self.chunk - 1) // self.chunk

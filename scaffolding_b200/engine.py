@@ -279,15 +279,19 @@ def attention(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride,
           "sf_attention_fwd")
 
 
-def attention_launch_count(batch, heads, q_len, kv_len, part_mode=0, device=None):
+def attention_launch_count(batch, heads, q_len, kv_len, skip_lo=None, skip_hi=None,
+                           device=None):
     """Kernel launches of one attention / attention_partial call of these
-    sizes (sf_attention_launch_count): 1, or 2 with a split last wave."""
+    sizes, keys [skip_lo, skip_hi) skipped (sf_attention_launch_count): 1, or
+    2 when the last wave runs as a stream-K tail followed by a merge."""
+    lo = kv_len if skip_lo is None else skip_lo
+    hi = kv_len if skip_hi is None else skip_hi
     prev = current_device()
     if device is not None and device != prev:
         set_device(device)
     try:
         n = C.c_int32()
-        check(lib.sf_attention_launch_count(batch, heads, q_len, kv_len, part_mode, C.byref(n)),
+        check(lib.sf_attention_launch_count(batch, heads, q_len, kv_len, lo, hi, C.byref(n)),
               "sf_attention_launch_count")
         return n.value
     finally:

@@ -76,8 +76,9 @@ def main():
             # rank's own keys and the gathered ones (another fp32 summation
             # order): the bf16 bar instead of bit equality.
             split = plan.kv_exchange and st.overlap
-            # The split dispatch of the attention's last wave (key-range pieces,
-            # merged) depends on how many query blocks a call has, so it too
+            # The stream-K tail of the attention's last wave (units split into
+            # key-range parts, merged) depends on how many query blocks a call
+            # has, so it too
             # changes the fp32 summation order between the sharded and the
             # one-GPU run; bit equality is required only with it off.
             exact = os.environ.get("SF_ATTN_SPLIT") == "0" and not split

@@ -146,20 +146,24 @@ def test_fused_attention_separate_qkv_lengths(gpu, ops):
     assert device_error(0) == 0
 
 
-@pytest.mark.parametrize("split", ["1", "0"])
+@pytest.mark.parametrize("split", ["2", "0"])
 @pytest.mark.parametrize("B,H,Lq,Lk", [(1, 2, 300, 641), (1, 3, 128, 64), (2, 1, 129, 700),
-                                      (1, 2, 257, 65)])
+                                      (1, 2, 257, 65), (2, 3, 700, 1500)])
 def test_fused_attention_grid_shapes(gpu, ops, monkeypatch, B, H, Lq, Lk, split):
     """Ragged query units (one or both tiles of a 256-row unit holding rows,
     the second tile a single row), ragged and single key blocks, q_len !=
     kv_len and large logits, against the oracle restating the kernel's key
-    block and row bases; with the split last wave (key pieces merged by a
-    second kernel) and with one CTA per unit (SF_ATTN_SPLIT=0)."""
+    block and row bases; with the last wave run as a stream-K tail
+    (SF_ATTN_SPLIT=2 forces it; at 2x3x700x1500 its 27 CTAs of 16 key blocks
+    split every unit, so CTAs run two segments and a merge kernel combines
+    the parts) and with one CTA per unit (SF_ATTN_SPLIT=0)."""
     from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
     monkeypatch.setenv("SF_ATTN_SPLIT", split)
-    if split == "0":
+    if split == "0" or Lk <= 64:
         assert E.attention_launch_count(B, H, Lq, Lk) == 1
+    else:
+        assert E.attention_launch_count(B, H, Lq, Lk) == 2
     rng = np.random.default_rng(Lq * 7 + Lk)
     q32 = rng.standard_normal((B, Lq, H * 64), dtype=np.float32) * np.float32(3)
     k32 = rng.standard_normal((B, Lk, H * 64), dtype=np.float32) * np.float32(3)
@@ -180,14 +184,16 @@ def test_fused_attention_grid_shapes(gpu, ops, monkeypatch, B, H, Lq, Lk, split)
     assert device_error(0) == 0
 
 
-def test_fused_attention_two_streams(gpu, ops):
-    """Split-dispatch calls on two streams at once (each stream has its own
-    piece workspace) give the same bits as the same calls run one by one."""
+def test_fused_attention_two_streams(gpu, ops, monkeypatch):
+    """Stream-K tail calls on two streams at once (each stream has its own
+    workspace for the parts) give the same bits as the same calls run one by
+    one."""
     import ctypes as C
 
     from scaffolding_b200 import engine as E
     from scaffolding_b200._lib import lib
     from tests.gpu_util import device_error
+    monkeypatch.setenv("SF_ATTN_SPLIT", "2")
     B, H, L = 1, 3, 700
     W = H * 64
     assert E.attention_launch_count(B, H, L, L) == 2
@@ -240,18 +246,30 @@ def test_fused_attention_rejects_bad_arguments(gpu, ops):
                                 1.0, 2, None) == SF_ERR_INVALID_ARGUMENT
 
 
-@pytest.mark.parametrize("lo,hi", [(300, 500), (0, 256), (520, 700)])
-def test_fused_attention_split_keys_merge(gpu, ops, lo, hi):
+@pytest.mark.parametrize("lo,hi,Lq,Lk,split", [(300, 500, 200, 700, "1"), (0, 256, 200, 700, "1"),
+                                              (520, 700, 200, 700, "1"),
+                                              (1000, 3200, 300, 5000, "2"),
+                                              (0, 2400, 300, 5000, "2"),
+                                              (2600, 5000, 300, 5000, "2")])
+def test_fused_attention_split_keys_merge(gpu, ops, monkeypatch, lo, hi, Lq, Lk, split):
     """Two-pass attention as the sharded DiT stack runs it: keys [lo, hi)
     from their own buffer (partial result written), then every other key
     (skip [lo, hi)) merged with it.  Equals the one-pass kernel up to fp32
-    summation order, and the oracle with its usual bar."""
+    summation order, and the oracle with its usual bar.  The 5000-key cases
+    force the stream-K tail (SF_ATTN_SPLIT=2) on all three calls: tail CTAs
+    of 16 key blocks split units whose keys straddle the skipped range, and
+    the merge kernel writes the partial result (mode 1) or merges it
+    (mode 2)."""
     import ctypes as C
 
     from scaffolding_b200 import engine as E
     from tests.gpu_util import device_error
+    monkeypatch.setenv("SF_ATTN_SPLIT", split)
     rng = np.random.default_rng(lo + hi)
-    B, H, Lq, Lk = 2, 3, 200, 700
+    B, H = 2, 3
+    if split == "2":
+        assert E.attention_launch_count(B, H, Lq, hi - lo) == 2
+        assert E.attention_launch_count(B, H, Lq, Lk, lo, hi) == 2
     W = H * 64
     gq, q = to_device(ops, rng.standard_normal((B, Lq, W), dtype=np.float32), "bf16")
     gk, k = to_device(ops, rng.standard_normal((B, Lk, W), dtype=np.float32), "bf16")

@@ -218,7 +218,7 @@ def test_stack_small_fused_matches_oracle(gpu, ops):
     x = O.round_bf16(np.random.default_rng(61).standard_normal((B * N, Cw), dtype=np.float32))
     st = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, L, 0, weights=ws, fused=True)
     from scaffolding_b200 import engine as E
-    n_attn = E.attention_launch_count(B, H, N, N)  # 2 here: the last wave is split
+    n_attn = E.attention_launch_count(B, H, N, N)
     assert st.S is None and st.launches_per_forward() == (5 + n_attn) * L
     gx = _upload_x(ops, x)
     cur_ptr, cur = gx.ptr, x
