@@ -78,10 +78,11 @@ static int pick_bn(int64_t n) {
   if (n <= 32) return 32;
   if (n <= 64) return 64;
   if (n <= 128) return 128;
-  // 192 or 256: whichever pads the last N tile less (ties: the larger tile).
-  const int64_t w256 = ceil_div(n, 256) * 256 - n;
-  const int64_t w192 = ceil_div(n, 192) * 192 - n;
-  return w192 < w256 ? 192 : 256;
+  // One 192-wide tile covers N <= 192; wider outputs take 256-wide tiles even
+  // where 192 would pad less.  Measured on B200 (bf16, K = 1920 and 7680,
+  // M = 4444 .. 35552): at N = 1920 (ten 192-wide tiles exactly, or eight
+  // 256-wide with 6.7 % padding) the 256-wide tiles are 13-25 % faster.
+  return n <= 192 ? 192 : 256;
 }
 
 // Skinny pair GEMMs (M <= 256: one 256-row pair tile holds every activation
@@ -149,7 +150,7 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   if (p.tb == 0) {
     pl.kind = kPlanTc;
     pl.b_mn = true;
-    pl.bn = p.N <= 64 ? 64 : (p.N <= 128 ? 128 : (pick_bn(p.N) == 192 ? 192 : 256));
+    pl.bn = pick_bn(p.N) < 64 ? 64 : pick_bn(p.N);
     // Long reductions into narrow outputs (attention P.V: K = keys, N = head
     // dim) average thousands of small terms; keep them IEEE-accurate by
     // promoting TMEM partial sums into fp32 registers every 4 k-blocks.
@@ -226,13 +227,17 @@ static Plan make_plan(const Problem& p, int sm_count, bool have_ptrs) {
   pl.bn = pick_bn(p.N);
   if (pl.bn < 64 && p.M > 4096) pl.bn = 64;
   // CTA pairs over 256-row tiles: a third less operand traffic per SM than
-  // 1-CTA 128-row tiles.  Measured on B200 they win only for wide (BN = 256),
-  // tall GEMMs (the DiT FFN-up shape); elsewhere the 1-CTA kernel is as fast
-  // or faster, so AUTO picks pairs for that class only.  Test hook: SF_PAIR=1
-  // puts every eligible GEMM on the pair kernel (parity of its code paths).
+  // 1-CTA 128-row tiles.  Measured on B200 they pay only for wide (BN = 256),
+  // tall GEMMs with long reductions (the square 16384 shape); on the DiT
+  // linears (K = 1920 and 7680, M = 8888 .. 35552, 256-wide tiles) the 1-CTA
+  // kernel is 0-13 % faster, so AUTO picks pairs for that class only.  Test
+  // hook: SF_PAIR=1 puts every eligible GEMM on the pair kernel (parity of
+  // its code paths).
   if (pl.bn >= 128 && p.M >= 1024 && p.K >= 256 && ovr != SF_KERNEL_TCGEN05_1CTA) {
     const int knob = env_int("SF_PAIR", -1);
-    if (knob == 1 || (knob < 0 && pl.bn == 256 && p.N >= 4096 && p.M >= 16384)) pl.pair = true;
+    if (knob == 1 ||
+        (knob < 0 && pl.bn == 256 && p.N >= 4096 && p.M >= 16384 && p.K >= 8192))
+      pl.pair = true;
   }
   return pl;
 }

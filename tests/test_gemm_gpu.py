@@ -31,8 +31,10 @@ def test_bounded_wait_selftest(gpu, ops):
     np.testing.assert_array_equal(ops.gputensor_to_numpy(ops.dev_muls(a, 2.0)), 2 * np.ones((4, 4)))
 
 
+# N = 160 and 192 take the 192-wide tile (one tile covers N), the others 256 or narrower
 NT_SHAPES = [(128, 256, 64), (256, 512, 512), (300, 200, 136), (129, 257, 72), (512, 16, 64),
-             (64, 4096, 8), (1000, 1000, 1000), (777, 333, 264)]
+             (64, 4096, 8), (1000, 1000, 1000), (777, 333, 264), (300, 160, 136),
+             (777, 192, 264)]
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
