@@ -697,6 +697,8 @@ def run_gpu_arm(args, dist):
 
     if comm is not None:
         E.stream_sync(stream)
+        if stack is not None:
+            stack.close()
         if stack is not None and stack.kv_comm:
             lib.sf_comm_destroy(C.c_void_p(stack.kv_comm))
         lib.sf_comm_destroy(C.c_void_p(comm))

@@ -364,6 +364,36 @@ int32_t sf_comm_async_error(void* comm, int32_t* nccl_result);
 int32_t sf_comm_abort(void* comm);
 int32_t sf_comm_destroy(void* comm);
 
+/* ──────────────────── peer buffers and flags (one node) ──────────────────── */
+/* New (no counterpart in the reference, whose DataParallel moves rows
+ * through the host, nn/parallel.py:111-147, :229-267).  Lets the ranks of a
+ * node exchange device data with copy-engine copies (cudaMemcpyAsync into a
+ * peer's buffer, no SMs used) and order them with sequence flags.
+ *
+ * sf_ipc_alloc: a zeroed device buffer of its own allocation on the current
+ * device, shareable with sf_ipc_handle (64-byte handle, sent to the peers
+ * over any channel) and mapped in a peer process with sf_ipc_open (peer
+ * access enabled on demand); sf_ipc_close unmaps, sf_ipc_free frees (after
+ * every peer has closed its mapping).
+ *
+ * sf_flag_store: after the stream's earlier work, stores `value` to each of
+ * `count` (<= 8) int32 flags (local or peer-mapped; release, system scope).
+ * sf_flag_wait: the stream's later work starts once flags[i * stride] >=
+ * value for every i < count except i == skip (-1: none), read with acquire
+ * loads.  The wait is bounded (timeout_ns, 0 = 2 s): when it expires the
+ * device error word (sf_device_error_status) reads 7 and the stream goes on.
+ * A wait must only depend on stores issued by other GPUs' streams, never on
+ * later work of its own GPU. */
+#define SF_IPC_HANDLE_BYTES 64
+int32_t sf_ipc_alloc(size_t bytes, void** ptr);
+int32_t sf_ipc_free(void* ptr);
+int32_t sf_ipc_handle(void* ptr, uint8_t handle[SF_IPC_HANDLE_BYTES]);
+int32_t sf_ipc_open(const uint8_t handle[SF_IPC_HANDLE_BYTES], void** ptr);
+int32_t sf_ipc_close(void* ptr);
+int32_t sf_flag_store(int32_t* const* flags, int32_t count, int32_t value, void* stream);
+int32_t sf_flag_wait(const int32_t* flags, int32_t count, int32_t stride, int32_t skip,
+                     int32_t value, int64_t timeout_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,6 +101,13 @@ SIGNATURES: dict[str, list] = {
     "sf_host_free_pinned": [_vp],
     "sf_memcpy": [_vp, _vp, _sz, _i32, _vp],
     "sf_memcpy_peer": [_vp, _i32, _vp, _i32, _sz, _vp],
+    "sf_ipc_alloc": [_sz, _P(_vp)],
+    "sf_ipc_free": [_vp],
+    "sf_ipc_handle": [_vp, _P(C.c_uint8)],
+    "sf_ipc_open": [_P(C.c_uint8), _P(_vp)],
+    "sf_ipc_close": [_vp],
+    "sf_flag_store": [_P(_vp), _i32, _i32, _vp],
+    "sf_flag_wait": [_vp, _i32, _i32, _i32, _i32, _i64, _vp],
     "sf_memset": [_vp, _i32, _sz, _vp],
     "sf_stream_create": [_i32, _i32, _P(_vp)],
     "sf_stream_create_priority": [_i32, _i32, _i32, _P(_vp)],

@@ -23,7 +23,8 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(PKG, "libsf_engine.so")
 
-SOURCES = ["runtime.cu", "engine.cu", "attention.cu", "norm.cu", "noalloc.cu", "comm.cpp"]
+SOURCES = ["runtime.cu", "engine.cu", "attention.cu", "norm.cu", "noalloc.cu", "peer.cu",
+           "comm.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevTimeoutDrain = 4,      // abort path could not drain in-flight copies
   kDevBadConfig = 5,         // launch configuration inconsistent with the kernel
   kDevTimeoutSelftest = 6,   // bounded-wait self test expired (expected)
+  kDevTimeoutPeer = 7,       // a flag another GPU stores was not seen in time
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

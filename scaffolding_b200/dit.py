@@ -3,8 +3,8 @@
 Shapes follow the reference ``DiTBlock`` (``diffusion/models.py:490-590``):
 fused ``to_qkv`` (dim -> 3*dim, no bias, ``:508``), ``self_out``
 (dim -> dim, ``:509``), FFN dim -> 4*dim -> dim (``:522-527``; GELU-tanh as
-the benchmark configuration specifies).  Adaptive LayerNorm modulation is not
-part of the matmul path and is omitted.
+the benchmark configuration specifies).  The adaptive LayerNorm modulation
+(``:470-487``) is optional in ``DitStack`` (``adaln=True``).
 
 Block linears (config 4), per token shard x[m, C]:
     qkv = x . Wqkv^T                              [m, 3C]
@@ -133,6 +133,179 @@ class DitBlock:
 
 
 
+# ───────────────────────────── peer K/V exchange ─────────────────────────────
+
+class PeerKV:
+    """Copy-engine K/V exchange inside one K/V group of a token-sharded stack
+    (one process per GPU on one node).
+
+    Every rank of the group owns a ``[tokens, 2C]`` key buffer shared with
+    the others through CUDA IPC; its K/V projection writes its own rows
+    there (rows ``group_rank * m ..``) and side streams, one per peer, push
+    those rows into the peers' buffers with ``cudaMemcpyAsync`` (copy
+    engines over NVLink: no SMs taken from the attention that runs
+    meanwhile).  Order is kept with int32 sequence flags in each rank's flag
+    buffer (``ready[g]`` then ``consumed[g]``), one sequence number per layer:
+
+    * push to peer p: wait until p has consumed the previous layer
+      (``consumed[p] >= seq - 1`` here), copy, store ``p.ready[r] = seq``;
+    * before the attention over the peers' keys: ``ready[q] >= seq`` for all
+      peers q (bounded wait, ``sf_flag_wait``);
+    * after it: store ``p.consumed[r] = seq`` on every peer p;
+    * before the next K/V projection overwrites the own rows: the pushes of
+      the previous layer are done (stream events).
+
+    Each wait depends only on stores made by other GPUs.  Replaces the NCCL
+    all-gather of the K/V rows, whose kernels took SMs from the overlapped
+    attention; handles are swapped once over the group's NCCL communicator.
+    """
+
+    def __init__(self, plan: "ShardPlan", kv_comm, row_bytes: int, device: int):
+        import ctypes as C
+
+        from ._lib import check, lib
+        self.g, self.r, self.m = plan.group_size, plan.group_rank, plan.m
+        self.row_bytes, self.dev, self.kv_comm = row_bytes, device, kv_comm
+        self.seq = 0
+        self._lib, self._C, self._check = lib, C, check
+        with E.on_device(device):
+            self._setup(plan)
+
+    def _setup(self, plan: "ShardPlan") -> None:
+        C, lib, check, device = self._C, self._lib, self._check, self.dev
+        row_bytes = self.row_bytes
+        self.kv_full = self._ipc_alloc(plan.tokens * row_bytes)
+        self.flags = self._ipc_alloc(8 * self.g)
+        # swap (key buffer, flag buffer) handles inside the group
+        hb = 2 * 64
+        mine = np.zeros(hb, np.uint8)
+        for i, ptr in enumerate((self.kv_full, self.flags)):
+            h = (C.c_uint8 * 64)()
+            check(lib.sf_ipc_handle(C.c_void_p(ptr), h), "sf_ipc_handle")
+            mine[i * 64:(i + 1) * 64] = np.frombuffer(bytes(h), np.uint8)
+        allh = self._allgather_host(mine)
+        self.peer_kv, self.peer_flags = {}, {}
+        for p in range(self.g):
+            if p == self.r:
+                continue
+            opened = []
+            for i in range(2):
+                h = (C.c_uint8 * 64).from_buffer_copy(allh[p * hb + i * 64:p * hb + (i + 1) * 64].tobytes())
+                ptr = C.c_void_p()
+                check(lib.sf_ipc_open(h, C.byref(ptr)), "sf_ipc_open")
+                opened.append(ptr.value)
+            self.peer_kv[p], self.peer_flags[p] = opened
+        self.streams, self.ev_push = {}, {}
+        for p in self.peer_kv:
+            sp, ev = C.c_void_p(), C.c_void_p()
+            check(lib.sf_stream_create(device, 1, C.byref(sp)), "sf_stream_create")
+            check(lib.sf_event_create(0, C.byref(ev)), "sf_event_create")
+            self.streams[p], self.ev_push[p] = sp.value, ev.value
+        ev = C.c_void_p()
+        check(lib.sf_event_create(0, C.byref(ev)), "sf_event_create")
+        self.ev_kv = ev.value
+        self.closed = False
+
+    def _ipc_alloc(self, nbytes: int) -> int:
+        p = self._C.c_void_p()
+        self._check(self._lib.sf_ipc_alloc(int(nbytes), self._C.byref(p)), "sf_ipc_alloc")
+        return p.value
+
+    def _allgather_host(self, buf: np.ndarray) -> np.ndarray:
+        """All-gather a small host byte array over the group communicator."""
+        C, lib, check = self._C, self._lib, self._check
+        n = buf.nbytes
+        src = E.DeviceBuffer.alloc(n, self.dev)
+        dst = E.DeviceBuffer.alloc(n * self.g, self.dev)
+        host = np.ascontiguousarray(buf)
+        check(lib.sf_memcpy(C.c_void_p(src.ptr), C.c_void_p(host.ctypes.data), n, 0, None),
+              "sf_memcpy")
+        check(lib.sf_comm_allgather(C.c_void_p(self.kv_comm), C.c_void_p(src.ptr),
+                                    C.c_void_p(dst.ptr), n, None), "sf_comm_allgather")
+        check(lib.sf_device_synchronize(), "sf_device_synchronize")
+        out = np.empty(n * self.g, np.uint8)
+        check(lib.sf_memcpy(C.c_void_p(out.ctypes.data), C.c_void_p(dst.ptr), n * self.g, 1,
+                            None), "sf_memcpy")
+        return out
+
+    def _store(self, ptrs, stream) -> None:
+        C = self._C
+        arr = (C.c_void_p * len(ptrs))(*ptrs)
+        self._check(self._lib.sf_flag_store(arr, len(ptrs), self.seq,
+                                            C.c_void_p(stream) if stream else None),
+                    "sf_flag_store")
+
+    def own_rows(self) -> int:
+        """Device address of this rank's rows in its key buffer."""
+        return self.kv_full + self.r * self.m * self.row_bytes
+
+    def before_kv(self, stream) -> None:
+        """The pushes of the previous layer have read the own rows."""
+        C = self._C
+        for p, ev in self.ev_push.items():
+            self._check(self._lib.sf_stream_wait_event(C.c_void_p(stream) if stream else None,
+                                                       C.c_void_p(ev)), "sf_stream_wait_event")
+
+    def push(self, stream) -> None:
+        """After the K/V projection: push the own rows to every peer."""
+        C, lib, check = self._C, self._lib, self._check
+        self.seq += 1
+        s = C.c_void_p(stream) if stream else None
+        check(lib.sf_event_record(C.c_void_p(self.ev_kv), s), "sf_event_record")
+        off = self.r * self.m * self.row_bytes
+        nbytes = self.m * self.row_bytes
+        for p, ps in self.streams.items():
+            check(lib.sf_stream_wait_event(C.c_void_p(ps), C.c_void_p(self.ev_kv)),
+                  "sf_stream_wait_event")
+            check(lib.sf_flag_wait(C.c_void_p(self.flags + 4 * (self.g + p)), 1, 1, -1,
+                                   self.seq - 1, 0, C.c_void_p(ps)), "sf_flag_wait")
+            check(lib.sf_memcpy(C.c_void_p(self.peer_kv[p] + off), C.c_void_p(self.kv_full + off),
+                                nbytes, 3, C.c_void_p(ps)), "sf_memcpy")
+            self._store([self.peer_flags[p] + 4 * self.r], ps)
+            check(lib.sf_event_record(C.c_void_p(self.ev_push[p]), C.c_void_p(ps)),
+                  "sf_event_record")
+
+    def wait_ready(self, stream) -> None:
+        """Every peer's rows of this layer have landed in the key buffer."""
+        C = self._C
+        self._check(self._lib.sf_flag_wait(C.c_void_p(self.flags), self.g, 1, self.r, self.seq, 0,
+                                           C.c_void_p(stream) if stream else None),
+                    "sf_flag_wait")
+
+    def consumed(self, stream) -> None:
+        """After the attention over the peers' keys: they may push the next layer."""
+        self._store([self.peer_flags[p] + 4 * (self.g + self.r) for p in self.peer_flags], stream)
+
+    def launches_per_layer(self) -> int:
+        """Kernels of the exchange per layer: a flag wait and store on the main
+        stream, a flag wait and store per peer on the push streams."""
+        return 2 + 2 * len(self.peer_kv)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers, then free the own ones once every peer
+        has unmapped them (two group barriers)."""
+        if self.closed:
+            return
+        with E.on_device(self.dev):
+            self._close()
+
+    def _close(self) -> None:
+        C, lib, check = self._C, self._lib, self._check
+        check(lib.sf_device_synchronize(), "sf_device_synchronize")
+        self._allgather_host(np.zeros(4, np.uint8))
+        for p in self.peer_kv:
+            check(lib.sf_ipc_close(C.c_void_p(self.peer_kv[p])), "sf_ipc_close")
+            check(lib.sf_ipc_close(C.c_void_p(self.peer_flags[p])), "sf_ipc_close")
+        self._allgather_host(np.zeros(4, np.uint8))
+        for p in self.streams:
+            lib.sf_stream_destroy(C.c_void_p(self.streams[p]))
+            lib.sf_event_destroy(C.c_void_p(self.ev_push[p]))
+        lib.sf_event_destroy(C.c_void_p(self.ev_kv))
+        check(lib.sf_ipc_free(C.c_void_p(self.kv_full)), "sf_ipc_free")
+        check(lib.sf_ipc_free(C.c_void_p(self.flags)), "sf_ipc_free")
+        self.closed = True
+
+
 # ───────────────────────────── token sharding ─────────────────────────────
 
 class ShardPlan:
@@ -249,9 +422,21 @@ class DitStack:
         spr = plan.samples_per_rank
         keys = plan.tokens
         self.q = ops._alloc((m, Cw), bf, device)
-        self.kv_local = ops._alloc((m, 2 * Cw), bf, device)
-        self.kv_full = (ops._alloc((keys, 2 * Cw), bf, device) if plan.kv_exchange
-                        else self.kv_local)
+        # K/V exchange inside a split sample's rank group: copy-engine pushes
+        # into the peers' key buffers (PeerKV), or the NCCL all-gather (test
+        # hook SF_KV_EXCHANGE=nccl).
+        self.peer = None
+        if (plan.kv_exchange and kv_comm is not None
+                and os.environ.get("SF_KV_EXCHANGE", "ce") != "nccl"):
+            self.peer = PeerKV(plan, kv_comm, 2 * Cw * 2, device)
+            full = E.DeviceBuffer(self.peer.kv_full, keys * 2 * Cw * 2, device, False)
+            own = E.DeviceBuffer(self.peer.own_rows(), m * 2 * Cw * 2, device, False)
+            self.kv_full = ops.GpuTensor(full, (keys, 2 * Cw), bf, device)
+            self.kv_local = ops.GpuTensor(own, (m, 2 * Cw), bf, device)
+        else:
+            self.kv_local = ops._alloc((m, 2 * Cw), bf, device)
+            self.kv_full = (ops._alloc((keys, 2 * Cw), bf, device) if plan.kv_exchange
+                            else self.kv_local)
         q_rows = plan.tokens if plan.whole_samples else m
         crow = min(chunk, q_rows)
         self.S = self.P = None
@@ -298,7 +483,7 @@ class DitStack:
         if self.overlap:
             self.part_o = ops._alloc((m, Cw), np.float32, device)
             self.part_ml = ops._alloc((m, heads, 2), np.float32, device)
-            if kv_comm is not None:
+            if kv_comm is not None and self.peer is None:
                 sp, e1, e2 = C.c_void_p(), C.c_void_p(), C.c_void_p()
                 # high priority: the gather's kernel is scheduled onto SMs as
                 # soon as attention blocks retire instead of after them all
@@ -336,8 +521,10 @@ class DitStack:
                                 self.attn.ptr, Cw, m * Cw, scale, m, m, self.part_o.ptr,
                                 self.part_ml.ptr, 1, dtype=bf, head_dim=D, stream=stream,
                                 device=self.dev)
-            if self.comm_stream is not None:
-                s = stream if stream else E.get_stream(self.dev)
+            s = stream if stream else E.get_stream(self.dev)
+            if self.peer is not None:
+                self.peer.wait_ready(s)
+            elif self.comm_stream is not None:
                 check(lib.sf_stream_wait_event(C.c_void_p(s), C.c_void_p(self.ev_gather)),
                       "sf_stream_wait_event")
             # the group's other keys (the local slice skipped), merged
@@ -346,9 +533,26 @@ class DitStack:
                                 self.attn.ptr, Cw, m * Cw, scale, p.token0, p.token0 + m,
                                 self.part_o.ptr, self.part_ml.ptr, 2, dtype=bf, head_dim=D,
                                 stream=stream, device=self.dev)
+            if self.peer is not None:
+                self.peer.consumed(s)
             if timer is not None:
                 timer.stop("attn")
             return
+        if self.peer is not None:
+            self.peer.wait_ready(stream if stream else E.get_stream(self.dev))
+            self._attention_local(stream, timer)
+            self.peer.consumed(stream if stream else E.get_stream(self.dev))
+            return
+        self._attention_local(stream, timer)
+
+    def _attention_local(self, stream, timer):
+        """Attention of the rank's query rows over the keys in kv_full."""
+        p, Cw, H, D = self.plan, self.C, self.H, self.D
+        keys = p.tokens
+        spr = p.samples_per_rank
+        q_rows = p.tokens if p.whole_samples else p.m
+        scale = 1.0 / math.sqrt(D)
+        bf = DT_BF16
         if self.fused:
             # Q rows of each local sample; K and V in place in the [keys, 2C]
             # rows of kv_full (K at column 0, V at column C, head h at h*64).
@@ -417,6 +621,9 @@ class DitStack:
 
     def _kv(self, li: int, x_ptr: int, stream, timer) -> None:
         p, Cw, w = self.plan, self.C, self.w[li]
+        if self.peer is not None:
+            # the previous layer's pushes have read the rows this overwrites
+            self.peer.before_kv(stream if stream else E.get_stream(self.dev))
         self._gemm("kv", timer, stream, p.m, 2 * Cw, Cw, x_ptr, Cw, 0,
                    w["qkv_w"].ptr + Cw * Cw * 2, Cw, 1, self.kv_local.ptr, 2 * Cw, DT_BF16,
                    DT_BF16)
@@ -434,6 +641,9 @@ class DitStack:
         from ._lib import check, lib
         p = self.plan
         if not p.kv_exchange:
+            return
+        if self.peer is not None:
+            self.peer.push(stream if stream else E.get_stream(self.dev))
             return
         if self.comm_stream is not None:
             # gather on the side stream once the K/V projection is done; the
@@ -476,7 +686,7 @@ class DitStack:
 
     def layer(self, li: int, x_ptr: int, out_ptr: int, stream=None, timer=None) -> None:
         x_in = self._qkv_input(li, x_ptr, stream, timer)
-        if self.comm_stream is not None:
+        if self.comm_stream is not None or self.peer is not None:
             # K/V first, so that their gather on the side stream runs during
             # the Q projection as well as the attention over the own keys
             self._kv(li, x_in, stream, timer)
@@ -526,9 +736,17 @@ class DitStack:
             else:
                 n_attn = E.attention_launch_count(p.samples_per_rank, self.H, q_rows, p.tokens,
                                                   device=self.dev)
-            return self.L * (5 + n_attn + self._adaln_launches())
+            n_peer = self.peer.launches_per_layer() if self.peer is not None else 0
+            return self.L * (5 + n_attn + n_peer + self._adaln_launches())
         chunks = (q_rows + self.chunk - 1) // self.chunk
-        return self.L * (5 + 3 * chunks + self._adaln_launches())
+        n_peer = self.peer.launches_per_layer() if self.peer is not None else 0
+        return self.L * (5 + 3 * chunks + n_peer + self._adaln_launches())
+
+    def close(self) -> None:
+        """Release the peer key buffers (collective over the K/V group: every
+        rank of the group calls it)."""
+        if self.peer is not None:
+            self.peer.close()
 
     def _adaln_launches(self) -> int:
         """Per layer: two modulation linears and two norm kernels (a linear

@@ -2,7 +2,8 @@
 process per GPU; driven by tests/test_multi_gpu.py).
 
 For batch 2 (whole samples per rank) and batch 1 (a sample split across
-ranks, K/V all-gathered inside the sample's group) the gathered output of the
+ranks, K/V exchanged inside the sample's group: copy-engine pushes, or the
+NCCL all-gather with SF_KV_EXCHANGE=nccl) the gathered output of the
 sharded run must equal the output of the same stack run on one GPU bit for
 bit: every row goes through the same kernels over the same keys (the sizes
 keep every shard on the same GEMM path as the single-GPU run).
@@ -59,6 +60,11 @@ def main():
         gx = ops.gputensor_from_numpy(x[plan.row0:plan.row0 + plan.m].astype(bf), dev)
         out_ptr = st.forward(gx.ptr)
         E.check(lib.sf_device_synchronize(), "sync")
+        code = C.c_int32()
+        E.check(lib.sf_device_error_status(dev, C.byref(code), 1), "error status")
+        if code.value != 0:  # e.g. 7: a peer flag wait ran out
+            print(f"[mgpu] rank {rank} device error word {code.value}", flush=True)
+            failures += 1
         got = ops.gputensor_to_numpy(st.out_full).astype(np.float32)
         if rank == 0:
             one = dit.DitStack(dit.ShardPlan(B, N, 1, 0), Cw, H, L, dev, chunk=320, weights=ws)
@@ -69,7 +75,9 @@ def main():
             same = np.array_equal(got, ref)
             ok, stats = O.elementwise_rel_check(got, ref, rtol=1e-2, tau=1e-2)
             differ = int(np.count_nonzero(got != ref))
-            print(f"[mgpu] world={world} batch={B} kv_exchange={plan.kv_exchange} overlap={st.overlap} bitwise_equal={same} "
+            mode = "ce" if st.peer is not None else ("nccl" if plan.kv_exchange else "-")
+            print(f"[mgpu] world={world} batch={B} kv_exchange={plan.kv_exchange} exchange={mode} "
+                  f"overlap={st.overlap} bitwise_equal={same} "
                   f"differing={differ}/{got.size} max_abs_diff={float(np.abs(got - ref).max()):.3e} "
                   f"bf16_bar_ok={ok} rel_frob={O.rel_frobenius(got, ref):.2e}", flush=True)
             # With the K/V exchange overlapped, attention is split into the
@@ -87,6 +95,7 @@ def main():
             close = (O.rel_frobenius(got, ref) < 2e-3
                      and float(np.abs(got - ref).max()) <= 2.0 ** -5 * float(np.abs(ref).max()))
             failures += 0 if (same if exact else close) else 1
+        st.close()
         if kv:
             lib.sf_comm_destroy(C.c_void_p(kv))
         td.barrier()
