@@ -210,10 +210,11 @@ int32_t sf_attention_fwd_partial(int32_t batch, int32_t heads, int32_t q_len, in
 
 /* Kernel launches one sf_attention_fwd or sf_attention_fwd_partial call of
  * these sizes makes on the current device (keys [skip_lo, skip_hi) skipped;
- * skip_lo = skip_hi = kv_len for sf_attention_fwd): 1, or 2 when the last,
+ * skip_lo = skip_hi = kv_len for sf_attention_fwd): 1; or, when the last,
  * partial wave of query blocks runs as a stream-K tail (its key blocks shared
- * evenly by all CTA slots) and a merge kernel combines the split units; 0 for
- * empty sizes.  Lets callers count their launches (no reference counterpart:
+ * evenly by all CTA slots), 3 = the whole units' kernel, the tail kernel and
+ * a merge kernel that combines the split units (2 when every unit is in the
+ * tail); 0 for empty sizes.  Lets callers count their launches (no reference counterpart:
  * the reference's attention chain, nn/functional.py:310-321, launches a fixed
  * sequence). */
 int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_len,

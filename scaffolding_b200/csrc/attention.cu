@@ -27,16 +27,40 @@ namespace {
 // columns and ~96 KB of shared memory, two CTAs per SM.
 using AttnCfg = AttnPpCfg<2, 64, 4>;
 
+// `tail_ctas` stream-K tail CTAs (none when 0), then the whole units on
+// `grid` (none when grid.x == 0).  The tail kernel triggers its dependents at
+// once, so the whole units' kernel, launched with programmatic stream
+// serialisation, starts on the slots the tail CTAs leave: the two run as one
+// grid.  Neither reads what the other writes; work later in the stream waits
+// for both.
 template <bool BF16>
-int32_t launch_attention(const dim3& grid, const CUtensorMap& mq, const CUtensorMap& mk,
-                         const CUtensorMap& mv, const AttnArgs& a, cudaStream_t s, int device) {
+int32_t launch_attention(const dim3& grid, int tail_ctas, const CUtensorMap& mq,
+                         const CUtensorMap& mk, const CUtensorMap& mv, const AttnArgs& a,
+                         cudaStream_t s, int device) {
   static bool attr_set[64] = {false};
   if (device < 64 && !attr_set[device]) {
     SF_CUDA_TRY(cudaFuncSetAttribute(attention_pp_kernel<BF16, AttnCfg>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg::BYTES));
+    SF_CUDA_TRY(cudaFuncSetAttribute(attention_pp_tail_kernel<BF16, AttnCfg>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, AttnCfg::BYTES));
     attr_set[device] = true;
   }
-  attention_pp_kernel<BF16, AttnCfg><<<grid, AttnCfg::THREADS, AttnCfg::BYTES, s>>>(mq, mk, mv, a);
+  if (tail_ctas > 0)
+    attention_pp_tail_kernel<BF16, AttnCfg>
+        <<<dim3(static_cast<unsigned>(tail_ctas)), AttnCfg::THREADS, AttnCfg::BYTES, s>>>(mq, mk, mv, a);
+  if (grid.x > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(AttnCfg::THREADS);
+    cfg.dynamicSmemBytes = AttnCfg::BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = tail_ctas > 0 ? 1 : 0;
+    SF_CUDA_TRY(cudaLaunchKernelEx(&cfg, attention_pp_kernel<BF16, AttnCfg>, mq, mk, mv, a));
+  }
   return SF_OK;
 }
 
@@ -219,11 +243,11 @@ int32_t attention_impl(int32_t batch, int32_t heads, int32_t q_len, int32_t kv_l
       a.tail_units = tp.units;
       a.ws_o = static_cast<float*>(ws.ptr);
       a.ws_ml = a.ws_o + static_cast<size_t>(2 * tp.ctas) * rows * kAttnD;
-      grid = dim3(static_cast<unsigned>(tp.split_first + tp.ctas), 1, 1);
+      grid = dim3(static_cast<unsigned>(tp.split_first), 1, 1);
     }
   }
-  st = dtype == kBF16 ? launch_attention<true>(grid, mq, mk, mv, a, s, device)
-                      : launch_attention<false>(grid, mq, mk, mv, a, s, device);
+  st = dtype == kBF16 ? launch_attention<true>(grid, a.tail_ctas, mq, mk, mv, a, s, device)
+                      : launch_attention<false>(grid, a.tail_ctas, mq, mk, mv, a, s, device);
   if (st != SF_OK) return st;
   SF_CUDA_TRY(cudaGetLastError());
   if (a.split_first >= 0) {
@@ -257,8 +281,9 @@ using namespace sf;
 
 // Number of kernel launches of sf_attention_fwd (part_mode 0, no skipped
 // keys: skip_lo = skip_hi = kv_len) or sf_attention_fwd_partial for these
-// sizes on the current device: 1, or 2 when the last wave runs as a
-// stream-K tail and a merge kernel follows.
+// sizes on the current device: 1; or, when the last wave runs as a stream-K
+// tail, the tail kernel, the whole units' kernel and the merge kernel (3; 2
+// when every unit is in the tail).
 extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32_t q_len,
                                              int32_t kv_len, int32_t skip_lo, int32_t skip_hi,
                                              int32_t* count) {
@@ -274,7 +299,7 @@ extern "C" int32_t sf_attention_launch_count(int32_t batch, int32_t heads, int32
   attn_key_blocks(kv_len, skip_lo, skip_hi, &na, &ne);
   const int64_t units = ceil_div(q_len, AttnCfg::ROWS) * heads * batch;
   const AttnTail tp = attn_tail_plan(units, AttnCfg::MIN_BLOCKS * dev->sm_count, ne);
-  *count = tp.split_first >= 0 ? 2 : 1;
+  *count = tp.split_first < 0 ? 1 : (tp.split_first > 0 ? 3 : 2);
   return SF_OK;
 }
 

@@ -43,11 +43,11 @@ struct AttnArgs {
   // [0, skip_lo), then blocks from skip_hi cover [skip_hi, kv_len); nkb_e
   // blocks in all (the unit's effective blocks).
   int nkb_a, nkb_e;
-  // Stream-K tail, so that the last wave of CTAs is not partly empty: a 1-D
-  // grid whose blocks [0, split_first) are whole units u (query block
-  // u % nqb, head (u / nqb) % heads, batch u / (nqb * heads)) and whose
-  // tail_ctas further blocks share the effective key blocks of the last
-  // tail_units units laid end to end: tail CTA c takes blocks
+  // Stream-K tail, so that the last wave of CTAs is not partly empty: the
+  // tail kernel's tail_ctas CTAs share the effective key blocks of the last
+  // tail_units units laid end to end, and the whole-unit kernel runs the first
+  // split_first units on a 1-D grid (unit u = query block u % nqb, head
+  // (u / nqb) % heads, batch u / (nqb * heads)) on the slots they leave: tail CTA c takes blocks
   // [c W / T, (c + 1) W / T) (W = tail_units * nkb_e, T = tail_ctas >=
   // tail_units), one or two segments (parts of consecutive units).  A
   // segment that covers a whole unit writes its output as usual; a part of

@@ -95,39 +95,30 @@ struct PpSeg {
   __device__ __forceinline__ int valid(int j) const { return min(KB, (j < nb0 ? e0 : k1) - start(j)); }
 };
 
-// Segments of this CTA: one for a whole unit, one or two for a tail CTA
-// (its block range is at most one unit long, so it meets at most two units).
+// Segments of tail CTA blockIdx.x: one or two (its block range is at most one
+// unit long, so it meets at most two units; none when the range is empty).
 __device__ __forceinline__ int pp_nseg(const AttnArgs& p) {
-  if (p.split_first < 0 || static_cast<int>(blockIdx.x) < p.split_first) return 1;
-  const int c = static_cast<int>(blockIdx.x) - p.split_first;
+  const int c = static_cast<int>(blockIdx.x);
   const int64_t lo = attn_tail_lo(p, c), hi = attn_tail_lo(p, c + 1);
   if (hi <= lo) return 0;
   return static_cast<int>((hi - 1) / p.nkb_e - lo / p.nkb_e) + 1;
 }
 
+// Segment i of tail CTA blockIdx.x: a part (or the whole) of tail unit
+// split_first + ur, effective key blocks [ea, eb).
 template <int KB>
-__device__ __forceinline__ PpSeg<KB> pp_seg(const AttnArgs& p, int i) {
+__device__ __forceinline__ PpSeg<KB> pp_tail_seg(const AttnArgs& p, int i) {
   PpSeg<KB> w;
-  int ea = 0, eb = p.nkb_e, u = static_cast<int>(blockIdx.x);
-  w.slot = -1;
-  if (p.split_first < 0) {
-    w.qb = blockIdx.x;
-    w.h = blockIdx.y;
-    w.b = blockIdx.z;
-  } else {
-    if (u >= p.split_first) {
-      const int c = u - p.split_first;
-      const int64_t lo = attn_tail_lo(p, c), hi = attn_tail_lo(p, c + 1);
-      const int64_t ur = lo / p.nkb_e + i, u0 = ur * p.nkb_e;
-      ea = static_cast<int>(max(lo, u0) - u0);
-      eb = static_cast<int>(min(hi, u0 + p.nkb_e) - u0);
-      u = p.split_first + static_cast<int>(ur);
-      if (ea > 0 || eb < p.nkb_e) w.slot = 2 * c + i;
-    }
-    w.qb = u % p.nqb;
-    w.h = (u / p.nqb) % p.heads;
-    w.b = u / (p.nqb * p.heads);
-  }
+  const int c = static_cast<int>(blockIdx.x);
+  const int64_t lo = attn_tail_lo(p, c), hi = attn_tail_lo(p, c + 1);
+  const int64_t ur = lo / p.nkb_e + i, u0 = ur * p.nkb_e;
+  const int ea = static_cast<int>(max(lo, u0) - u0);
+  const int eb = static_cast<int>(min(hi, u0 + p.nkb_e) - u0);
+  const int u = p.split_first + static_cast<int>(ur);
+  w.slot = (ea > 0 || eb < p.nkb_e) ? 2 * c + i : -1;
+  w.qb = u % p.nqb;
+  w.h = (u / p.nqb) % p.heads;
+  w.b = u / (p.nqb * p.heads);
   const int na = p.nkb_a;
   w.nb0 = max(0, min(eb, na) - ea);
   w.k0 = ea * KB;
@@ -138,6 +129,32 @@ __device__ __forceinline__ PpSeg<KB> pp_seg(const AttnArgs& p, int i) {
   return w;
 }
 
+// A whole unit: the 3-D grid (query unit, head, batch), or unit blockIdx.x
+// of the 1-D grid of the first split_first units when a stream-K tail runs
+// the rest; every key but [skip_lo, skip_hi).
+template <int KB>
+__device__ __forceinline__ PpSeg<KB> pp_unit(const AttnArgs& p) {
+  PpSeg<KB> w;
+  if (p.split_first < 0) {
+    w.qb = blockIdx.x;
+    w.h = blockIdx.y;
+    w.b = blockIdx.z;
+  } else {
+    const int u = static_cast<int>(blockIdx.x);
+    w.qb = u % p.nqb;
+    w.h = (u / p.nqb) % p.heads;
+    w.b = u / (p.nqb * p.heads);
+  }
+  w.slot = -1;
+  w.k0 = 0;
+  w.k1 = p.kv_len;
+  w.e0 = min(w.k1, p.skip_lo);
+  w.s1 = max(w.k0, p.skip_hi);
+  w.nb0 = w.e0 > w.k0 ? (w.e0 - w.k0 + KB - 1) / KB : 0;
+  w.nblk = w.nb0 + (w.k1 > w.s1 ? (w.k1 - w.s1 + KB - 1) / KB : 0);
+  return w;
+}
+
 // Query tiles of a segment that hold rows (past q_len they are skipped; a
 // unit is never empty).
 template <class Cfg, int KB>
@@ -145,12 +162,380 @@ __device__ __forceinline__ int pp_tiles(const AttnArgs& p, const PpSeg<KB>& w) {
   return min(Cfg::NT, (p.q_len - w.qb * Cfg::ROWS + 127) / 128);
 }
 
+// Whole units, one per CTA (pp_unit).  When a stream-K tail runs, this is
+// launched after the tail kernel with programmatic stream serialisation and
+// takes the SM slots the tail CTAs leave; it reads nothing they write.
 template <bool BF16, class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     attention_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int ST = Cfg::KV_STAGES, NT = Cfg::NT, KB = Cfg::KB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t& q_full = bars[0];
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + ST;
+  uint64_t* s_full = kv_empty + ST;   // [NT]: S_t(j) ready (covers O_t += P_t(j-1) V)
+  uint64_t* p_full = s_full + NT;     // [NT]: P_t(j) stored (4 warp arrivals)
+  uint64_t* o_last = p_full + NT;     // [NT]: the last P.V of tile t done
+  uint64_t& drain_bar = o_last[NT];
+  uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(&o_last[NT + 1]);
+  int& abort_flag = *(reinterpret_cast<int*>(&o_last[NT + 1]) + 1);
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadConfig);
+    return;
+  }
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const PpSeg<KB> w = pp_unit<KB>(p);
+  const int nblk = w.nblk;
+  // Only tiles that hold query rows run (the unit is never empty).
+  const int ntiles = min(NT, (p.q_len - w.qb * Cfg::ROWS + 127) / 128);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_last[t], 1);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == Cfg::TMA_WARP && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == Cfg::MMA_WARP) {
+    tmem_alloc(&tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  volatile int* abortp = &abort_flag;
+
+  if (warp == Cfg::TMA_WARP) {
+    // ───────────── TMA producer ─────────────
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0, stage = 0;
+      uint32_t phase = 0;
+      mbar_arrive_expect_tx(&q_full, ntiles * Cfg::Q_TILE);
+      for (int t = 0; t < ntiles; ++t)
+        tma_load_4d(smem + Cfg::Q_OFF + t * Cfg::Q_TILE, &tmQ, &q_full, 0,
+                    w.qb * Cfg::ROWS + t * 128, w.h, w.b);
+      for (int j = 0; j < nblk; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, p.err, kDevTimeoutProducer, abortp)) {
+          ok = false;
+          break;
+        }
+        uint8_t* kt = smem + Cfg::KV_OFF + stage * 2 * Cfg::KV_TILE;
+        mbar_arrive_expect_tx(&kv_full[stage], 2 * Cfg::KV_TILE);
+        const int ks = w.start(j);
+        tma_load_4d(kt, &tmK, &kv_full[stage], 0, ks, w.h, w.b);
+        tma_load_4d(kt + Cfg::KV_TILE, &tmV, &kv_full[stage], 0, ks, w.h, w.b);
+        ++issued;
+        if (++stage == ST) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!mbar_wait_quiet(&q_full, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      if (!ok) {
+        // Wait for the copies still in flight before the CTA exits.
+        const int n = issued < ST ? issued : ST;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = ST - 1;
+            ph ^= 1u;
+          }
+          if (!mbar_wait_quiet(&kv_full[s], ph, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == Cfg::MMA_WARP) {
+    // ───────────── MMA issuer ─────────────
+    // Tiles are served out of order: whenever tile t's P for block j-1 is
+    // stored and block j's K/V are loaded, O_t += P_t(j-1) V(j-1) and
+    // S_t(j) are issued for it, whatever the other tiles are doing, so a
+    // slow tile never holds back the others.  A K/V stage is released once
+    // every running tile has issued its P.V on it (the commit covers all
+    // MMAs issued before it).  Tiles can drift apart by up to KV_STAGES-1
+    // blocks; the producer refills stages in block order.
+    if (lane == 0) {
+      const uint32_t fmt = BF16 ? 1u : 0u;
+      const uint32_t idesc_s = make_idesc(fmt, 128, KB, 0u, 0u);
+      const uint32_t idesc_o = make_idesc(fmt, 128, 64, 0u, 1u);
+      bool ok = nblk == 0 || mbar_wait(&q_full, 0, p.err, kDevTimeoutMma, abortp);
+      bool issued_any = false;
+      int jt[NT];                 // next block each tile issues S for (P.V of jt-1 with it)
+      int pv_done[ST];            // tiles that have issued their P.V on each stage's block
+#pragma unroll
+      for (int t = 0; t < NT; ++t) jt[t] = 0;
+#pragma unroll
+      for (int s2 = 0; s2 < ST; ++s2) pv_done[s2] = 0;
+      int finished = 0;
+      unsigned long long t_last = global_timer_ns();
+      while (ok && finished < ntiles) {
+        bool progress = false;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          if (t >= ntiles) continue;
+          const int j = jt[t];
+          if (j > nblk) continue;
+          if (j > 0 && !mbar_test(&p_full[t], static_cast<uint32_t>(j - 1) & 1u)) continue;
+          if (j < nblk && !mbar_test(&kv_full[j % ST], static_cast<uint32_t>(j / ST) & 1u)) continue;
+          tc_fence_after();
+          if (j > 0) {
+            // O_t += P_t(j-1) V(j-1), P from TMEM, V MN-major from its stage.
+            const int ps = (j - 1) % ST;
+            const uint32_t v_addr = smem_u32(smem + Cfg::KV_OFF + ps * 2 * Cfg::KV_TILE + Cfg::KV_TILE);
+#pragma unroll
+            for (int ks = 0; ks < KB / 16; ++ks) {
+              const uint64_t bd = make_sw128_desc(v_addr + ks * 2048, Cfg::KV_TILE, 1024);
+              umma_f16_tmem_a(tmem_base + Cfg::O_COL + t * 64,
+                              tmem_base + Cfg::S_COL + t * KB + ks * 8, bd, idesc_o,
+                              (j > 1 || ks > 0) ? 1u : 0u);
+            }
+            if (++pv_done[ps] == ntiles) {
+              pv_done[ps] = 0;
+              umma_commit(&kv_empty[ps]);
+            }
+            if (j == nblk) umma_commit(&o_last[t]);
+          }
+          if (j < nblk) {
+            const uint32_t q_addr = smem_u32(smem + Cfg::Q_OFF + t * Cfg::Q_TILE);
+            const uint32_t k_addr = smem_u32(smem + Cfg::KV_OFF + (j % ST) * 2 * Cfg::KV_TILE);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t ad = make_sw128_desc(q_addr + ks * 32, 16, 1024);
+              const uint64_t bd = make_sw128_desc(k_addr + ks * 32, 16, 1024);
+              umma_f16(tmem_base + Cfg::S_COL + t * KB, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+            }
+            issued_any = true;
+            umma_commit(&s_full[t]);
+          }
+          jt[t] = j + 1;
+          if (j == nblk) ++finished;
+          progress = true;
+        }
+        if (progress) {
+          t_last = global_timer_ns();
+        } else if (*abortp) {
+          ok = false;
+        } else if (global_timer_ns() - t_last > kWaitLimitNs) {
+          *abortp = 1;
+          atomicCAS(p.err, 0, kDevTimeoutMma);
+          ok = false;
+        }
+      }
+      if (!ok && issued_any) {
+        umma_commit(&drain_bar);
+        if (!mbar_wait_quiet(&drain_bar, 0, 200000000ull)) atomicCAS(p.err, 0, kDevTimeoutDrain);
+      }
+    }
+  } else if ((warp >> 2) < ntiles) {
+    // ───────────── softmax of tile t: one thread per query row ─────────────
+    const int t = warp >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;                 // row within the tile
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_base + Cfg::S_COL + t * KB;
+    const uint32_t o_addr = tmem_base + lane_base + Cfg::O_COL + t * 64;
+    float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
+    const float c = p.scale_log2;
+    bool ok = true;
+    uint32_t r[KB > 64 ? KB : 64];
+    // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
+    auto rescale_o = [&](float alpha) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(o_addr + half * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+        tmem_st32(o_addr + half * 32, r);
+      }
+    };
+    for (int j = 0; j < nblk; ++j) {
+      // Waits end the loop for the whole warp together: the TMEM loads and
+      // stores that follow are warp-collective.
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1u, p.err,
+                                             kDevTimeoutEpilogue, abortp))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+      tmem_ld_wait();
+      const int valid = w.valid(j);
+      const bool full = valid == KB;
+      float mx;
+      if (full) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int i = 0; i < KB; i += 8) {
+          m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+          m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+        }
+        mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+      } else {
+        mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < KB; ++i)
+          if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float cand = ceilf(mx * c);
+      const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+      const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+      const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
+      if (need) {
+        l_run *= alpha;
+        m_run = cand;
+      }
+      const float nm = -m_run;
+      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
+        float* pv = reinterpret_cast<float*>(r + ch * 32);
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float x0, x1;
+            fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
+            pv[i] = ex2_approx(x0);
+            pv[i + 1] = ex2_approx(x1);
+            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float e = ex2_approx(fmaf(pv[i], c, nm));
+            pv[i] = ch * 32 + i < valid ? e : 0.0f;
+            sp[i & 7] += pv[i];
+          }
+        }
+        // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first),
+        // over score columns this thread has already read.
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_16bit(pv[2 * i], pv[2 * i + 1], BF16);
+        tmem_st16(s_addr + ch * 16, pk);
+      }
+      l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
+      // is issued only after the arrival below.
+      if (rescale) rescale_o(alpha);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && nblk > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
+    const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
+    if (ok) {
+      tc_fence_after();
+      const bool live = qrow < p.q_len;
+      const int64_t prow = (static_cast<int64_t>(w.b) * p.q_len + qrow) * p.heads + w.h;
+      // A split piece writes its partial result to its workspace slot.
+      const int mode = w.slot >= 0 ? 1 : p.part_mode;
+      const int urow = t * 128 + row;
+      float* const pml = w.slot >= 0 ? p.ws_ml + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * 2
+                                     : p.part_ml + 2 * prow;
+      float* const pob = w.slot >= 0
+                             ? p.ws_o + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * kAttnD
+                             : p.part_o + prow * kAttnD;
+      // Merge with a partial result over other keys: both bases are integers,
+      // so the rescale factors are exact powers of two.
+      float a_own = 1.0f, a_part = 0.0f;
+      if (mode == 2 && live) {
+        const float m_p = pml[0], l_p = pml[1];
+        const float m = fmaxf(m_run, m_p);
+        a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
+        a_part = ex2_approx(m_p - m);
+        l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
+      }
+      if (mode == 1 && live) {
+        pml[0] = m_run;
+        pml[1] = l_run;
+      }
+      const float inv = 1.0f / l_run;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
+                     (static_cast<int64_t>(w.b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
+                      static_cast<int64_t>(w.h) * kAttnD) * 2;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        tmem_ld32(o_addr + half * 32, r);
+        tmem_ld_wait();
+        if (!live) continue;
+        if (mode == 1) {
+          float4* po = reinterpret_cast<float4*>(pob + half * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            po[q] = nblk > 0 ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          continue;
+        }
+        float ov[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] = nblk > 0 ? __uint_as_float(r[i]) : 0.0f;
+        if (mode == 2) {
+          const float4* po = reinterpret_cast<const float4*>(pob + half * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = po[q];
+            ov[4 * q] = ov[4 * q] * a_own + v.x * a_part;
+            ov[4 * q + 1] = ov[4 * q + 1] * a_own + v.y * a_part;
+            ov[4 * q + 2] = ov[4 * q + 2] * a_own + v.z * a_part;
+            ov[4 * q + 3] = ov[4 * q + 3] * a_own + v.w * a_part;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(dst)[half * 4 + q] =
+              make_uint4(pack_16bit(ov[8 * q] * inv, ov[8 * q + 1] * inv, BF16),
+                         pack_16bit(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv, BF16),
+                         pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
+                         pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == Cfg::MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// Stream-K tail CTA blockIdx.x: one or two segments (pp_nseg, pp_tail_seg)
+// through the same barriers.  Launched before the whole units' kernel, which
+// it lets start at once (its CTAs take the slots this kernel leaves).
+template <bool BF16, class Cfg>
+__global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
+    attention_pp_tail_kernel(const __grid_constant__ CUtensorMap tmQ,
+                             const __grid_constant__ CUtensorMap tmK,
+                             const __grid_constant__ CUtensorMap tmV, const AttnArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (threadIdx.x == 0) pdl_launch_dependents();
   constexpr int ST = Cfg::KV_STAGES, NT = Cfg::NT, KB = Cfg::KB;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t& q_full = bars[0];
@@ -214,7 +599,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       int issued = 0, stage = 0, nq = 0;
       uint32_t phase = 0;
       for (int si = 0; si < nseg && ok; ++si) {
-        const PpSeg<KB> w = pp_seg<KB>(p, si);
+        const PpSeg<KB> w = pp_tail_seg<KB>(p, si);
         if (w.nblk == 0) continue;
         const int nt = pp_tiles<Cfg>(p, w);
         if (nq > 0 && !mbar_wait(&q_empty, static_cast<uint32_t>(nq - 1) & 1u, p.err,
@@ -284,7 +669,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       for (int s2 = 0; s2 < ST; ++s2) pv_done[s2] = 0;
       int g0 = 0, nq = 0;         // K/V blocks and Q loads of the earlier segments
       for (int si = 0; si < nseg && ok; ++si) {
-        const PpSeg<KB> w = pp_seg<KB>(p, si);
+        const PpSeg<KB> w = pp_tail_seg<KB>(p, si);
         const int nblk = w.nblk;
         if (nblk == 0) continue;
         const int nt = pp_tiles<Cfg>(p, w);
@@ -389,7 +774,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       }
     };
     for (int si = 0; si < nseg && ok; ++si) {
-      const PpSeg<KB> w = pp_seg<KB>(p, si);
+      const PpSeg<KB> w = pp_tail_seg<KB>(p, si);
       if (t >= pp_tiles<Cfg>(p, w)) continue;
       const int nblk = w.nblk;
       float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)

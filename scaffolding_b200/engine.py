@@ -282,8 +282,9 @@ def attention(batch, heads, q_len, kv_len, q, ldq, q_bstride, k, ldk, k_bstride,
 def attention_launch_count(batch, heads, q_len, kv_len, skip_lo=None, skip_hi=None,
                            device=None):
     """Kernel launches of one attention / attention_partial call of these
-    sizes, keys [skip_lo, skip_hi) skipped (sf_attention_launch_count): 1, or
-    2 when the last wave runs as a stream-K tail followed by a merge."""
+    sizes, keys [skip_lo, skip_hi) skipped (sf_attention_launch_count): 1;
+    with a stream-K tail, the whole units' kernel, the tail kernel and the
+    merge kernel (2 when every unit is in the tail)."""
     lo = kv_len if skip_lo is None else skip_lo
     hi = kv_len if skip_hi is None else skip_hi
     prev = current_device()
