@@ -382,60 +382,90 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       tmem_ld_wait();
       const int valid = w.valid(j);
       const bool full = valid == KB;
-      float mx;
-      if (full) {
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < KB; i += 8) {
-          m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-          m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-          m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-        }
-        mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-      } else {
-        mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < KB; ++i)
-          if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      const float cand = ceilf(mx * c);
-      const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-      const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-      const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
-      if (need) {
-        l_run *= alpha;
-        m_run = cand;
-      }
-      const float nm = -m_run;
       float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      // A full block after the first: p = 2^(c s - m) with the row's current
+      // base first.  When every row's block sum is below 2^7, every p is, so
+      // the exact test below (raise when some p would exceed 2^8) raises no
+      // base and would compute the same p: the row max is skipped.  Else the
+      // scores are read again (P is not stored yet) and the exact path runs.
+      // Packed P of the block: keys 2i, 2i+1 in pk[i].
+      uint32_t pk[KB / 2];
+      bool fast = false;
+      if (j > 0 && full) {
+        const float nm = -m_run;
 #pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-        float* pv = reinterpret_cast<float*>(r + ch * 32);
+        for (int i = 0; i < KB; i += 2) {
+          float x0, x1, e0, e1;
+          fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
+          e0 = ex2_approx(x0);
+          e1 = ex2_approx(x1);
+          add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+          pk[i >> 1] = pack_16bit(e0, e1, BF16);
+        }
+        const float bs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+        fast = __all_sync(0xffffffffu, bs < 128.0f);
+        if (!fast) {
+#pragma unroll
+          for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+        }
+      }
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (!fast) {
+        float mx;
+        if (full) {
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int i = 0; i < KB; i += 8) {
+            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+          }
+          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+        } else {
+          mx = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < KB; ++i)
+            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
+        const float cand = ceilf(mx * c);
+        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+        alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+        rescale = j >= 1 && __any_sync(0xffffffffu, need);
+        if (need) {
+          l_run *= alpha;
+          m_run = cand;
+        }
+        const float nm = -m_run;
         if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            float x0, x1;
-            fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
-            pv[i] = ex2_approx(x0);
-            pv[i + 1] = ex2_approx(x1);
-            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
+          for (int i = 0; i < KB; i += 2) {
+            float x0, x1, e0, e1;
+            fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+            pk[i >> 1] = pack_16bit(e0, e1, BF16);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float e = ex2_approx(fmaf(pv[i], c, nm));
-            pv[i] = ch * 32 + i < valid ? e : 0.0f;
-            sp[i & 7] += pv[i];
+          for (int i = 0; i < KB; i += 2) {
+            const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
+            const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
+            sp[i & 7] += e0;
+            sp[(i + 1) & 7] += e1;
+            pk[i >> 1] = pack_16bit(e0, e1, BF16);
           }
         }
-        // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first),
-        // over score columns this thread has already read.
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_16bit(pv[2 * i], pv[2 * i + 1], BF16);
-        tmem_st16(s_addr + ch * 16, pk);
       }
+      // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first), over
+      // score columns already read.
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
       l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
       // is issued only after the arrival below.
@@ -792,60 +822,86 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
         tmem_ld_wait();
         const int valid = w.valid(j);
         const bool full = valid == KB;
-        float mx;
-        if (full) {
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int i = 0; i < KB; i += 8) {
-            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-          }
-          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-        } else {
-          mx = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < KB; ++i)
-            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-        }
-        const float cand = ceilf(mx * c);
-        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-        const float alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-        const bool rescale = j >= 1 && __any_sync(0xffffffffu, need);
-        if (need) {
-          l_run *= alpha;
-          m_run = cand;
-        }
-        const float nm = -m_run;
         float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        // The row max is skipped when every row's block sum under the current
+        // base is below 2^7 (as in attention_pp_kernel).
+        uint32_t pk[KB / 2];
+        bool fast = false;
+        if (j > 0 && full) {
+          const float nm = -m_run;
 #pragma unroll
-        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) {
-          float* pv = reinterpret_cast<float*>(r + ch * 32);
+          for (int i = 0; i < KB; i += 2) {
+            float x0, x1, e0, e1;
+            fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+            pk[i >> 1] = pack_16bit(e0, e1, BF16);
+          }
+          const float bs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+          fast = __all_sync(0xffffffffu, bs < 128.0f);
+          if (!fast) {
+#pragma unroll
+            for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+          }
+        }
+        float alpha = 1.0f;
+        bool rescale = false;
+        if (!fast) {
+          float mx;
+          if (full) {
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < KB; i += 8) {
+              m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+              m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+              m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+              m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+            }
+            mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+          } else {
+            mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < KB; ++i)
+              if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+          }
+          const float cand = ceilf(mx * c);
+          const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+          alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+          rescale = j >= 1 && __any_sync(0xffffffffu, need);
+          if (need) {
+            l_run *= alpha;
+            m_run = cand;
+          }
+          const float nm = -m_run;
           if (full) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
-              float x0, x1;
-              fma2(x0, x1, pv[i], pv[i + 1], c, c, nm, nm);
-              pv[i] = ex2_approx(x0);
-              pv[i + 1] = ex2_approx(x1);
-              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], pv[i], pv[i + 1]);
+            for (int i = 0; i < KB; i += 2) {
+              float x0, x1, e0, e1;
+              fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
+              e0 = ex2_approx(x0);
+              e1 = ex2_approx(x1);
+              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+              pk[i >> 1] = pack_16bit(e0, e1, BF16);
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float e = ex2_approx(fmaf(pv[i], c, nm));
-              pv[i] = ch * 32 + i < valid ? e : 0.0f;
-              sp[i & 7] += pv[i];
+            for (int i = 0; i < KB; i += 2) {
+              const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
+              const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
+              sp[i & 7] += e0;
+              sp[(i + 1) & 7] += e1;
+              pk[i >> 1] = pack_16bit(e0, e1, BF16);
             }
           }
-          // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first),
-          // over score columns this thread has already read.
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = pack_16bit(pv[2 * i], pv[2 * i + 1], BF16);
-          tmem_st16(s_addr + ch * 16, pk);
         }
+        // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first), over
+        // score columns already read.
+#pragma unroll
+        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
         l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
         // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
         // is issued only after the arrival below.
