@@ -626,7 +626,9 @@ def run_gpu_arm(args, dist):
             roof["launch_ms_mean"] = ms_top
             if top == "attn":
                 roof["kernel"] = ("sf::attention_pp_kernel<AttnPpCfg<2, 64, 4>> (tcgen05, fused "
-                                  "QK^T-softmax-PV, two query tiles per CTA, P in TMEM)")
+                                  "QK^T-softmax-PV, two query tiles per CTA, P in TMEM; with "
+                                  "attention_pp_tail_kernel and attention_merge_kernel when the "
+                                  "last wave runs as a stream-K tail: the time is the call's)")
                 roof["algorithmic_flops_per_launch"] = fl
         roof["kernel_share"] = totals[top] / sum(totals.values())
         roof["top_kernel"] = top

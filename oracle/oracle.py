@@ -311,8 +311,9 @@ def flash_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
     (``m' = max(m, ceil(c * max_j s_ij))``).  With integer bases the rounding
     of ``2^(c s - m)`` does not depend on which base is used (a change of base
     scales every p by an exact power of two), so this also stands for the
-    device kernel that raises its integer base only when a block exceeds it
-    by more than 8.
+    device kernel, which sets a row's base from its first block and raises
+    it (to ``ceil(c * block max)``) only when a block's ``p`` under the
+    current base sum to ``2^8`` or more.
 
     With ``return_allowance`` it also returns, per output element, the
     change that rounding p the other way could cause for every p lying

@@ -118,8 +118,24 @@ __device__ __forceinline__ uint32_t pack_16bit(float a, float b, bool bf16) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Row exponent bases are raised only when a block's ceil(c * max) exceeds
-// them by more than this (p then stays below 2^8 before the rescale).
+// Two 16-bit products a * b (bf16x2 or f16x2, round to nearest).
+__device__ __forceinline__ uint32_t mul_16bit2(uint32_t a, uint32_t b, bool bf16) {
+  if (bf16) {
+    const __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  }
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// Sum-first softmax: a row keeps its integer exponent base while the
+// p = 2^(c s - m) of a key block sum to less than this; a block that reaches
+// it raises the base by floor(log2 sum) + 1.
+constexpr float kAttnSumLimit = 256.0f;
+
+// Max-first softmax: the base is raised to ceil(c * block max) only when that
+// exceeds it by more than this (p then stays below 2^8 before the rescale).
 constexpr float kAttnRescaleLog2 = 8.0f;
 
 // Combines the parts of each split tail unit, and in part_mode 2 the

@@ -35,13 +35,22 @@
 // tensor-core time per score at head_dim 64) and the tensor core overlap.
 //
 // Softmax (per row, log2 domain, c = scale * log2(e)): the row's integer
-// exponent base m is raised only when a block's ceil(c * max) exceeds it by
-// more than kAttnRescaleLog2, and then the row of O_t in TMEM is scaled by
-// 2^(m_old - m_new) (warp-collective load, multiply, store; factor 1 on the
-// warp's other rows).  Because m is an integer, the 16-bit rounding of
-// p = 2^(c s - m) does not depend on which base is in force (a change of
-// base is an exact power-of-two scale).
-//
+// exponent base m is set by its first block (ceil(c * max)).  After that a
+// warp works sum-first: p = 2^(c s - m) is formed with the current base
+// (packed to 16 bits as it is formed, stored after the checks), and the base
+// changes only when a block's p sum to kAttnSumLimit (2^8) or more: m then
+// rises by k = floor(log2 sum) + 1, taken from the sum's exponent bits, and
+// the block's p, packed P and sum, the row's l and its row of O_t in TMEM all
+// scale by the exact power of two 2^-k (O: warp-collective load, multiply,
+// store; factor 1 on the warp's other rows).  No row max is computed.  A sum
+// too large to scale that way, or not finite (huge or non-finite scores),
+// switches the warp to max-first for the rest of its unit: the scores are
+// read from TMEM again, and from then on every block takes the row max first
+// and raises m to ceil(c * max) only when that exceeds m by more than
+// kAttnRescaleLog2.  Because m is an integer, the 16-bit rounding of p does
+// not depend on which base is in force (a change of base is an exact
+// power-of-two scale), and every stored p is below 2^8.
+
 // Tiles of a unit that hold no query rows (past q_len) are skipped.  Keys
 // past kv_len (TMA zero-fills them) and skipped keys are masked to p = 0;
 // query rows past q_len are computed and not stored.  The partial modes,
@@ -368,31 +377,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
         tmem_st32(o_addr + half * 32, r);
       }
     };
-    for (int j = 0; j < nblk; ++j) {
-      // Waits end the loop for the whole warp together: the TMEM loads and
-      // stores that follow are warp-collective.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1u, p.err,
-                                             kDevTimeoutEpilogue, abortp))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    // P of a block: keys 2i, 2i+1 packed in pk[i]; sp: partial row sums.
+    uint32_t pk[KB / 2];
+    float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    auto row_sum = [&]() {
+      return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+    };
+    // p = 2^(c s - m) of the block's valid keys, from the scores in r.
+    auto p_block = [&](float nm, int valid) {
 #pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-      tmem_ld_wait();
-      const int valid = w.valid(j);
-      const bool full = valid == KB;
-      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-      // A full block after the first: p = 2^(c s - m) with the row's current
-      // base first.  When every row's block sum is below 2^7, every p is, so
-      // the exact test below (raise when some p would exceed 2^8) raises no
-      // base and would compute the same p: the row max is skipped.  Else the
-      // scores are read again (P is not stored yet) and the exact path runs.
-      // Packed P of the block: keys 2i, 2i+1 in pk[i].
-      uint32_t pk[KB / 2];
-      bool fast = false;
-      if (j > 0 && full) {
-        const float nm = -m_run;
+      for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+      if (valid == KB) {
 #pragma unroll
         for (int i = 0; i < KB; i += 2) {
           float x0, x1, e0, e1;
@@ -402,78 +397,136 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
           add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
           pk[i >> 1] = pack_16bit(e0, e1, BF16);
         }
-        const float bs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-        fast = __all_sync(0xffffffffu, bs < 128.0f);
-        if (!fast) {
+      } else {
 #pragma unroll
-          for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+        for (int i = 0; i < KB; i += 2) {
+          const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
+          const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
+          sp[i & 7] += e0;
+          sp[(i + 1) & 7] += e1;
+          pk[i >> 1] = pack_16bit(e0, e1, BF16);
         }
       }
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (!fast) {
-        float mx;
-        if (full) {
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    };
+    // Waits end the loop for the whole warp together: the TMEM loads and
+    // stores that follow are warp-collective.
+    auto wait_scores = [&](int j) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1u, p.err,
+                                             kDevTimeoutEpilogue, abortp)))
+        return false;
+      tc_fence_after();
+      return true;
+    };
+    auto load_scores = [&]() {
 #pragma unroll
-          for (int i = 0; i < KB; i += 8) {
-            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-          }
-          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-        } else {
-          mx = -INFINITY;
+      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+      tmem_ld_wait();
+    };
+    // Max-first block: the row max; the base rises to ceil(c * max) when that
+    // exceeds it by more than kAttnRescaleLog2 (always on the first block);
+    // then p.  Returns whether some row of the warp raised its base.
+    auto max_first = [&](int j, int valid, float& alpha) -> bool {
+      float mx;
+      if (valid == KB) {
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < KB; ++i)
-            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        for (int i = 0; i < KB; i += 8) {
+          m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+          m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+          m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
         }
-        const float cand = ceilf(mx * c);
-        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-        alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-        rescale = j >= 1 && __any_sync(0xffffffffu, need);
-        if (need) {
-          l_run *= alpha;
-          m_run = cand;
-        }
-        const float nm = -m_run;
-        if (full) {
+        mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+      } else {
+        mx = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < KB; i += 2) {
-            float x0, x1, e0, e1;
-            fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
-            e0 = ex2_approx(x0);
-            e1 = ex2_approx(x1);
-            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
-            pk[i >> 1] = pack_16bit(e0, e1, BF16);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < KB; i += 2) {
-            const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
-            const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
-            sp[i & 7] += e0;
-            sp[(i + 1) & 7] += e1;
-            pk[i >> 1] = pack_16bit(e0, e1, BF16);
-          }
-        }
+        for (int i = 0; i < KB; ++i)
+          if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
       }
-      // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first), over
-      // score columns already read.
+      const float cand = ceilf(mx * c);
+      const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+      alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+      const bool raised = j >= 1 && __any_sync(0xffffffffu, need);
+      if (need) {
+        l_run *= alpha;
+        m_run = cand;
+      }
+      p_block(-m_run, valid);
+      return raised;
+    };
+    // Store P over the scores already read (keys ch*32 + 2i, +2i+1 in column
+    // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
+    // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
+    // and P_t(j) V is issued only after the arrival.
+    auto finish = [&](bool raised, float alpha) {
 #pragma unroll
       for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-      l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-      // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
-      // is issued only after the arrival below.
-      if (rescale) rescale_o(alpha);
+      l_run += row_sum();
+      if (raised) rescale_o(alpha);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
+    };
+    int j = 0;
+    // Sum-first blocks: the first block max-first, then p with the current base
+    // (no row max).  Leaves for the max-first loop below at the first block
+    // whose sum is too large to scale by a power of two (or infinite).
+    for (; j < nblk; ++j) {
+      if (!wait_scores(j)) {
+        ok = false;
+        break;
+      }
+      load_scores();
+      const int valid = w.valid(j);
+      float alpha = 1.0f;
+      bool raised = false, leave = false;
+      if (j == 0) {
+        raised = max_first(j, valid, alpha);
+      } else {
+        p_block(-m_run, valid);
+        const float bs = row_sum();
+        if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
+          // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
+          if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
+            const bool need = bs >= kAttnSumLimit;
+            const int k = need ? static_cast<int>((__float_as_uint(bs) >> 23) & 0xffu) - 126 : 0;
+            alpha = __uint_as_float(static_cast<uint32_t>(127 - k) << 23);
+            raised = __any_sync(0xffffffffu, need);
+            if (need) {
+              l_run *= alpha;
+              m_run += static_cast<float>(k);
+            }
+            if (raised) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) sp[i] *= alpha;
+              const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
+#pragma unroll
+              for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
+            }
+          } else {
+            load_scores();
+            raised = max_first(j, valid, alpha);
+            leave = true;
+          }
+        }
+      }
+      finish(raised, alpha);
+      if (leave) {
+        ++j;
+        break;
+      }
+    }
+    // Max-first blocks: the rest of the unit after a sum too large to scale.
+    for (; ok && j < nblk; ++j) {
+      if (!wait_scores(j)) {
+        ok = false;
+        break;
+      }
+      load_scores();
+      float alpha = 1.0f;
+      const bool raised = max_first(j, w.valid(j), alpha);
+      finish(raised, alpha);
     }
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
@@ -808,27 +861,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       if (t >= pp_tiles<Cfg>(p, w)) continue;
       const int nblk = w.nblk;
       float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
-      for (int j = 0; j < nblk; ++j) {
-        // Waits end the loop for the whole warp together: the TMEM loads and
-        // stores that follow are warp-collective.
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(sbase + j) & 1u,
-                                               p.err, kDevTimeoutEpilogue, abortp))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      // P of a block: keys 2i, 2i+1 packed in pk[i]; sp: partial row sums.
+      uint32_t pk[KB / 2];
+      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      auto row_sum = [&]() {
+        return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      };
+      // p = 2^(c s - m) of the block's valid keys, from the scores in r.
+      auto p_block = [&](float nm, int valid) {
 #pragma unroll
-        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-        tmem_ld_wait();
-        const int valid = w.valid(j);
-        const bool full = valid == KB;
-        float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        // The row max is skipped when every row's block sum under the current
-        // base is below 2^7 (as in attention_pp_kernel).
-        uint32_t pk[KB / 2];
-        bool fast = false;
-        if (j > 0 && full) {
-          const float nm = -m_run;
+        for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+        if (valid == KB) {
 #pragma unroll
           for (int i = 0; i < KB; i += 2) {
             float x0, x1, e0, e1;
@@ -838,78 +881,136 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
             add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
             pk[i >> 1] = pack_16bit(e0, e1, BF16);
           }
-          const float bs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-          fast = __all_sync(0xffffffffu, bs < 128.0f);
-          if (!fast) {
+        } else {
 #pragma unroll
-            for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+          for (int i = 0; i < KB; i += 2) {
+            const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
+            const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
+            sp[i & 7] += e0;
+            sp[(i + 1) & 7] += e1;
+            pk[i >> 1] = pack_16bit(e0, e1, BF16);
           }
         }
-        float alpha = 1.0f;
-        bool rescale = false;
-        if (!fast) {
-          float mx;
-          if (full) {
-            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      };
+      // Waits end the loop for the whole warp together: the TMEM loads and
+      // stores that follow are warp-collective.
+      auto wait_scores = [&](int j) -> bool {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(sbase + j) & 1u, p.err,
+                                               kDevTimeoutEpilogue, abortp)))
+          return false;
+        tc_fence_after();
+        return true;
+      };
+      auto load_scores = [&]() {
 #pragma unroll
-            for (int i = 0; i < KB; i += 8) {
-              m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-              m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-              m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-              m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-            }
-            mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-          } else {
-            mx = -INFINITY;
+        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+        tmem_ld_wait();
+      };
+      // Max-first block: the row max; the base rises to ceil(c * max) when that
+      // exceeds it by more than kAttnRescaleLog2 (always on the first block);
+      // then p.  Returns whether some row of the warp raised its base.
+      auto max_first = [&](int j, int valid, float& alpha) -> bool {
+        float mx;
+        if (valid == KB) {
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int i = 0; i < KB; ++i)
-              if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < KB; i += 8) {
+            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
           }
-          const float cand = ceilf(mx * c);
-          const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-          alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-          rescale = j >= 1 && __any_sync(0xffffffffu, need);
-          if (need) {
-            l_run *= alpha;
-            m_run = cand;
-          }
-          const float nm = -m_run;
-          if (full) {
+          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+        } else {
+          mx = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < KB; i += 2) {
-              float x0, x1, e0, e1;
-              fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
-              e0 = ex2_approx(x0);
-              e1 = ex2_approx(x1);
-              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
-              pk[i >> 1] = pack_16bit(e0, e1, BF16);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < KB; i += 2) {
-              const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
-              const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
-              sp[i & 7] += e0;
-              sp[(i + 1) & 7] += e1;
-              pk[i >> 1] = pack_16bit(e0, e1, BF16);
-            }
-          }
+          for (int i = 0; i < KB; ++i)
+            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
-        // Keys ch*32 + 2i, +2i+1 go to column ch*16 + i (low half first), over
-        // score columns already read.
+        const float cand = ceilf(mx * c);
+        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+        alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+        const bool raised = j >= 1 && __any_sync(0xffffffffu, need);
+        if (need) {
+          l_run *= alpha;
+          m_run = cand;
+        }
+        p_block(-m_run, valid);
+        return raised;
+      };
+      // Store P over the scores already read (keys ch*32 + 2i, +2i+1 in column
+      // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
+      // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
+      // and P_t(j) V is issued only after the arrival.
+      auto finish = [&](bool raised, float alpha) {
 #pragma unroll
         for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-        l_run += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-        // O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it) and P_t(j) V
-        // is issued only after the arrival below.
-        if (rescale) rescale_o(alpha);
+        l_run += row_sum();
+        if (raised) rescale_o(alpha);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
+      };
+      int j = 0;
+      // Sum-first blocks: the first block max-first, then p with the current base
+      // (no row max).  Leaves for the max-first loop below at the first block
+      // whose sum is too large to scale by a power of two (or infinite).
+      for (; j < nblk; ++j) {
+        if (!wait_scores(j)) {
+          ok = false;
+          break;
+        }
+        load_scores();
+        const int valid = w.valid(j);
+        float alpha = 1.0f;
+        bool raised = false, leave = false;
+        if (j == 0) {
+          raised = max_first(j, valid, alpha);
+        } else {
+          p_block(-m_run, valid);
+          const float bs = row_sum();
+          if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
+            // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
+            if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
+              const bool need = bs >= kAttnSumLimit;
+              const int k = need ? static_cast<int>((__float_as_uint(bs) >> 23) & 0xffu) - 126 : 0;
+              alpha = __uint_as_float(static_cast<uint32_t>(127 - k) << 23);
+              raised = __any_sync(0xffffffffu, need);
+              if (need) {
+                l_run *= alpha;
+                m_run += static_cast<float>(k);
+              }
+              if (raised) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sp[i] *= alpha;
+                const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
+#pragma unroll
+                for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
+              }
+            } else {
+              load_scores();
+              raised = max_first(j, valid, alpha);
+              leave = true;
+            }
+          }
+        }
+        finish(raised, alpha);
+        if (leave) {
+          ++j;
+          break;
+        }
+      }
+      // Max-first blocks: the rest of the unit after a sum too large to scale.
+      for (; ok && j < nblk; ++j) {
+        if (!wait_scores(j)) {
+          ok = false;
+          break;
+        }
+        load_scores();
+        float alpha = 1.0f;
+        const bool raised = max_first(j, w.valid(j), alpha);
+        finish(raised, alpha);
       }
       if (ok && nblk > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], static_cast<uint32_t>(ocnt) & 1u, p.err,

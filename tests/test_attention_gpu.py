@@ -304,3 +304,46 @@ def test_fused_attention_split_keys_merge(gpu, ops, monkeypatch, lo, hi, Lq, Lk,
                                         C.c_void_p(gk.ptr), W, Lk * W, C.c_void_p(gv.ptr), W,
                                         Lk * W, C.c_void_p(two.ptr), W, Lq * W, 0.125, 2, 10, 1,
                                         None, None, 1, None) == SF_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("jump", [12.0, 60.0, 140.0, 250.0])
+def test_fused_attention_base_raises(gpu, ops, dt, jump):
+    """The row base after the first key block: rows whose later scores climb
+    above it, one key `jump` log2 units above everything before it (blocks
+    after the first whose p sum reaches 2^8 raise the base by a power of two
+    read off the sum; a sum past 2^120, 2^15 for f16 P, or infinite takes the
+    row max and recomputes), and a steady climb that raises the base in
+    block after block.  Against the oracle's blockwise restatement."""
+    from tests.gpu_util import device_error
+    rng = np.random.default_rng(int(jump) + (7 if dt == "f16" else 0))
+    Lq, Lk, scale = 130, 700, 0.125
+    c = scale * 1.4426950408889634
+    q32 = rng.standard_normal((Lq, 64), dtype=np.float32) * np.float32(0.5)
+    k32 = rng.standard_normal((Lk, 64), dtype=np.float32) * np.float32(0.2)
+    v32 = rng.standard_normal((Lk, 64), dtype=np.float32)
+    q32[:, 0] = 8.0
+    # rows 0..63: one key (index 333, block 5) `jump` log2 units up
+    k32[333, 0] = np.float32(jump / c / 8.0)
+    # rows 64..129: a steady climb through every block (another head)
+    q2 = q32.copy()
+    k2 = k32.copy()
+    k2[:, 0] = np.linspace(0.0, 40.0 / c / 8.0, Lk, dtype=np.float32)
+    k2[333, 0] = 0.0
+    qh = np.concatenate([q32, q2], axis=1)       # [Lq, 2 heads * 64]
+    kh = np.concatenate([k32, k2], axis=1)
+    vh = np.concatenate([v32, v32[::-1]], axis=1)
+    gq, q = to_device(ops, qh, dt)
+    gk, k = to_device(ops, kh, dt)
+    gv, v = to_device(ops, vh, dt)
+    out = _fused(ops, 1, 2, Lq, Lk, gq, gk, gv, 128, 128, 128, Lq * 128, Lk * 128, Lk * 128, scale,
+                 dt=dt)
+    for h in range(2):
+        sl = slice(h * 64, (h + 1) * 64)
+        p = O.softmax_rows((q[:, sl] @ k[:, sl].T * np.float32(scale)).astype(np.float32))
+        ref, allow = O.flash_attention(q[:, sl], k[:, sl], v[:, sl], scale, p_dtype=dt,
+                                       return_allowance=True, **attn_oracle_opts())
+        assert np.isfinite(out[:, sl]).all()
+        _check_attn(out[:, sl], ref, O.abs_product(p, v[:, sl].T), allow,
+                    f"{dt} jump {jump} head {h}")
+    assert device_error(0) == 0
