@@ -347,3 +347,60 @@ def test_fused_attention_base_raises(gpu, ops, dt, jump):
         _check_attn(out[:, sl], ref, O.abs_product(p, v[:, sl].T), allow,
                     f"{dt} jump {jump} head {h}")
     assert device_error(0) == 0
+
+
+def test_fused_attention_graph_keeps_captured_workspace(gpu, ops, monkeypatch):
+    """A stream-K attention call captured into a CUDA graph keeps using the
+    tail workspace it was captured with: a later direct call on the same
+    stream that needs a larger workspace retires the captured buffer instead
+    of freeing it, so replaying the graph afterwards gives the same bits as
+    the direct call of the captured shape."""
+    import ctypes as C
+
+    from scaffolding_b200 import engine as E
+    from scaffolding_b200._lib import lib
+    from tests.gpu_util import device_error
+    monkeypatch.setenv("SF_ATTN_SPLIT", "2")
+    bf = np_dtype("bf16")
+    rng = np.random.default_rng(91)
+
+    def inputs(B, H, L):
+        W = H * 64
+        g, _ = to_device(ops, rng.standard_normal((B * L, 3 * W), dtype=np.float32), "bf16")
+        return g, W
+
+    def call(g, B, H, L, W, out, stream):
+        base = g.ptr
+        E.attention(B, H, L, L, base, 3 * W, L * 3 * W, base + W * 2, 3 * W, L * 3 * W,
+                    base + 2 * W * 2, 3 * W, L * 3 * W, out.ptr, W, L * W, 0.125, stream=stream)
+
+    sp = C.c_void_p()
+    assert lib.sf_stream_create(0, 1, C.byref(sp)) == 0
+    s = sp.value
+    # small shape: 6 units, all in the tail (a small workspace)
+    Ba, Ha, La = 1, 2, 700
+    ga, Wa = inputs(Ba, Ha, La)
+    assert E.attention_launch_count(Ba, Ha, La, La) == 2
+    direct = ops._alloc((Ba * La, Wa), bf, 0)
+    replay = ops._alloc((Ba * La, Wa), bf, 0)
+    call(ga, Ba, Ha, La, Wa, direct, s)  # sizes the workspace
+    E.stream_sync(s)
+    g = C.c_void_p()
+    assert lib.sf_graph_begin(C.c_void_p(s)) == 0
+    call(ga, Ba, Ha, La, Wa, replay, s)
+    assert lib.sf_graph_end(C.c_void_p(s), C.byref(g)) == 0
+    # a larger shape on the same stream grows the workspace (128 units, 256 tail CTAs)
+    Bb, Hb, Lb = 2, 8, 2000
+    gb, Wb = inputs(Bb, Hb, Lb)
+    big = ops._alloc((Bb * Lb, Wb), bf, 0)
+    call(gb, Bb, Hb, Lb, Wb, big, s)
+    E.stream_sync(s)
+    for _ in range(2):
+        assert lib.sf_graph_launch(g, C.c_void_p(s)) == 0
+    E.stream_sync(s)
+    assert lib.sf_graph_destroy(g) == 0
+    lib.sf_stream_destroy(C.c_void_p(s))
+    a = ops.gputensor_to_numpy(direct).view(np.uint16)
+    b = ops.gputensor_to_numpy(replay).view(np.uint16)
+    assert np.array_equal(a, b)
+    assert device_error(0) == 0
