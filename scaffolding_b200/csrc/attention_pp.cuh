@@ -385,8 +385,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     };
     // p = 2^(c s - m) of the block's valid keys, from the scores in r.
     auto p_block = [&](float nm, int valid) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
       if (valid == KB) {
 #pragma unroll
         for (int i = 0; i < KB; i += 2) {
@@ -394,10 +392,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
           fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
           e0 = ex2_approx(x0);
           e1 = ex2_approx(x1);
-          add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+          if ((i & 2) == 0 && i < 16) {  // first keys of each pair of sums
+            sp[(i >> 1) & 6] = e0;
+            sp[((i >> 1) & 6) + 1] = e1;
+          } else {
+            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+          }
           pk[i >> 1] = pack_16bit(e0, e1, BF16);
         }
       } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
 #pragma unroll
         for (int i = 0; i < KB; i += 2) {
           const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
@@ -458,10 +463,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
     // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
     // and P_t(j) V is issued only after the arrival.
-    auto finish = [&](bool raised, float alpha) {
+    auto finish = [&](bool raised, float alpha, float sum) {
 #pragma unroll
       for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-      l_run += row_sum();
+      l_run += sum;
       if (raised) rescale_o(alpha);
       tmem_st_wait();
       tc_fence_before();
@@ -481,11 +486,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       const int valid = w.valid(j);
       float alpha = 1.0f;
       bool raised = false, leave = false;
+      float sum = 0.0f;  // the block's row sum as stored
       if (j == 0) {
         raised = max_first(j, valid, alpha);
+        sum = row_sum();
       } else {
         p_block(-m_run, valid);
         const float bs = row_sum();
+        sum = bs;
         if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
           // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
           if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
@@ -497,9 +505,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
               l_run *= alpha;
               m_run += static_cast<float>(k);
             }
+            sum = bs * alpha;  // exact: alpha is a power of two (1 where no row raised)
             if (raised) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i) sp[i] *= alpha;
               const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
 #pragma unroll
               for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
@@ -507,11 +514,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
           } else {
             load_scores();
             raised = max_first(j, valid, alpha);
+            sum = row_sum();
             leave = true;
           }
         }
       }
-      finish(raised, alpha);
+      finish(raised, alpha, sum);
       if (leave) {
         ++j;
         break;
@@ -526,7 +534,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       load_scores();
       float alpha = 1.0f;
       const bool raised = max_first(j, w.valid(j), alpha);
-      finish(raised, alpha);
+      const float sum = row_sum();
+      finish(raised, alpha, sum);
     }
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
@@ -869,8 +878,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       };
       // p = 2^(c s - m) of the block's valid keys, from the scores in r.
       auto p_block = [&](float nm, int valid) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
         if (valid == KB) {
 #pragma unroll
           for (int i = 0; i < KB; i += 2) {
@@ -878,10 +885,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
             fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
             e0 = ex2_approx(x0);
             e1 = ex2_approx(x1);
-            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+            if ((i & 2) == 0 && i < 16) {  // first keys of each pair of sums
+              sp[(i >> 1) & 6] = e0;
+              sp[((i >> 1) & 6) + 1] = e1;
+            } else {
+              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+            }
             pk[i >> 1] = pack_16bit(e0, e1, BF16);
           }
         } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
 #pragma unroll
           for (int i = 0; i < KB; i += 2) {
             const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
@@ -942,10 +956,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
       // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
       // and P_t(j) V is issued only after the arrival.
-      auto finish = [&](bool raised, float alpha) {
+      auto finish = [&](bool raised, float alpha, float sum) {
 #pragma unroll
         for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-        l_run += row_sum();
+        l_run += sum;
         if (raised) rescale_o(alpha);
         tmem_st_wait();
         tc_fence_before();
@@ -965,11 +979,14 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
         const int valid = w.valid(j);
         float alpha = 1.0f;
         bool raised = false, leave = false;
+        float sum = 0.0f;  // the block's row sum as stored
         if (j == 0) {
           raised = max_first(j, valid, alpha);
+          sum = row_sum();
         } else {
           p_block(-m_run, valid);
           const float bs = row_sum();
+          sum = bs;
           if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
             // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
             if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
@@ -981,9 +998,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
                 l_run *= alpha;
                 m_run += static_cast<float>(k);
               }
+              sum = bs * alpha;  // exact: alpha is a power of two (1 where no row raised)
               if (raised) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) sp[i] *= alpha;
                 const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
 #pragma unroll
                 for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
@@ -991,11 +1007,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
             } else {
               load_scores();
               raised = max_first(j, valid, alpha);
+              sum = row_sum();
               leave = true;
             }
           }
         }
-        finish(raised, alpha);
+        finish(raised, alpha, sum);
         if (leave) {
           ++j;
           break;
@@ -1010,7 +1027,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
         load_scores();
         float alpha = 1.0f;
         const bool raised = max_first(j, w.valid(j), alpha);
-        finish(raised, alpha);
+        const float sum = row_sum();
+        finish(raised, alpha, sum);
       }
       if (ok && nblk > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], static_cast<uint32_t>(ocnt) & 1u, p.err,
