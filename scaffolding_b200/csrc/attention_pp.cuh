@@ -171,6 +171,195 @@ __device__ __forceinline__ int pp_tiles(const AttnArgs& p, const PpSeg<KB>& w) {
   return min(Cfg::NT, (p.q_len - w.qb * Cfg::ROWS + 127) / 128);
 }
 
+// The softmax warps' part of a unit (or of a segment of one), one query row
+// per thread: key blocks 0 .. nblk-1 of w, sum-first then max-first as the
+// header describes.  s_full_t / p_full_t: the tile's score-ready and
+// P-stored barriers, with sbase phases completed before this segment;
+// s_addr / o_addr: the warp's score and output columns in TMEM; r: scratch
+// registers (at least 64).  m_run and l_run end as the row's base and sum.
+// Returns false when a wait expired.
+template <bool BF16, int KB, int CHUNKS>
+__device__ __forceinline__ bool pp_softmax_rows(const AttnArgs& p, const PpSeg<KB>& w, int nblk,
+                                                int sbase, uint64_t* s_full_t, uint64_t* p_full_t,
+                                                uint32_t s_addr, uint32_t o_addr, int lane,
+                                                volatile int* abortp, float& m_run, float& l_run,
+                                                uint32_t* r) {
+  const float c = p.scale_log2;
+  bool ok = true;
+  // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
+  auto rescale_o = [&](float alpha) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tmem_ld32(o_addr + half * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+      tmem_st32(o_addr + half * 32, r);
+    }
+  };
+  // P of a block: keys 2i, 2i+1 packed in pk[i]; sp: partial row sums.
+  uint32_t pk[KB / 2];
+  float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+  auto row_sum = [&]() {
+    return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+  };
+  // p = 2^(c s - m) of the block's valid keys, from the scores in r.
+  auto p_block = [&](float nm, int valid) {
+    if (valid == KB) {
+#pragma unroll
+      for (int i = 0; i < KB; i += 2) {
+        float x0, x1, e0, e1;
+        fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
+        e0 = ex2_approx(x0);
+        e1 = ex2_approx(x1);
+        if ((i & 2) == 0 && i < 16) {  // first keys of each pair of sums
+          sp[(i >> 1) & 6] = e0;
+          sp[((i >> 1) & 6) + 1] = e1;
+        } else {
+          add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
+        }
+        pk[i >> 1] = pack_16bit(e0, e1, BF16);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < KB; i += 2) {
+        const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
+        const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
+        sp[i & 7] += e0;
+        sp[(i + 1) & 7] += e1;
+        pk[i >> 1] = pack_16bit(e0, e1, BF16);
+      }
+    }
+  };
+  // Waits end the loop for the whole warp together: the TMEM loads and
+  // stores that follow are warp-collective.
+  auto wait_scores = [&](int j) -> bool {
+    if (!__all_sync(0xffffffffu, mbar_wait(s_full_t, static_cast<uint32_t>(sbase + j) & 1u, p.err,
+                                           kDevTimeoutEpilogue, abortp)))
+      return false;
+    tc_fence_after();
+    return true;
+  };
+  auto load_scores = [&]() {
+#pragma unroll
+    for (int ch = 0; ch < CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
+    tmem_ld_wait();
+  };
+  // Max-first block: the row max; the base rises to ceil(c * max) when that
+  // exceeds it by more than kAttnRescaleLog2 (always on the first block);
+  // then p.  Returns whether some row of the warp raised its base.
+  auto max_first = [&](int j, int valid, float& alpha) -> bool {
+    float mx;
+    if (valid == KB) {
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < KB; i += 8) {
+        m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+        m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+        m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+        m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+      }
+      mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+    } else {
+      mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < KB; ++i)
+        if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+    }
+    const float cand = ceilf(mx * c);
+    const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
+    alpha = need ? ex2_approx(m_run - cand) : 1.0f;
+    const bool raised = j >= 1 && __any_sync(0xffffffffu, need);
+    if (need) {
+      l_run *= alpha;
+      m_run = cand;
+    }
+    p_block(-m_run, valid);
+    return raised;
+  };
+  // Store P over the scores already read (keys ch*32 + 2i, +2i+1 in column
+  // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
+  // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
+  // and P_t(j) V is issued only after the arrival.
+  auto finish = [&](bool raised, float alpha, float sum) {
+#pragma unroll
+    for (int ch = 0; ch < CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
+    l_run += sum;
+    if (raised) rescale_o(alpha);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full_t);
+  };
+  int j = 0;
+  // Sum-first blocks: the first block max-first, then p with the current base
+  // (no row max).  Leaves for the max-first loop below at the first block
+  // whose sum is too large to scale by a power of two (or infinite).
+  for (; j < nblk; ++j) {
+    if (!wait_scores(j)) {
+      ok = false;
+      break;
+    }
+    load_scores();
+    const int valid = w.valid(j);
+    float alpha = 1.0f;
+    bool raised = false, leave = false;
+    float sum = 0.0f;  // the block's row sum as stored
+    if (j == 0) {
+      raised = max_first(j, valid, alpha);
+      sum = row_sum();
+    } else {
+      p_block(-m_run, valid);
+      const float bs = row_sum();
+      sum = bs;
+      if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
+        // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
+        if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
+          const bool need = bs >= kAttnSumLimit;
+          const int k = need ? static_cast<int>((__float_as_uint(bs) >> 23) & 0xffu) - 126 : 0;
+          alpha = __uint_as_float(static_cast<uint32_t>(127 - k) << 23);
+          raised = __any_sync(0xffffffffu, need);
+          if (need) {
+            l_run *= alpha;
+            m_run += static_cast<float>(k);
+          }
+          sum = bs * alpha;  // exact: alpha is a power of two (1 where no row raised)
+          if (raised) {
+            const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
+#pragma unroll
+            for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
+          }
+        } else {
+          load_scores();
+          raised = max_first(j, valid, alpha);
+          sum = row_sum();
+          leave = true;
+        }
+      }
+    }
+    finish(raised, alpha, sum);
+    if (leave) {
+      ++j;
+      break;
+    }
+  }
+  // Max-first blocks: the rest of the unit after a sum too large to scale.
+  for (; ok && j < nblk; ++j) {
+    if (!wait_scores(j)) {
+      ok = false;
+      break;
+    }
+    load_scores();
+    float alpha = 1.0f;
+    const bool raised = max_first(j, w.valid(j), alpha);
+    const float sum = row_sum();
+    finish(raised, alpha, sum);
+  }
+  return ok;
+}
+
 // Whole units, one per CTA (pp_unit).  When a stream-K tail runs, this is
 // launched after the tail kernel with programmatic stream serialisation and
 // takes the SM slots the tail CTAs leave; it reads nothing they write.
@@ -363,180 +552,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     const uint32_t s_addr = tmem_base + lane_base + Cfg::S_COL + t * KB;
     const uint32_t o_addr = tmem_base + lane_base + Cfg::O_COL + t * 64;
     float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
-    const float c = p.scale_log2;
-    bool ok = true;
     uint32_t r[KB > 64 ? KB : 64];
-    // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
-    auto rescale_o = [&](float alpha) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(o_addr + half * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-        tmem_st32(o_addr + half * 32, r);
-      }
-    };
-    // P of a block: keys 2i, 2i+1 packed in pk[i]; sp: partial row sums.
-    uint32_t pk[KB / 2];
-    float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-    auto row_sum = [&]() {
-      return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-    };
-    // p = 2^(c s - m) of the block's valid keys, from the scores in r.
-    auto p_block = [&](float nm, int valid) {
-      if (valid == KB) {
-#pragma unroll
-        for (int i = 0; i < KB; i += 2) {
-          float x0, x1, e0, e1;
-          fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
-          e0 = ex2_approx(x0);
-          e1 = ex2_approx(x1);
-          if ((i & 2) == 0 && i < 16) {  // first keys of each pair of sums
-            sp[(i >> 1) & 6] = e0;
-            sp[((i >> 1) & 6) + 1] = e1;
-          } else {
-            add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
-          }
-          pk[i >> 1] = pack_16bit(e0, e1, BF16);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < KB; i += 2) {
-          const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
-          const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
-          sp[i & 7] += e0;
-          sp[(i + 1) & 7] += e1;
-          pk[i >> 1] = pack_16bit(e0, e1, BF16);
-        }
-      }
-    };
-    // Waits end the loop for the whole warp together: the TMEM loads and
-    // stores that follow are warp-collective.
-    auto wait_scores = [&](int j) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(j) & 1u, p.err,
-                                             kDevTimeoutEpilogue, abortp)))
-        return false;
-      tc_fence_after();
-      return true;
-    };
-    auto load_scores = [&]() {
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-      tmem_ld_wait();
-    };
-    // Max-first block: the row max; the base rises to ceil(c * max) when that
-    // exceeds it by more than kAttnRescaleLog2 (always on the first block);
-    // then p.  Returns whether some row of the warp raised its base.
-    auto max_first = [&](int j, int valid, float& alpha) -> bool {
-      float mx;
-      if (valid == KB) {
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < KB; i += 8) {
-          m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-          m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-          m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-          m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-        }
-        mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-      } else {
-        mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < KB; ++i)
-          if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      const float cand = ceilf(mx * c);
-      const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-      alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-      const bool raised = j >= 1 && __any_sync(0xffffffffu, need);
-      if (need) {
-        l_run *= alpha;
-        m_run = cand;
-      }
-      p_block(-m_run, valid);
-      return raised;
-    };
-    // Store P over the scores already read (keys ch*32 + 2i, +2i+1 in column
-    // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
-    // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
-    // and P_t(j) V is issued only after the arrival.
-    auto finish = [&](bool raised, float alpha, float sum) {
-#pragma unroll
-      for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-      l_run += sum;
-      if (raised) rescale_o(alpha);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    };
-    int j = 0;
-    // Sum-first blocks: the first block max-first, then p with the current base
-    // (no row max).  Leaves for the max-first loop below at the first block
-    // whose sum is too large to scale by a power of two (or infinite).
-    for (; j < nblk; ++j) {
-      if (!wait_scores(j)) {
-        ok = false;
-        break;
-      }
-      load_scores();
-      const int valid = w.valid(j);
-      float alpha = 1.0f;
-      bool raised = false, leave = false;
-      float sum = 0.0f;  // the block's row sum as stored
-      if (j == 0) {
-        raised = max_first(j, valid, alpha);
-        sum = row_sum();
-      } else {
-        p_block(-m_run, valid);
-        const float bs = row_sum();
-        sum = bs;
-        if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
-          // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
-          if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
-            const bool need = bs >= kAttnSumLimit;
-            const int k = need ? static_cast<int>((__float_as_uint(bs) >> 23) & 0xffu) - 126 : 0;
-            alpha = __uint_as_float(static_cast<uint32_t>(127 - k) << 23);
-            raised = __any_sync(0xffffffffu, need);
-            if (need) {
-              l_run *= alpha;
-              m_run += static_cast<float>(k);
-            }
-            sum = bs * alpha;  // exact: alpha is a power of two (1 where no row raised)
-            if (raised) {
-              const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
-#pragma unroll
-              for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
-            }
-          } else {
-            load_scores();
-            raised = max_first(j, valid, alpha);
-            sum = row_sum();
-            leave = true;
-          }
-        }
-      }
-      finish(raised, alpha, sum);
-      if (leave) {
-        ++j;
-        break;
-      }
-    }
-    // Max-first blocks: the rest of the unit after a sum too large to scale.
-    for (; ok && j < nblk; ++j) {
-      if (!wait_scores(j)) {
-        ok = false;
-        break;
-      }
-      load_scores();
-      float alpha = 1.0f;
-      const bool raised = max_first(j, w.valid(j), alpha);
-      const float sum = row_sum();
-      finish(raised, alpha, sum);
-    }
+    bool ok = pp_softmax_rows<BF16, KB, Cfg::CHUNKS>(p, w, nblk, 0, &s_full[t], &p_full[t], s_addr,
+                                                     o_addr, lane, abortp, m_run, l_run, r);
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
     const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
@@ -850,186 +868,16 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t s_addr = tmem_base + lane_base + Cfg::S_COL + t * KB;
     const uint32_t o_addr = tmem_base + lane_base + Cfg::O_COL + t * 64;
-    const float c = p.scale_log2;
     bool ok = true;
     int sbase = 0, ocnt = 0;  // s_full phases and finished segments of this tile so far
     uint32_t r[KB > 64 ? KB : 64];
-    // O row scaling by alpha (warp-collective; factor 1 on the warp's other rows).
-    auto rescale_o = [&](float alpha) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(o_addr + half * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-        tmem_st32(o_addr + half * 32, r);
-      }
-    };
     for (int si = 0; si < nseg && ok; ++si) {
       const PpSeg<KB> w = pp_tail_seg<KB>(p, si);
       if (t >= pp_tiles<Cfg>(p, w)) continue;
       const int nblk = w.nblk;
       float m_run = -INFINITY, l_run = 0.0f;  // m_run: integer-valued base (log2 domain)
-      // P of a block: keys 2i, 2i+1 packed in pk[i]; sp: partial row sums.
-      uint32_t pk[KB / 2];
-      float sp[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-      auto row_sum = [&]() {
-        return ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
-      };
-      // p = 2^(c s - m) of the block's valid keys, from the scores in r.
-      auto p_block = [&](float nm, int valid) {
-        if (valid == KB) {
-#pragma unroll
-          for (int i = 0; i < KB; i += 2) {
-            float x0, x1, e0, e1;
-            fma2(x0, x1, __uint_as_float(r[i]), __uint_as_float(r[i + 1]), c, c, nm, nm);
-            e0 = ex2_approx(x0);
-            e1 = ex2_approx(x1);
-            if ((i & 2) == 0 && i < 16) {  // first keys of each pair of sums
-              sp[(i >> 1) & 6] = e0;
-              sp[((i >> 1) & 6) + 1] = e1;
-            } else {
-              add2(sp[(i >> 1) & 6], sp[((i >> 1) & 6) + 1], e0, e1);
-            }
-            pk[i >> 1] = pack_16bit(e0, e1, BF16);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) sp[i] = 0.0f;
-#pragma unroll
-          for (int i = 0; i < KB; i += 2) {
-            const float e0 = i < valid ? ex2_approx(fmaf(__uint_as_float(r[i]), c, nm)) : 0.0f;
-            const float e1 = i + 1 < valid ? ex2_approx(fmaf(__uint_as_float(r[i + 1]), c, nm)) : 0.0f;
-            sp[i & 7] += e0;
-            sp[(i + 1) & 7] += e1;
-            pk[i >> 1] = pack_16bit(e0, e1, BF16);
-          }
-        }
-      };
-      // Waits end the loop for the whole warp together: the TMEM loads and
-      // stores that follow are warp-collective.
-      auto wait_scores = [&](int j) -> bool {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], static_cast<uint32_t>(sbase + j) & 1u, p.err,
-                                               kDevTimeoutEpilogue, abortp)))
-          return false;
-        tc_fence_after();
-        return true;
-      };
-      auto load_scores = [&]() {
-#pragma unroll
-        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_ld32(s_addr + ch * 32, r + ch * 32);
-        tmem_ld_wait();
-      };
-      // Max-first block: the row max; the base rises to ceil(c * max) when that
-      // exceeds it by more than kAttnRescaleLog2 (always on the first block);
-      // then p.  Returns whether some row of the warp raised its base.
-      auto max_first = [&](int j, int valid, float& alpha) -> bool {
-        float mx;
-        if (valid == KB) {
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int i = 0; i < KB; i += 8) {
-            m4[0] = max3f(m4[0], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-            m4[1] = max3f(m4[1], __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-            m4[2] = max3f(m4[2], __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-            m4[3] = max3f(m4[3], __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-          }
-          mx = max3f(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-        } else {
-          mx = -INFINITY;
-#pragma unroll
-          for (int i = 0; i < KB; ++i)
-            if (i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-        }
-        const float cand = ceilf(mx * c);
-        const bool need = cand > m_run + kAttnRescaleLog2;  // always on the first block
-        alpha = need ? ex2_approx(m_run - cand) : 1.0f;
-        const bool raised = j >= 1 && __any_sync(0xffffffffu, need);
-        if (need) {
-          l_run *= alpha;
-          m_run = cand;
-        }
-        p_block(-m_run, valid);
-        return raised;
-      };
-      // Store P over the scores already read (keys ch*32 + 2i, +2i+1 in column
-      // ch*16 + i), add the block to l, rescale O if a base rose, and hand P to
-      // the MMA warp: O_t is final up to P_t(j-1) V (S_t(j)'s barrier covers it)
-      // and P_t(j) V is issued only after the arrival.
-      auto finish = [&](bool raised, float alpha, float sum) {
-#pragma unroll
-        for (int ch = 0; ch < Cfg::CHUNKS; ++ch) tmem_st16(s_addr + ch * 16, pk + ch * 16);
-        l_run += sum;
-        if (raised) rescale_o(alpha);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
-      };
-      int j = 0;
-      // Sum-first blocks: the first block max-first, then p with the current base
-      // (no row max).  Leaves for the max-first loop below at the first block
-      // whose sum is too large to scale by a power of two (or infinite).
-      for (; j < nblk; ++j) {
-        if (!wait_scores(j)) {
-          ok = false;
-          break;
-        }
-        load_scores();
-        const int valid = w.valid(j);
-        float alpha = 1.0f;
-        bool raised = false, leave = false;
-        float sum = 0.0f;  // the block's row sum as stored
-        if (j == 0) {
-          raised = max_first(j, valid, alpha);
-          sum = row_sum();
-        } else {
-          p_block(-m_run, valid);
-          const float bs = row_sum();
-          sum = bs;
-          if (!__all_sync(0xffffffffu, bs < kAttnSumLimit)) {
-            // A NaN sum (non-finite scores) raises nothing: its row is NaN anyway.
-            if (__all_sync(0xffffffffu, bs < (BF16 ? 0x1p120f : 0x1p15f) || bs != bs)) {
-              const bool need = bs >= kAttnSumLimit;
-              const int k = need ? static_cast<int>((__float_as_uint(bs) >> 23) & 0xffu) - 126 : 0;
-              alpha = __uint_as_float(static_cast<uint32_t>(127 - k) << 23);
-              raised = __any_sync(0xffffffffu, need);
-              if (need) {
-                l_run *= alpha;
-                m_run += static_cast<float>(k);
-              }
-              sum = bs * alpha;  // exact: alpha is a power of two (1 where no row raised)
-              if (raised) {
-                const uint32_t a2 = pack_16bit(alpha, alpha, BF16);
-#pragma unroll
-                for (int i = 0; i < KB / 2; ++i) pk[i] = mul_16bit2(pk[i], a2, BF16);
-              }
-            } else {
-              load_scores();
-              raised = max_first(j, valid, alpha);
-              sum = row_sum();
-              leave = true;
-            }
-          }
-        }
-        finish(raised, alpha, sum);
-        if (leave) {
-          ++j;
-          break;
-        }
-      }
-      // Max-first blocks: the rest of the unit after a sum too large to scale.
-      for (; ok && j < nblk; ++j) {
-        if (!wait_scores(j)) {
-          ok = false;
-          break;
-        }
-        load_scores();
-        float alpha = 1.0f;
-        const bool raised = max_first(j, w.valid(j), alpha);
-        const float sum = row_sum();
-        finish(raised, alpha, sum);
-      }
+      ok = pp_softmax_rows<BF16, KB, Cfg::CHUNKS>(p, w, nblk, sbase, &s_full[t], &p_full[t], s_addr,
+                                                  o_addr, lane, abortp, m_run, l_run, r);
       if (ok && nblk > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], static_cast<uint32_t>(ocnt) & 1u, p.err,
                                                kDevTimeoutEpilogue, abortp));
