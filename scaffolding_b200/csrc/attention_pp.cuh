@@ -360,6 +360,82 @@ __device__ __forceinline__ bool pp_softmax_rows(const AttnArgs& p, const PpSeg<K
   return ok;
 }
 
+// The output rows of a finished unit (or segment), one query row per
+// thread, O read from TMEM: normalised 16-bit O (mode 0), merged first with
+// the partial result over other keys (mode 2), or the unnormalised fp32 O
+// with the row's (m, l) as a partial result (mode 1, and every part of a
+// split tail unit, which writes its workspace slot).
+template <bool BF16, class Cfg, int KB>
+__device__ __forceinline__ void pp_write_rows(const AttnArgs& p, const PpSeg<KB>& w, int t, int row,
+                                              uint32_t o_addr, float m_run, float l_run, int nblk,
+                                              uint32_t* r) {
+  const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
+  const bool live = qrow < p.q_len;
+  const int64_t prow = (static_cast<int64_t>(w.b) * p.q_len + qrow) * p.heads + w.h;
+  // A part of a split unit writes its partial result to its workspace slot.
+  const int mode = w.slot >= 0 ? 1 : p.part_mode;
+  const int urow = t * 128 + row;
+  float* const pml = w.slot >= 0 ? p.ws_ml + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * 2
+                                 : p.part_ml + 2 * prow;
+  float* const pob = w.slot >= 0
+                         ? p.ws_o + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * kAttnD
+                         : p.part_o + prow * kAttnD;
+  // Merge with a partial result over other keys: both bases are integers,
+  // so the rescale factors are exact powers of two.
+  float a_own = 1.0f, a_part = 0.0f;
+  if (mode == 2 && live) {
+    const float m_p = pml[0], l_p = pml[1];
+    const float m = fmaxf(m_run, m_p);
+    a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
+    a_part = ex2_approx(m_p - m);
+    l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
+  }
+  if (mode == 1 && live) {
+    pml[0] = m_run;
+    pml[1] = l_run;
+  }
+  const float inv = 1.0f / l_run;
+  uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
+                 (static_cast<int64_t>(w.b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
+                  static_cast<int64_t>(w.h) * kAttnD) * 2;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    tmem_ld32(o_addr + half * 32, r);
+    tmem_ld_wait();
+    if (!live) continue;
+    if (mode == 1) {
+      float4* po = reinterpret_cast<float4*>(pob + half * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        po[q] = nblk > 0 ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      continue;
+    }
+    float ov[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ov[i] = nblk > 0 ? __uint_as_float(r[i]) : 0.0f;
+    if (mode == 2) {
+      const float4* po = reinterpret_cast<const float4*>(pob + half * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 v = po[q];
+        ov[4 * q] = ov[4 * q] * a_own + v.x * a_part;
+        ov[4 * q + 1] = ov[4 * q + 1] * a_own + v.y * a_part;
+        ov[4 * q + 2] = ov[4 * q + 2] * a_own + v.z * a_part;
+        ov[4 * q + 3] = ov[4 * q + 3] * a_own + v.w * a_part;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<uint4*>(dst)[half * 4 + q] =
+          make_uint4(pack_16bit(ov[8 * q] * inv, ov[8 * q + 1] * inv, BF16),
+                     pack_16bit(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv, BF16),
+                     pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
+                     pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
+  }
+}
+
 // Whole units, one per CTA (pp_unit).  When a stream-K tail runs, this is
 // launched after the tail kernel with programmatic stream serialisation and
 // takes the SM slots the tail CTAs leave; it reads nothing they write.
@@ -557,73 +633,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
                                                      o_addr, lane, abortp, m_run, l_run, r);
     if (ok && nblk > 0)
       ok = __all_sync(0xffffffffu, mbar_wait(&o_last[t], 0u, p.err, kDevTimeoutEpilogue, abortp));
-    const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
     if (ok) {
       tc_fence_after();
-      const bool live = qrow < p.q_len;
-      const int64_t prow = (static_cast<int64_t>(w.b) * p.q_len + qrow) * p.heads + w.h;
-      // A split piece writes its partial result to its workspace slot.
-      const int mode = w.slot >= 0 ? 1 : p.part_mode;
-      const int urow = t * 128 + row;
-      float* const pml = w.slot >= 0 ? p.ws_ml + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * 2
-                                     : p.part_ml + 2 * prow;
-      float* const pob = w.slot >= 0
-                             ? p.ws_o + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * kAttnD
-                             : p.part_o + prow * kAttnD;
-      // Merge with a partial result over other keys: both bases are integers,
-      // so the rescale factors are exact powers of two.
-      float a_own = 1.0f, a_part = 0.0f;
-      if (mode == 2 && live) {
-        const float m_p = pml[0], l_p = pml[1];
-        const float m = fmaxf(m_run, m_p);
-        a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
-        a_part = ex2_approx(m_p - m);
-        l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
-      }
-      if (mode == 1 && live) {
-        pml[0] = m_run;
-        pml[1] = l_run;
-      }
-      const float inv = 1.0f / l_run;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
-                     (static_cast<int64_t>(w.b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
-                      static_cast<int64_t>(w.h) * kAttnD) * 2;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(o_addr + half * 32, r);
-        tmem_ld_wait();
-        if (!live) continue;
-        if (mode == 1) {
-          float4* po = reinterpret_cast<float4*>(pob + half * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            po[q] = nblk > 0 ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
-                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          continue;
-        }
-        float ov[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] = nblk > 0 ? __uint_as_float(r[i]) : 0.0f;
-        if (mode == 2) {
-          const float4* po = reinterpret_cast<const float4*>(pob + half * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 v = po[q];
-            ov[4 * q] = ov[4 * q] * a_own + v.x * a_part;
-            ov[4 * q + 1] = ov[4 * q + 1] * a_own + v.y * a_part;
-            ov[4 * q + 2] = ov[4 * q + 2] * a_own + v.z * a_part;
-            ov[4 * q + 3] = ov[4 * q + 3] * a_own + v.w * a_part;
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          reinterpret_cast<uint4*>(dst)[half * 4 + q] =
-              make_uint4(pack_16bit(ov[8 * q] * inv, ov[8 * q + 1] * inv, BF16),
-                         pack_16bit(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv, BF16),
-                         pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
-                         pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
-      }
+      pp_write_rows<BF16, Cfg>(p, w, t, row, o_addr, m_run, l_run, nblk, r);
     }
   }
 
@@ -885,73 +897,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
       if (nblk > 0) ++ocnt;
       if (!ok) break;
       tc_fence_after();
-      const int qrow = w.qb * Cfg::ROWS + t * 128 + row;
-      const bool live = qrow < p.q_len;
-      const int64_t prow = (static_cast<int64_t>(w.b) * p.q_len + qrow) * p.heads + w.h;
-      // A part of a split unit writes its partial result to its workspace slot.
-      const int mode = w.slot >= 0 ? 1 : p.part_mode;
-      const int urow = t * 128 + row;
-      float* const pml = w.slot >= 0 ? p.ws_ml + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * 2
-                                     : p.part_ml + 2 * prow;
-      float* const pob = w.slot >= 0
-                             ? p.ws_o + (static_cast<int64_t>(w.slot) * Cfg::ROWS + urow) * kAttnD
-                             : p.part_o + prow * kAttnD;
-      // Merge with a partial result over other keys: both bases are integers,
-      // so the rescale factors are exact powers of two.
-      float a_own = 1.0f, a_part = 0.0f;
-      if (mode == 2 && live) {
-        const float m_p = pml[0], l_p = pml[1];
-        const float m = fmaxf(m_run, m_p);
-        a_own = nblk > 0 ? ex2_approx(m_run - m) : 0.0f;
-        a_part = ex2_approx(m_p - m);
-        l_run = (nblk > 0 ? l_run * a_own : 0.0f) + l_p * a_part;
-      }
-      if (mode == 1 && live) {
-        pml[0] = m_run;
-        pml[1] = l_run;
-      }
-      const float inv = 1.0f / l_run;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) +
-                     (static_cast<int64_t>(w.b) * p.o_bstride + static_cast<int64_t>(qrow) * p.ldo +
-                      static_cast<int64_t>(w.h) * kAttnD) * 2;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(o_addr + half * 32, r);
-        tmem_ld_wait();
-        if (!live) continue;
-        if (mode == 1) {
-          float4* po = reinterpret_cast<float4*>(pob + half * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            po[q] = nblk > 0 ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
-                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-          continue;
-        }
-        float ov[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] = nblk > 0 ? __uint_as_float(r[i]) : 0.0f;
-        if (mode == 2) {
-          const float4* po = reinterpret_cast<const float4*>(pob + half * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 v = po[q];
-            ov[4 * q] = ov[4 * q] * a_own + v.x * a_part;
-            ov[4 * q + 1] = ov[4 * q + 1] * a_own + v.y * a_part;
-            ov[4 * q + 2] = ov[4 * q + 2] * a_own + v.z * a_part;
-            ov[4 * q + 3] = ov[4 * q + 3] * a_own + v.w * a_part;
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          reinterpret_cast<uint4*>(dst)[half * 4 + q] =
-              make_uint4(pack_16bit(ov[8 * q] * inv, ov[8 * q + 1] * inv, BF16),
-                         pack_16bit(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv, BF16),
-                         pack_16bit(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv, BF16),
-                         pack_16bit(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv, BF16));
-      }
-      // This tile's O_t reads are complete (tcgen05.wait::ld above) before its
-      // next P arrival lets the next segment's first P.V overwrite O_t.
+      pp_write_rows<BF16, Cfg>(p, w, t, row, o_addr, m_run, l_run, nblk, r);
+      // This tile's O_t reads are complete (pp_write_rows waits for its TMEM
+      // loads) before its next P arrival lets the next segment's first P.V
+      // overwrite O_t.
       tc_fence_before();
     }
   }
