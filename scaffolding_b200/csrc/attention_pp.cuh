@@ -54,8 +54,8 @@
 // Tiles of a unit that hold no query rows (past q_len) are skipped.  Keys
 // past kv_len (TMA zero-fills them) and skipped keys are masked to p = 0;
 // query rows past q_len are computed and not stored.  The partial modes,
-// key-range skips and split pieces are those of AttnArgs, with units of
-// NT * 128 rows (ws_o is [slot][NT * 128][64]).
+// key-range skips and stream-K tail parts are those of AttnArgs, with units
+// of NT * 128 rows (ws_o is [slot][NT * 128][64]).
 //
 // Every wait is bounded (global timer): an expired wait records an error
 // code in the device error word, the CTA drains its copies and MMAs and

@@ -38,7 +38,7 @@ int32_t current_device_info(DeviceInfo** out, int* device);
 // with the per-device word above.
 int32_t noalloc_error_word(int* value, bool clear);
 
-// Releases the fused attention's split-piece workspace held for `stream`
+// Releases the fused attention's stream-K tail workspace held for `stream`
 // (called by sf_stream_destroy before the stream goes away).
 void attention_release_stream(void* stream);
 
