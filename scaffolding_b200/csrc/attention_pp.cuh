@@ -560,7 +560,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
 #pragma unroll
       for (int s2 = 0; s2 < ST; ++s2) pv_done[s2] = 0;
       int finished = 0;
-      unsigned long long t_last = global_timer_ns();
+      unsigned long long t_last = 0;  // start of the current idle period
+      int idle = 0;
       while (ok && finished < ntiles) {
         bool progress = false;
 #pragma unroll
@@ -605,13 +606,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
           progress = true;
         }
         if (progress) {
-          t_last = global_timer_ns();
-        } else if (*abortp) {
-          ok = false;
-        } else if (global_timer_ns() - t_last > kWaitLimitNs) {
-          *abortp = 1;
-          atomicCAS(p.err, 0, kDevTimeoutMma);
-          ok = false;
+          idle = 0;
+        } else {
+          // Nothing ready: back off briefly (the thread shares its scheduler
+          // with softmax warps) and check the abort flag and the time limit
+          // every 16 idle passes.
+          if (idle == 0) t_last = global_timer_ns();
+          if ((++idle & 15) == 0) {
+            if (*abortp) {
+              ok = false;
+            } else if (global_timer_ns() - t_last > kWaitLimitNs) {
+              *abortp = 1;
+              atomicCAS(p.err, 0, kDevTimeoutMma);
+              ok = false;
+            }
+          }
+          __nanosleep(20);
         }
       }
       if (!ok && issued_any) {
@@ -803,7 +813,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
 #pragma unroll
         for (int t = 0; t < NT; ++t) jt[t] = 0;
         int finished = 0;
-        unsigned long long t_last = global_timer_ns();
+        unsigned long long t_last = 0;  // start of the current idle period
+        int idle = 0;
         while (ok && finished < nt) {
           bool progress = false;
 #pragma unroll
@@ -849,13 +860,22 @@ __global__ void __launch_bounds__(Cfg::THREADS, Cfg::MIN_BLOCKS)
             progress = true;
           }
           if (progress) {
-            t_last = global_timer_ns();
-          } else if (*abortp) {
-            ok = false;
-          } else if (global_timer_ns() - t_last > kWaitLimitNs) {
-            *abortp = 1;
-            atomicCAS(p.err, 0, kDevTimeoutMma);
-            ok = false;
+            idle = 0;
+          } else {
+            // Nothing ready: back off briefly (the thread shares its scheduler
+            // with softmax warps) and check the abort flag and the time limit
+            // every 16 idle passes.
+            if (idle == 0) t_last = global_timer_ns();
+            if ((++idle & 15) == 0) {
+              if (*abortp) {
+                ok = false;
+              } else if (global_timer_ns() - t_last > kWaitLimitNs) {
+                *abortp = 1;
+                atomicCAS(p.err, 0, kDevTimeoutMma);
+                ok = false;
+              }
+            }
+            __nanosleep(20);
           }
         }
         if (!ok) break;
