@@ -404,3 +404,28 @@ def test_fused_attention_graph_keeps_captured_workspace(gpu, ops, monkeypatch):
     b = ops.gputensor_to_numpy(replay).view(np.uint16)
     assert np.array_equal(a, b)
     assert device_error(0) == 0
+
+
+def test_fused_attention_full_wave_plus_tail(gpu, ops):
+    """More units than CTA slots: a full wave of whole units (one kernel,
+    launched behind the tail kernel) plus a stream-K tail of 34 units, whose
+    split parts the merge kernel combines after both.  The tail units are the
+    last ones (the last heads); every row of those heads is checked against
+    the oracle, and one head of whole units beside them."""
+    from scaffolding_b200 import engine as E
+    from tests.gpu_util import device_error
+    B, H, L = 1, 30, 2600                     # 11 units per head, 330 units
+    assert E.attention_launch_count(B, H, L, L) == 3
+    rng = np.random.default_rng(2600)
+    W = H * 64
+    gq, q = to_device(ops, rng.standard_normal((L, W), dtype=np.float32), "bf16")
+    gk, k = to_device(ops, rng.standard_normal((L, W), dtype=np.float32), "bf16")
+    gv, v = to_device(ops, rng.standard_normal((L, W), dtype=np.float32), "bf16")
+    out = _fused(ops, B, H, L, L, gq, gk, gv, W, W, W, L * W, L * W, L * W, 0.125)
+    for h in (0, 26, 27, 28, 29):
+        sl = slice(h * 64, (h + 1) * 64)
+        p = O.softmax_rows((q[:, sl] @ k[:, sl].T * np.float32(0.125)).astype(np.float32))
+        ref, allow = O.flash_attention(q[:, sl], k[:, sl], v[:, sl], 0.125, return_allowance=True,
+                                       **attn_oracle_opts())
+        _check_attn(out[:, sl], ref, O.abs_product(p, v[:, sl].T), allow, f"wave+tail head {h}")
+    assert device_error(0) == 0
